@@ -1,0 +1,189 @@
+// Internal definitions shared by the VAULT v3 B200 engine translation units.
+//
+// Device data layouts
+// -------------------
+// Weight matrices are re-tiled once at load time ("repack") into 8-row tiles whose bytes are already in
+// mma.sync m16n8k16 B-fragment order, so a decode GEMV streams each tile with one 16-byte load per lane and
+// feeds the tensor core without shared-memory staging:
+//   Q8_0 : 8 rows x 64 k  = 512 B int8 + 32 B fp16 scales   (544 B, 34/32 B per weight as in the file)
+//   Q4_0 : 8 rows x 128 k = 512 B nibbles + 64 B fp16 scales (576 B, 18/32 B per weight as in the file)
+//   BF16 / F16 : 8 rows x 32 k = 512 B
+//   F32  : 8 rows x 32 k, three bf16 planes hi/mid/lo whose sum is the fp32 weight exactly (1536 B)
+// Lane L = 4g + t of a warp owns tile row g and, for every 16-wide k step s of the tile, the k offsets
+// 16s + {2t, 2t+1, 2t+8, 2t+9}.  The tensor-core result hands lane (g,t) the outputs of tile rows 2t and 2t+1
+// for batch row g.  Fused QKV tiles list RoPE pairs (i, i + D/2) as adjacent rows and gate/up tiles interleave
+// gate_f and up_f, so each lane holds both operands of its RoPE rotation / SiLU product in registers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace v3g {
+
+enum WFmt : int { FMT_F32 = 0, FMT_F16 = 1, FMT_BF16 = 2, FMT_Q8 = 8, FMT_Q4 = 9 };
+
+__host__ __device__ constexpr int tile_k(int fmt) { return fmt == FMT_Q8 ? 64 : (fmt == FMT_Q4 ? 128 : 32); }
+__host__ __device__ constexpr int tile_bytes(int fmt) {
+    return fmt == FMT_Q8 ? 544 : (fmt == FMT_Q4 ? 576 : (fmt == FMT_F32 ? 1536 : 512));
+}
+// fp16 activations for integer / fp16 weights, bf16 activations for bf16 / f32 weights (mma operand types match)
+__host__ __device__ constexpr bool x_is_bf16(int fmt) { return fmt == FMT_BF16 || fmt == FMT_F32; }
+
+enum RowMap : int { ROWS_IDENTITY = 0, ROWS_ROPE_PAIRS = 1, ROWS_GATE_UP = 2 };
+
+struct MatW {
+    const uint8_t *tiles = nullptr;  // [n_rtiles][n_ktiles][tile_bytes]
+    int fmt = 0;
+    int rows = 0;                    // logical output rows (gate/up: 2 * d_ff)
+    int cols = 0;                    // K
+    int n_rtiles = 0, n_ktiles = 0;
+    int rowmap = ROWS_IDENTITY;
+    uint64_t file_bytes = 0;         // payload bytes of the source tensor(s) in the VLT3 file
+};
+
+constexpr int MAX_LAYERS = 64;
+constexpr int MAX_SEG_FEAT = 4;
+constexpr int MAX_SINK = 512;
+constexpr int MAX_SEG_BUDGET = 16384;
+constexpr int GEMV_MB = 8;             // batch rows per GEMV pass (mma rows 0..7)
+constexpr int GEMV_THREADS = 256;
+constexpr int ATT_KEYS_PER_CTA = 128;  // split-KV chunk
+constexpr int ATT_THREADS = 128;
+
+struct LayerW {
+    MatW q, k, v, o, gu, down;
+    const float *ln1, *ln2, *bq, *bk, *bv;
+};
+
+struct ModelDev {
+    int vocab, d, n_layers, H, G, D, F, W;
+    float rms_eps, rope_theta;
+    int pad_id, im_start_id, im_end_id, newline_id, system_id, n_sink, sink_cap, max_sink;
+    int seg_n_feat, seg_hidden, seg_min, seg_max, seg_budget_default;
+    int seg_layers[MAX_SEG_FEAT];
+    LayerW layers[MAX_LAYERS];
+    MatW embed;                      // tied embedding / lm head
+    const float *norm;
+    // segment scorer (F32, row-major as in the file)
+    const float *sc_ln_w, *sc_ln_b, *sc_w1, *sc_b1, *sc_w2, *sc_b2;
+    // RoPE table: rows for positions [rope_pos0, rope_pos0 + rope_rows), each D/2 cos then D/2 sin (fp32)
+    const float *rope;
+    int rope_pos0, rope_rows;
+    // token tables
+    const uint8_t *tier;             // [vocab] segment-break tier 0..3
+    const uint32_t *tok_off;         // [vocab] byte offset in tok_pool (0xFFFFFFFF = no bytes)
+    const uint16_t *tok_len;         // [vocab]
+    const uint8_t *tok_pool;
+};
+
+// Per-sequence control block (device resident; mirrors the scalar fields of src/vault_v3_model.py:974-1011)
+struct SeqCtl {
+    int32_t n_pin, pin_locked, saw_im_start, awaiting_sys_nl;
+    int32_t ema_ready, mem_cnt, n_uniq_segs, seg_id_offset;
+    int32_t cur_seg_id, seg_len, bank_par, seg_budget;
+    int32_t seg_on, auto_pin, last_im_end, pad0;
+};
+
+// Step-level control (device resident, shared by the batch: the reference keeps one st.pos per batch)
+struct StepCtl {
+    int64_t pos;             // absolute token count before the current step
+    const int32_t *ids;      // token source for prefill (nullptr: tok_in)
+    int64_t ids_ld;          // row stride of ids
+    int64_t ids_idx;         // next column of ids
+    int32_t *out_tokens;     // greedy token sink (nullptr: none)
+    int64_t out_ld, out_idx;
+    int32_t status;          // sticky error bits (STATUS_*)
+    int32_t want_logits;
+};
+
+enum : int32_t {
+    STATUS_RESONANCE = 1,    // shingle-resonance bias would be active: unsupported, results diverge from reference
+    STATUS_BOUNDS = 2,       // an internal index check failed
+};
+
+struct StateDev {
+    int B, W, G, D, H, sink_cap, seg_cap, feat_dim, max_splits;
+    uint64_t lb_stride;          // bytes of one (layer, sequence) KV block
+    uint8_t *kv;                 // [layer][seq] KV blocks
+    // offsets inside a KV block (bytes)
+    uint64_t off_ring, ring_kind_stride, ring_par_stride;   // ring[par][kind k_rot/kraw/v][G][W][D]
+    uint64_t off_sink;                                      // sink[kind k_raw/k_rot/v][G][S][D]
+    uint64_t off_bank, bank_par_stride, off_bank_rot;       // bank[par][kind k_raw/v][G][Bc][D]; rot[G][Bc][D]
+    SeqCtl *seq;                 // [B]
+    StepCtl *step;
+    int32_t *tok_in;             // [B]
+    int32_t *tok_ring;           // [B][2][W]
+    float *sc_ring;              // [B][2][W]
+    int32_t *seg_ring;           // [B][2][W]
+    int64_t *mem_pos;            // [B][2][seg_cap]
+    float *mem_score;            // [B][2][seg_cap]
+    int32_t *mem_tok, *mem_seg;  // [B][2][seg_cap]
+    int32_t *mem_src;            // [B][seg_cap]  gather source: >=0 old bank slot, <0: -(t+1) prev-chunk row
+    float *ema, *feat;           // [B][feat_dim]
+    float *x;                    // [B][d] residual stream
+    float *attn;                 // [B][H*D]
+    float *hbuf;                 // [B][F]
+    float *q_cur, *q_far;        // [B][H][D]
+    float *att_part;             // [B][G][max_splits][grp][D + 2]
+    uint32_t *att_cnt;           // [B][G]
+    float *logits;               // [B][V]
+    unsigned long long *amax;    // [B]
+    float *sc_z;                 // [B][2][seg_hidden]
+};
+
+__device__ __forceinline__ uint64_t ring_off(const StateDev &s, int par, int kind, int g, int t) {
+    return s.off_ring + (uint64_t)par * s.ring_par_stride + (uint64_t)kind * s.ring_kind_stride +
+           ((uint64_t)g * s.W + t) * s.D * 2ull;
+}
+__device__ __forceinline__ uint64_t sink_off(const StateDev &s, int kind, int g, int j) {
+    return s.off_sink + (((uint64_t)kind * s.G + g) * s.sink_cap + j) * s.D * 2ull;
+}
+__device__ __forceinline__ uint64_t bank_off(const StateDev &s, int par, int kind, int g, int j) {
+    return s.off_bank + (uint64_t)par * s.bank_par_stride + (((uint64_t)kind * s.G + g) * s.seg_cap + j) * s.D * 2ull;
+}
+__device__ __forceinline__ uint64_t bank_rot_off(const StateDev &s, int g, int j) {
+    return s.off_bank_rot + ((uint64_t)g * s.seg_cap + j) * s.D * 2ull;
+}
+__device__ __forceinline__ __nv_bfloat16 *kvp(const StateDev &s, int layer, int b, uint64_t off) {
+    return reinterpret_cast<__nv_bfloat16 *>(s.kv + ((uint64_t)layer * s.B + b) * s.lb_stride + off);
+}
+
+__device__ __forceinline__ const float *rope_row(const ModelDev &m, int64_t pos) {
+    return m.rope + (pos - m.rope_pos0) * (int64_t)m.D;
+}
+
+// ------------------------------------------------------------------------------------------ small device helpers
+__device__ __forceinline__ uint4 ldg_stream16(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint2 ldg_stream8(const void *p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// order-preserving float -> uint32 (larger float -> larger key); NaN-free inputs assumed
+__device__ __forceinline__ uint32_t float_key(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+}  // namespace v3g

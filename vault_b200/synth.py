@@ -1,0 +1,130 @@
+"""Seeded synthetic VAULT v3 models and the synthetic byte-level tokenizer used for them.
+
+No real checkpoint or Qwen tokenizer exists in this environment, so every model this project runs is built here:
+weights are drawn from a seeded numpy generator (matrices and biases N(0, std), norm gains 1 or U(lo, hi)) and
+exported through `vlt3.write_vlt3`.  The tokenizer is a 256-token byte vocabulary in GPT-2 byte order (so byte
+'\\n' is id 198, the id the reference hard-codes at src/vault_v3_model.py:1968,2239), a "system" token, and the
+three ChatML control tokens as added tokens.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from typing import Callable, Dict, Optional, Tuple
+
+import numpy as np
+
+from .config import VAULTv3Config
+from .vlt3 import LAYER_KINDS, byte_to_unicode, write_vlt3
+
+
+def make_tokenizer_dir(path: str, vocab_size: int, extra_tokens: Optional[Dict[str, int]] = None) -> Dict[str, int]:
+    """Write `tokenizer.json` for a byte-level vocabulary that fits in `vocab_size` ids.
+
+    Full-size vocabularies (>= 151646) use the Qwen2 ids (system 8948, <|endoftext|>/<|im_start|>/<|im_end|> =
+    151643/151644/151645); small test vocabularies put "system" at 300 and the three control tokens at the top
+    three ids.  Returns the id map."""
+    os.makedirs(path, exist_ok=True)
+    b2u = byte_to_unicode()
+    vocab = {b2u[b]: i for i, b in enumerate(b2u)}
+    if vocab_size >= 151646:
+        ids = dict(system=8948, endoftext=151643, im_start=151644, im_end=151645)
+    else:
+        if vocab_size < 320:
+            raise ValueError("synthetic tokenizer needs vocab_size >= 320")
+        ids = dict(system=300, endoftext=vocab_size - 3, im_start=vocab_size - 2, im_end=vocab_size - 1)
+    vocab["system"] = ids["system"]
+    for text, tid in (extra_tokens or {}).items():
+        vocab["".join(b2u[b] for b in text.encode("utf-8"))] = tid
+    tj = {
+        "model": {"type": "BPE", "vocab": vocab, "merges": []},
+        "added_tokens": [
+            {"id": ids["endoftext"], "content": "<|endoftext|>", "special": True},
+            {"id": ids["im_start"], "content": "<|im_start|>", "special": True},
+            {"id": ids["im_end"], "content": "<|im_end|>", "special": True},
+        ],
+    }
+    with open(os.path.join(path, "tokenizer.json"), "w", encoding="utf-8") as f:
+        json.dump(tj, f, ensure_ascii=False)
+    ids["newline"] = 198
+    return ids
+
+
+# Extra multi-byte tokens of the small test vocabularies: they exercise every segment-break tier rule
+# (src/vault_v3_model.py:116-142): '",' is tier 2, '. ' is tier 1 (trailing whitespace ignored), ', ' tier 3.
+SMALL_EXTRA_TOKENS = {'",': 256, ". ": 257, ", ": 258, "ab;": 259, "x}y": 260, "&q": 261, "line\n": 262}
+
+
+def tensor_shapes(cfg: VAULTv3Config) -> Dict[str, Tuple[int, ...]]:
+    d, H, G, D, F = cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.d_ff
+    shapes: Dict[str, Tuple[int, ...]] = {"embed_tokens.weight": (cfg.vocab_size, d), "norm.weight": (d,)}
+    per_layer = {
+        "input_layernorm.weight": (d,),
+        "self_attn.q_proj.weight": (H * D, d), "self_attn.q_proj.bias": (H * D,),
+        "self_attn.k_proj.weight": (G * D, d), "self_attn.k_proj.bias": (G * D,),
+        "self_attn.v_proj.weight": (G * D, d), "self_attn.v_proj.bias": (G * D,),
+        "self_attn.o_proj.weight": (d, H * D),
+        "post_attention_layernorm.weight": (d,),
+        "mlp.gate_proj.weight": (F, d), "mlp.up_proj.weight": (F, d), "mlp.down_proj.weight": (d, F),
+    }
+    for li in range(cfg.n_layers):
+        for k in LAYER_KINDS:
+            shapes[f"layers.{li}.{k}"] = per_layer[k]
+    if cfg.seg_layers:
+        fd = len(cfg.seg_layers) * d
+        shapes.update({
+            "seg_scorer.ln.weight": (fd,), "seg_scorer.ln.bias": (fd,),
+            "seg_scorer.fc1.weight": (cfg.seg_hidden, fd), "seg_scorer.fc1.bias": (cfg.seg_hidden,),
+            "seg_scorer.fc2.weight": (1, cfg.seg_hidden), "seg_scorer.fc2.bias": (1,),
+        })
+    return shapes
+
+
+def _is_gain(name: str) -> bool:
+    return "layernorm" in name or name in ("norm.weight", "seg_scorer.ln.weight")
+
+
+def lazy_state(cfg: VAULTv3Config, seed: int, std: float = 0.02,
+               gain: Optional[Tuple[float, float]] = None, ln_bias_std: float = 0.0) -> Dict[str, Callable[[], np.ndarray]]:
+    """Per-tensor generators: every tensor gets its own seeded stream (seed, tensor index), so any tensor can be
+    regenerated alone and in any order.  Gains are 1 (or U(gain)), the scorer LayerNorm bias 0 (or N(0, ln_bias_std)),
+    everything else N(0, std)."""
+    shapes = tensor_shapes(cfg)
+    out: Dict[str, Callable[[], np.ndarray]] = {}
+    for idx, (name, shape) in enumerate(shapes.items()):
+        def gen(name=name, shape=shape, idx=idx) -> np.ndarray:
+            rng = np.random.default_rng([seed, idx])
+            if _is_gain(name):
+                if gain is None:
+                    return np.ones(shape, dtype=np.float32)
+                return rng.uniform(gain[0], gain[1], size=shape).astype(np.float32)
+            if name == "seg_scorer.ln.bias":
+                if ln_bias_std == 0.0:
+                    return np.zeros(shape, dtype=np.float32)
+                return (rng.standard_normal(size=shape, dtype=np.float32) * np.float32(ln_bias_std))
+            return rng.standard_normal(size=shape, dtype=np.float32) * np.float32(std)
+        out[name] = gen
+    return out
+
+
+def build_state(cfg: VAULTv3Config, seed: int, **kw) -> Dict[str, np.ndarray]:
+    return {k: g() for k, g in lazy_state(cfg, seed, **kw).items()}
+
+
+def write_synthetic_vlt3(path: str, cfg: VAULTv3Config, fmt: str, seed: int, tokenizer_dir: Optional[str] = None,
+                         model_name: str = "VAULT-v3-synthetic", **kw) -> Dict:
+    """Export a seeded synthetic model to VLT3 (tensors are generated one at a time)."""
+    if tokenizer_dir is None:
+        tokenizer_dir = os.path.join(os.path.dirname(os.path.abspath(path)), "synthetic_tokenizer")
+        make_tokenizer_dir(tokenizer_dir, cfg.vocab_size,
+                           None if cfg.vocab_size >= 151646 else SMALL_EXTRA_TOKENS)
+    return write_vlt3(path, lazy_state(cfg, seed, **kw), cfg, tokenizer_dir, fmt, model_name=model_name)
+
+
+def full_config(**overrides) -> VAULTv3Config:
+    """The 1.54B VAULT v3 architecture: d=1536, 28 layers, 12/2 heads, head_dim 128, FFN 8960."""
+    cfg = VAULTv3Config()
+    for k, v in overrides.items():
+        setattr(cfg, k, v)
+    return cfg
