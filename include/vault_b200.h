@@ -1,0 +1,142 @@
+/* vault_b200.h -- C ABI of the B200 (sm_100a) VAULT v3 decode/prefill engine.
+ *
+ * Drop-in boundary for the reference's inference path.  Each entry point names the reference interface it
+ * replaces (paths inside the batteryphil/VAULT checkout):
+ *   - the freestanding C runtime API   runtime/vault3.h  (v3_load, v3_state_*, v3_step, v3_set_*, v3_argmax)
+ *   - the Python streaming API          src/vault_v3_model.py  (VAULTv3ForCausalLM.new_state / prefill / step)
+ *
+ * Conventions (same as runtime/vault3.h):
+ *   - integer status codes, 0 = success, negative = error (values -1..-12 keep the V3_E_* meanings);
+ *   - the model file is a caller-owned host buffer (64-byte aligned), validated before anything is uploaded;
+ *   - the inference state lives in a caller-owned DEVICE arena whose size is queried first; no entry point
+ *     that advances the stream allocates memory;
+ *   - every GPU operation is enqueued on the caller's cudaStream_t (passed as void*, NULL = legacy stream);
+ *   - a state is not thread-safe; different states may be driven from different threads / streams.
+ * No torch types cross this boundary: plain pointers, sizes and integers only.
+ */
+#ifndef VAULT_B200_H
+#define VAULT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define V3G_API __attribute__((visibility("default")))
+#else
+#define V3G_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes: -1..-12 as runtime/vault3.h:35-49 */
+enum {
+    V3G_OK = 0,
+    V3G_E_SIZE = -1,
+    V3G_E_MAGIC = -2,
+    V3G_E_CRC = -3,
+    V3G_E_BOUNDS = -4,
+    V3G_E_DTYPE = -5,
+    V3G_E_MISSING = -6,
+    V3G_E_SHAPE = -7,
+    V3G_E_ARENA = -8,
+    V3G_E_TOKENIZER = -9,
+    V3G_E_LIMIT = -10,
+    V3G_E_ALIGN = -11,
+    V3G_E_NAN = -12,
+    V3G_E_CUDA = -20,        /* a CUDA call failed (message in v3g_last_error) */
+    V3G_E_ARG = -21,         /* invalid argument (null pointer, batch / budget out of range, ...) */
+    V3G_E_UNSUPPORTED = -22, /* valid file or request this engine does not run (message says why) */
+    V3G_E_DEVICE = -23       /* the device raised a status bit (see v3g_status) */
+};
+
+/* device status bits reported by v3g_status */
+enum {
+    V3G_STATUS_RESONANCE = 1, /* shingle-resonance bias would be active (src/vault_v3_model.py:1643-1716); not run */
+    V3G_STATUS_BOUNDS = 2
+};
+
+/* v3g_state_init flags */
+enum {
+    V3G_STATE_PER_SEQ_MEMORY = 1, /* batch > 1: give every sequence its own auto-pin + segment memory (the reference
+                                     runs those only at batch 1, src/vault_v3_model.py:1944,2222) */
+    V3G_STATE_NO_AUTOPIN = 2,     /* keep n_pin = n_sink (runtime/vault3_host.c --no-autopin) */
+    V3G_STATE_NO_GRAPHS = 4       /* launch kernels directly instead of replaying captured CUDA graphs */
+};
+
+typedef struct v3g_model v3g_model;
+typedef struct v3g_state v3g_state;
+
+typedef struct {
+    uint32_t vocab_size, d_model, n_layers, n_heads, n_kv_heads, head_dim, d_ff, window;
+    float rms_eps, rope_theta;
+    uint32_t bos_id, eos_id, im_start_id, im_end_id, pad_id, weight_format, flags, n_sink;
+    uint32_t seg_budget, seg_hidden, seg_min, seg_max, seg_n_feat, seg_layers[4];
+    uint32_t sink_cap;                /* sink rows per layer = max(1, n_sink, max_sink) */
+    uint64_t step_weight_bytes;       /* file bytes of every weight read by one decode step, lm head included */
+    uint64_t lm_head_bytes;           /* file bytes of the tied lm head */
+    uint64_t scorer_bytes;            /* file bytes of the segment scorer (read when segment memory is on) */
+    uint64_t device_bytes;            /* device memory held by the model */
+} v3g_model_info;
+
+/* Parse + validate a VLT3 buffer (same rules as v3_load, runtime/vault3.c:273-455; runtime/vault3.h:89) and
+ * upload it to `device`, re-tiled for the decode kernels.  verify_crc = 1 also checks every tensor CRC32.
+ * max_sink: cap of the ChatML auto-pinned prefix (the Python reference's VAULTv3Config.max_sink, default 512;
+ * 0 selects 512).  The loader allocates the model's device memory itself (freed by v3g_free). */
+V3G_API int v3g_load(v3g_model **out, const uint8_t *buf, uint64_t size, int verify_crc, int device, uint32_t max_sink);
+V3G_API int v3g_model_get_info(const v3g_model *m, v3g_model_info *out);
+V3G_API void v3g_free(v3g_model *m);
+
+/* Device-arena size for `batch` sequences with a segment bank of up to max_seg_budget rows each
+ * (runtime/vault3.h:153 v3_state_arena_size_ex).  Returns 0 on invalid arguments. */
+V3G_API size_t v3g_state_arena_size(const v3g_model *m, uint32_t batch, uint32_t max_seg_budget);
+/* Bind a state to a caller-owned device arena (256-byte aligned) and reset it (runtime/vault3.h:155
+ * v3_state_init_ex).  batch > 1 without V3G_STATE_PER_SEQ_MEMORY follows the reference's batched step: no
+ * auto-pin, no segment memory, n_pin = n_sink (src/vault_v3_model.py:2177-2220). */
+V3G_API int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_arena, size_t arena_size, uint32_t batch,
+                   uint32_t max_seg_budget, uint32_t flags);
+V3G_API void v3g_state_free(v3g_state *s);
+V3G_API int v3g_state_reset(v3g_state *s, void *stream);                           /* runtime/vault3.h:157 */
+V3G_API int v3g_set_pinned(v3g_state *s, uint32_t n_pin, void *stream);            /* runtime/vault3.h:158 */
+V3G_API int v3g_set_seg_budget(v3g_state *s, uint32_t budget, void *stream);       /* runtime/vault3.h:159 */
+V3G_API uint64_t v3g_state_pos(const v3g_state *s);                                /* VAULTv3State.pos */
+
+/* Feed one token per sequence (device int32 [batch]); optionally write fp32 logits [batch, vocab] and the greedy
+ * (first-max) next token [batch] to device memory.  Replaces v3_step (runtime/vault3.h:161) and
+ * VAULTv3ForCausalLM.step (src/vault_v3_model.py:2214).  Ids outside [0, vocab) are replaced by pad_id. */
+V3G_API int v3g_step(v3g_state *s, const int32_t *dev_tokens, float *dev_logits, int32_t *dev_next, void *stream);
+/* Same with HOST buffers (uint32 tokens in, fp32 logits / uint32 next token out; either output may be NULL):
+ * copies in, steps, copies out and synchronizes `stream`.  The v3_step calling convention for C callers. */
+V3G_API int v3g_step_host(v3g_state *s, const uint32_t *tokens, float *logits, uint32_t *next, void *stream);
+/* Stream n_tokens ids per sequence (device int32, row b at dev_ids + b * ld) through the state, computing the
+ * lm head only for the last one (src/vault_v3_model.py:2163 prefill). */
+V3G_API int v3g_prefill(v3g_state *s, const int32_t *dev_ids, uint32_t n_tokens, uint64_t ld, float *dev_logits,
+                int32_t *dev_next, void *stream);
+/* Greedy decode on the device: feeds dev_first [batch], then each step's argmax, for n_steps steps, writing the
+ * produced tokens to dev_out (row b at dev_out + b * ld).  No host round trip between steps. */
+V3G_API int v3g_generate(v3g_state *s, const int32_t *dev_first, uint32_t n_steps, int32_t *dev_out, uint64_t ld,
+                 void *stream);
+/* Synchronize `stream` and read the sticky device status bits (V3G_STATUS_*); clears them when clear != 0. */
+V3G_API int v3g_status(v3g_state *s, uint32_t *bits, int clear, void *stream);
+
+/* Snapshot of one sequence's streaming bookkeeping (VAULTv3State fields, src/vault_v3_model.py:974-1011);
+ * mem_pos / mem_score receive up to `cap` bank entries in chronological order.  Synchronizes `stream`. */
+typedef struct {
+    int32_t n_pin, pin_locked, mem_cnt, n_uniq_segs, seg_id_offset, ema_ready, seg_budget;
+    uint64_t pos;
+} v3g_seq_info_t;
+V3G_API int v3g_seq_info(v3g_state *s, uint32_t b, v3g_seq_info_t *info, int64_t *mem_pos, float *mem_score, uint32_t cap,
+                 void *stream);
+
+/* Kernel-level entry points (tests and the kernel sweep).  tensor_id uses the VLT3 ids of tools/vlt3.py:34-57. */
+V3G_API int v3g_dequant(const v3g_model *m, uint32_t tensor_id, float *dev_out, void *stream);
+V3G_API int v3g_gemv(const v3g_model *m, uint32_t tensor_id, const float *dev_x, uint32_t batch, float *dev_y, void *stream);
+
+V3G_API const char *v3g_error_string(int code);
+V3G_API const char *v3g_last_error(void);   /* detail of the last failure on this thread */
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VAULT_B200_H */

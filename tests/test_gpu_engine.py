@@ -1,0 +1,154 @@
+"""GPU parity of the sm_100a engine against the reference (golden logits from the reference model) and the oracle.
+
+Bars (from the project's parity contract): dequantized weights bit-exact; logits within max |dlogit| <= 2e-2 for
+the 0.02-std models and within 2e-2 relative to the logit range for the 0.15/0.2-std test models (bf16 KV cache,
+16-bit activations, fp32 accumulation); greedy top-1 agreement >= 99%.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import vault_oracle as vo
+from tests.golden.cases import CASES, case_config, case_ids
+
+pytestmark = pytest.mark.gpu
+
+_MODELS = {}
+
+
+def engine(case_files, name):
+    from vault_b200.model import VAULTv3ForCausalLM
+    if name not in _MODELS:
+        cfg = case_config(CASES[name])
+        _MODELS[name] = VAULTv3ForCausalLM(case_files(name), device=0, max_sink=cfg.max_sink)
+    return _MODELS[name]
+
+
+def _tol(ref: np.ndarray) -> float:
+    return 2e-2 * max(1.0, float(np.abs(ref).max()) / 4.0)
+
+
+def _golden(golden_dir, name):
+    return np.load(os.path.join(golden_dir, f"{name}.npz"))
+
+
+@pytest.mark.parametrize("name", ["tiny_seg_f32", "tiny_seg_bf16", "tiny_seg_q8_0", "tiny_seg_q4_0",
+                                  "mini_gqa_q8_0", "mini_gqa_q4_0", "mini_gqa_bf16"])
+def test_dequant_bit_exact(name, case_files):
+    m = engine(case_files, name)
+    om = vo.OracleModel.from_file(case_files(name))
+    cfg = m.cfg
+    for li in range(cfg.n_layers):
+        ref = om.layers[li]
+        base = (li + 1) << 8
+        for kind, key in ((2, "wq"), (4, "wk"), (6, "wv"), (8, "wo"), (12, "wd")):
+            w = ref[key]
+            got = m.dequant(base | kind, *w.shape).cpu().numpy()
+            assert got.view(np.uint32).tobytes() == w.astype(np.float32).view(np.uint32).tobytes(), (li, key)
+        gu = np.concatenate([ref["wg"], ref["wu"]], axis=0)
+        got = m.dequant(base | 10, *gu.shape).cpu().numpy()
+        assert got.view(np.uint32).tobytes() == gu.view(np.uint32).tobytes(), (li, "gate/up")
+    got = m.dequant(1, *om.embed.shape).cpu().numpy()
+    assert got.view(np.uint32).tobytes() == om.embed.view(np.uint32).tobytes()
+
+
+@pytest.mark.parametrize("name", ["mini_gqa_q8_0", "mini_gqa_q4_0", "mini_gqa_bf16", "tiny_seg_f32"])
+@pytest.mark.parametrize("batch", [1, 3, 8, 11])
+def test_gemv_matches_fp64(name, batch, case_files):
+    m = engine(case_files, name)
+    om = vo.OracleModel.from_file(case_files(name))
+    g = torch.Generator().manual_seed(batch)
+    for kind, key in ((2, "wq"), (4, "wk"), (8, "wo"), (12, "wd")):
+        w = om.layers[1][key].astype(np.float64)
+        x = torch.randn(batch, w.shape[1], generator=g)
+        y = m.gemv(((1 + 1) << 8) | kind, x, w.shape[0]).cpu().numpy().astype(np.float64)
+        ref = x.numpy().astype(np.float64) @ w.T
+        err = np.abs(y - ref).max() / (np.abs(ref).max() + 1e-12)
+        # 16-bit activations (fp16 with power-of-two scaling, or bf16 for bf16/f32 weights), fp32 accumulation
+        assert err < (6e-3 if name.endswith(("bf16", "f32")) else 1.5e-3), (key, err)
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_step_logits_match_reference(name, case_files, golden_dir):
+    spec = CASES[name]
+    cfg = case_config(spec)
+    m = engine(case_files, name)
+    g = _golden(golden_dir, name)
+    ids = torch.from_numpy(case_ids(spec, cfg))
+    out = m.forward(ids).cpu().numpy()
+    ref = g["step_logits"]
+    err = np.abs(out - ref).max()
+    top1 = (out.argmax(-1) == ref.argmax(-1)).mean()
+    assert err <= _tol(ref), (err, _tol(ref))
+    assert top1 >= 0.99, top1
+
+
+@pytest.mark.parametrize("name,splits", [("chat_pin_q8_0", [5, 14, 40, 100]), ("b2_swa_q8_0", [5, 8, 16, 29, 40]),
+                                         ("mini_gqa_q4_0", [20, 64])])
+def test_prefill_then_stream(name, splits, case_files, golden_dir):
+    spec = CASES[name]
+    cfg = case_config(spec)
+    m = engine(case_files, name)
+    ref = _golden(golden_dir, name)["step_logits"]
+    ids = torch.from_numpy(case_ids(spec, cfg))
+    for sp in splits:
+        lg, st = m.prefill(ids[:, :sp])
+        got = [lg.cpu().numpy()]
+        for t in range(sp, ids.shape[1]):
+            got.append(m.step(ids[:, t], st).cpu().numpy())
+        got = np.stack(got, axis=1)
+        assert np.abs(got - ref[:, sp - 1:]).max() <= _tol(ref), sp
+        assert st.pos == ids.shape[1]
+
+
+@pytest.mark.parametrize("name", ["tiny_seg_q8_0", "chat_pin_q8_0", "chat_spoof_q8_0", "mini_gqa_q8_0"])
+def test_bank_state_matches_reference(name, case_files, golden_dir):
+    spec = CASES[name]
+    cfg = case_config(spec)
+    m = engine(case_files, name)
+    g = _golden(golden_dir, name)
+    ids = torch.from_numpy(case_ids(spec, cfg))
+    _, st = m.prefill(ids)
+    si, mem_pos, mem_score = st.info(with_bank=True)
+    assert si.n_pin == int(g["final_n_pin"])
+    assert mem_pos.tolist() == g["final_mem_pos"].tolist()
+    assert np.abs(mem_score - g["final_mem_score"]).max() < 5e-2
+
+
+def test_generate_matches_stepwise_argmax(case_files):
+    m = engine(case_files, "mini_gqa_q8_0")
+    spec = CASES["mini_gqa_q8_0"]
+    ids = torch.from_numpy(case_ids(spec, case_config(spec)))[:, :40]
+    lg, st = m.prefill(ids)
+    first = lg.argmax(-1)
+    gen = m.generate(st, first, 30).cpu()
+    _, st2 = m.prefill(ids)
+    tok = first
+    chain = []
+    for _ in range(30):
+        tok = m.step(tok, st2).argmax(-1)
+        chain.append(int(tok[0]))
+    assert gen[0].tolist() == chain
+
+
+def test_state_size_constant_and_reset(case_files):
+    m = engine(case_files, "tiny_seg_q8_0")
+    st = m.new_state(1)
+    n0 = st.nbytes()
+    ids = torch.from_numpy(case_ids(CASES["tiny_seg_q8_0"], case_config(CASES["tiny_seg_q8_0"])))
+    a = [m.step(ids[:, t], st).cpu() for t in range(40)]
+    assert st.nbytes() == n0 and st.pos == 40
+    st.reset()
+    b = [m.step(ids[:, t], st).cpu() for t in range(40)]
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
+
+
+def test_out_of_range_token_becomes_pad(case_files):
+    m = engine(case_files, "tiny_seg_q8_0")
+    st1, st2 = m.new_state(1), m.new_state(1)
+    a = m.step(torch.tensor([10 ** 6]), st1)
+    b = m.step(torch.tensor([m.info.pad_id]), st2)
+    assert torch.equal(a, b)

@@ -51,6 +51,7 @@ constexpr int GEMV_MB = 8;             // batch rows per GEMV pass (mma rows 0..
 constexpr int GEMV_THREADS = 256;
 constexpr int ATT_KEYS_PER_CTA = 128;  // split-KV chunk
 constexpr int ATT_THREADS = 128;
+constexpr int GEMV_MAX_SMEM = 227 * 1024;
 
 struct LayerW {
     MatW q, k, v, o, gu, down;
@@ -185,5 +186,21 @@ __device__ __forceinline__ uint32_t float_key(float f) {
 }
 
 __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// logical (tile-order) row p of a re-tiled matrix -> (source matrix, source row); false for padding rows
+__host__ __device__ __forceinline__ bool map_tile_row(int rowmap, int head_dim, int src_rows, int p, int &src,
+                                                      int &row) {
+    src = 0;
+    if (rowmap == ROWS_ROPE_PAIRS) {
+        const int D = head_dim, head = p / D, w = p % D, j = w >> 3, r = w & 7;
+        row = head * D + 4 * j + (r >> 1) + ((r & 1) ? D / 2 : 0);
+    } else if (rowmap == ROWS_GATE_UP) {
+        src = p & 1;
+        row = p >> 1;
+    } else {
+        row = p;
+    }
+    return row < src_rows;
+}
 
 }  // namespace v3g

@@ -1,0 +1,59 @@
+// Host-side structures and cross-file entry points of the engine (not part of the public C ABI).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "v3g.cuh"
+#include "v3g_gemv.cuh"
+
+struct v3g_model {
+    v3g::ModelDev host;              // host copy of the device descriptor
+    v3g::ModelDev *dev = nullptr;    // device copy
+    int device = 0;
+    int n_sm = 148;
+    uint8_t *weights = nullptr;      // one allocation holding every tile buffer and vector
+    size_t weight_alloc = 0;
+    // per-step algorithmic bytes (file payload bytes of every tensor streamed in a decode step)
+    uint64_t step_bytes = 0, step_bytes_lm = 0, scorer_bytes = 0;
+    uint32_t bos_id = 0, eos_id = 0, weight_format = 0, flags = 0;
+    uint32_t file_seg_budget = 0;
+    std::vector<std::pair<uint32_t, v3g::MatW *>> tensor_index;  // tensor id -> matrix (tests / sweeps)
+    std::string last_error;
+};
+
+struct v3g_state {
+    const v3g_model *m = nullptr;
+    v3g::StateDev host;
+    v3g::StateDev *dev = nullptr;
+    uint8_t *arena = nullptr;
+    size_t arena_size = 0;
+    int B = 1;
+    int seg_cap = 0;                 // bank rows reserved per sequence
+    int per_seq_memory = 0;          // batch > 1 with segment memory + auto-pin per sequence
+    int auto_pin = 1;
+    uint64_t pos = 0;                // host mirror of StepCtl::pos
+    int seg_budget = 0;
+    cudaStream_t cap_stream = nullptr;
+    cudaGraphExec_t graphs[4] = {nullptr, nullptr, nullptr, nullptr};  // [boundary][with lm head]
+    uint64_t graph_B_pos[4] = {0, 0, 0, 0};
+    int use_graphs = 1;
+    std::string last_error;
+};
+
+namespace v3g {
+int repack_matrix(MatW &w, const uint8_t *dev_src0, const uint8_t *dev_src1, int fmt, int src_rows, int cols,
+                  int rowmap, int head_dim, uint8_t *dst, cudaStream_t st);
+size_t matrix_tile_bytes(int fmt, int rows, int cols);
+int dequant_matrix(const MatW &w, int head_dim, float *out, cudaStream_t st);
+
+// one decode step for the whole batch (kernels only; the caller updates the host pos mirror)
+cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool want_lm, cudaStream_t st);
+cudaError_t launch_prefix_refresh(const v3g_model *m, v3g_state *s, cudaStream_t st);
+cudaError_t launch_state_reset(const v3g_model *m, v3g_state *s, cudaStream_t st);
+cudaError_t init_kernel_attrs();
+cudaError_t launch_gemv_mapped(const v3g_model *m, const MatW &w, const float *x, int B, float *y, cudaStream_t st);
+cudaError_t launch_gemv_store(const v3g_model *m, const MatW &w, const float *x, int B, float *y, cudaStream_t st);
+}  // namespace v3g

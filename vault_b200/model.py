@@ -1,0 +1,272 @@
+"""Drop-in VAULT v3 streaming model on the B200 engine.
+
+Mirrors the public inference API of the reference's src/vault_v3_model.py:
+    VAULTv3ForCausalLM.new_state(batch, seg_budget)            :2159
+    VAULTv3ForCausalLM.prefill(input_ids, vault_on, seg_budget)  :2163-2212  -> (logits [B, V], state)
+    VAULTv3ForCausalLM.step(token_ids, st, vault_on)            :2214-2311  -> logits [B, V]
+    VAULTv3ForCausalLM.forward(input_ids, mode, vault_on, seg_budget)  :2153  -> logits [B, L, V]
+    VAULTv3State.pos / .n_pin / .set_pinned / .mem_pos / .nbytes       :974-1024
+Weights come from a VLT3 file (tools/vlt3.py format) and stay quantized on the device.  Every computation runs in
+the CUDA library through its C ABI; torch is used only to hold device buffers and to name the current stream.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Tuple, Union
+
+import numpy as np
+import torch
+
+from . import _lib
+from .config import VAULTv3Config
+from .vlt3 import VLT3Error
+
+
+def _aligned_bytes(src: Union[str, bytes, bytearray, memoryview]) -> np.ndarray:
+    """Host copy of a VLT3 file in a 64-byte aligned buffer (runtime/vault3.h:8 requires 64-byte alignment)."""
+    if isinstance(src, (bytes, bytearray, memoryview)):
+        data = np.frombuffer(src, dtype=np.uint8)
+        n = data.size
+    else:
+        with open(src, "rb") as f:
+            f.seek(0, 2)
+            n = f.tell()
+        data = None
+    raw = np.empty(n + 64, dtype=np.uint8)
+    off = (-raw.ctypes.data) % 64
+    buf = raw[off:off + n]
+    if data is not None:
+        buf[:] = data
+    else:
+        with open(src, "rb") as f:
+            f.readinto(memoryview(buf))
+    return buf
+
+
+def _stream() -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class VAULTv3State:
+    """Fixed-size streaming state held in a device arena (the reference's VAULTv3State / v3_state)."""
+
+    def __init__(self, model: "VAULTv3ForCausalLM", batch: int = 1, seg_budget: Optional[int] = None,
+                 per_sequence_memory: bool = False, auto_pin: bool = True, graphs: bool = True):
+        self.model = model
+        self.batch = int(batch)
+        cfg = model.cfg
+        budget = cfg.seg_budget if seg_budget is None else int(seg_budget)
+        if self.batch > 1 and not per_sequence_memory:
+            budget = 0          # reference batched step: sliding window + sinks only (src/vault_v3_model.py:2194)
+        self.seg_capacity = budget if cfg.seg_layers else 0
+        L = _lib.lib()
+        size = L.v3g_state_arena_size(model._h, self.batch, self.seg_capacity)
+        if size == 0:
+            raise ValueError("invalid state arguments")
+        self.arena = torch.empty(int(size), dtype=torch.uint8, device=model.device)
+        flags = (_lib.V3G_STATE_PER_SEQ_MEMORY if per_sequence_memory else 0) | \
+                (0 if auto_pin else _lib.V3G_STATE_NO_AUTOPIN) | (0 if graphs else _lib.V3G_STATE_NO_GRAPHS)
+        h = C.c_void_p()
+        with torch.cuda.device(model.device):
+            _lib.check(L.v3g_state_init(C.byref(h), model._h, C.c_void_p(self.arena.data_ptr()), int(size),
+                                        self.batch, self.seg_capacity, flags), "v3g_state_init")
+        self._h = h
+        self.seg_budget = budget if cfg.seg_layers else 0
+        if self.seg_budget > 0 and (self.batch == 1 or per_sequence_memory):
+            _lib.check(L.v3g_set_seg_budget(h, self.seg_budget, _stream()), "v3g_set_seg_budget")
+        self.seg_active = cfg.has_seg_scorer and self.seg_budget > 0 and (self.batch == 1 or per_sequence_memory)
+        if self.batch > 1 and not per_sequence_memory:
+            self.set_pinned(min(cfg.n_sink, cfg.window))
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                _lib.lib().v3g_state_free(h)
+            except Exception:
+                pass
+            self._h = None
+
+    @property
+    def pos(self) -> int:
+        return int(_lib.lib().v3g_state_pos(self._h))
+
+    def info(self, b: int = 0, with_bank: bool = False):
+        si = _lib.SeqInfo()
+        cap = max(1, self.seg_capacity)
+        mp = np.zeros(cap, np.int64)
+        ms = np.zeros(cap, np.float32)
+        _lib.check(_lib.lib().v3g_seq_info(self._h, b, C.byref(si), mp.ctypes.data_as(C.c_void_p),
+                                           ms.ctypes.data_as(C.c_void_p), cap, _stream()), "v3g_seq_info")
+        if with_bank:
+            return si, mp[:si.mem_cnt].copy(), ms[:si.mem_cnt].copy()
+        return si
+
+    @property
+    def n_pin(self) -> int:
+        return int(self.info().n_pin)
+
+    @property
+    def mem_pos(self) -> torch.Tensor:
+        return torch.from_numpy(self.info(with_bank=True)[1])
+
+    @property
+    def mem_score(self) -> torch.Tensor:
+        return torch.from_numpy(self.info(with_bank=True)[2])
+
+    def set_pinned(self, n_pin: int) -> None:
+        """Pin the first n_pin tokens as sinks (src/vault_v3_model.py:1013, runtime/vault3.c:898-910)."""
+        cap = min(self.model.cfg.window, self.model.cfg.sink_cap)
+        _lib.check(_lib.lib().v3g_set_pinned(self._h, max(0, min(int(n_pin), cap)), _stream()), "v3g_set_pinned")
+
+    def reset(self) -> None:
+        _lib.check(_lib.lib().v3g_state_reset(self._h, _stream()), "v3g_state_reset")
+
+    def status(self, clear: bool = False) -> int:
+        bits = C.c_uint32()
+        _lib.check(_lib.lib().v3g_status(self._h, C.byref(bits), int(clear), _stream()), "v3g_status")
+        return int(bits.value)
+
+    def check(self) -> None:
+        bits = self.status()
+        if bits & _lib.V3G_STATUS_RESONANCE:
+            raise NotImplementedError("shingle-resonance bias would be active for this stream (a non-pinned "
+                                      "<|im_end|> inside the last 38 tokens with > 2 bank segments); the engine "
+                                      "does not run it")
+        if bits:
+            raise RuntimeError(f"device status bits {bits:#x}")
+
+    def nbytes(self) -> int:
+        return int(self.arena.numel())
+
+
+class VAULTv3ForCausalLM:
+    """VAULT v3 model served by the sm_100a engine."""
+
+    def __init__(self, vlt3: Union[str, bytes], device: Optional[Union[int, torch.device]] = None,
+                 verify_crc: bool = True, max_sink: int = 512):
+        if not torch.cuda.is_available():
+            raise RuntimeError("VAULT v3 B200 engine needs a CUDA device (there is no CPU fallback)")
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                           (device.index if isinstance(device, torch.device) else int(device)))
+        self.device = dev
+        buf = _aligned_bytes(vlt3)
+        L = _lib.lib()
+        h = C.c_void_p()
+        with torch.cuda.device(dev):
+            _lib.check(L.v3g_load(C.byref(h), C.c_void_p(buf.ctypes.data), buf.size, int(verify_crc), dev.index,
+                                  int(max_sink)), "v3g_load")
+        self._h = h
+        info = _lib.ModelInfo()
+        _lib.check(L.v3g_model_get_info(h, C.byref(info)), "v3g_model_get_info")
+        self.info = info
+        nf = info.seg_n_feat
+        self.cfg = VAULTv3Config(
+            vocab_size=info.vocab_size, d_model=info.d_model, n_layers=info.n_layers, n_heads=info.n_heads,
+            n_kv_heads=info.n_kv_heads, head_dim=info.head_dim, d_ff=info.d_ff, rms_eps=info.rms_eps,
+            rope_theta=info.rope_theta, tie_embeddings=bool(info.flags & 1), window=info.window, n_sink=info.n_sink,
+            max_sink=int(max_sink), im_start_id=info.im_start_id, im_end_id=info.im_end_id,
+            seg_budget=info.seg_budget if nf else 0, seg_hidden=info.seg_hidden if nf else 256,
+            seg_min=info.seg_min if nf else 16, seg_max=info.seg_max if nf else 48,
+            seg_layers=tuple(info.seg_layers[:nf]) if nf else ())
+
+    @classmethod
+    def from_vlt3(cls, path: str, **kw) -> "VAULTv3ForCausalLM":
+        return cls(path, **kw)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                _lib.lib().v3g_free(h)
+            except Exception:
+                pass
+            self._h = None
+
+    # ---- streaming API
+    def new_state(self, batch: int = 1, seg_budget: Optional[int] = None, **kw) -> VAULTv3State:
+        return VAULTv3State(self, batch, seg_budget=seg_budget, **kw)
+
+    def _ids(self, t: torch.Tensor) -> torch.Tensor:
+        return t.to(device=self.device, dtype=torch.int32).contiguous()
+
+    @torch.no_grad()
+    def step(self, token_ids: torch.Tensor, st: VAULTv3State, vault_on: bool = False) -> torch.Tensor:
+        """token_ids [B] -> logits [B, V] (fp32, on the engine device)."""
+        _ = vault_on
+        ids = self._ids(token_ids.reshape(-1))
+        if ids.numel() != st.batch:
+            raise ValueError(f"expected {st.batch} token ids, got {ids.numel()}")
+        out = torch.empty(st.batch, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
+        _lib.check(_lib.lib().v3g_step(st._h, C.c_void_p(ids.data_ptr()), C.c_void_p(out.data_ptr()), None,
+                                       _stream()), "v3g_step")
+        if st.seg_active:
+            st.check()
+        return out
+
+    @torch.no_grad()
+    def prefill(self, input_ids: torch.Tensor, vault_on: bool = False,
+                seg_budget: Optional[int] = None) -> Tuple[torch.Tensor, VAULTv3State]:
+        """Stream a prompt from position 0; returns last-token logits [B, V] and the state."""
+        _ = vault_on
+        B, Lq = input_ids.shape
+        st = self.new_state(B, seg_budget=seg_budget)
+        ids = self._ids(input_ids)
+        out = torch.empty(B, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
+        _lib.check(_lib.lib().v3g_prefill(st._h, C.c_void_p(ids.data_ptr()), Lq, Lq, C.c_void_p(out.data_ptr()),
+                                          None, _stream()), "v3g_prefill")
+        st.check()
+        return out, st
+
+    @torch.no_grad()
+    def forward(self, input_ids: torch.Tensor, mode: str = "block", vault_on: bool = False,
+                seg_budget: Optional[int] = None) -> torch.Tensor:
+        """All-position logits [B, L, V].  mode='block' is the streaming path (identical to the reference's
+        chunk-recurrent / block-sliding forward); mode='full' equals it for L <= 2W."""
+        _ = vault_on
+        B, Lq = input_ids.shape
+        if mode == "full" and Lq > 2 * self.cfg.window:
+            raise NotImplementedError("mode='full' beyond 2W tokens is plain dense attention, not the streaming path")
+        st = self.new_state(B, seg_budget=seg_budget)
+        ids = self._ids(input_ids)
+        out = torch.empty(B, Lq, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
+        tmp = torch.empty(B, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
+        L = _lib.lib()
+        for t in range(Lq):
+            col = ids[:, t].contiguous()
+            _lib.check(L.v3g_step(st._h, C.c_void_p(col.data_ptr()), C.c_void_p(tmp.data_ptr()), None, _stream()),
+                       "v3g_step")
+            out[:, t] = tmp
+        st.check()
+        return out
+
+    __call__ = forward
+
+    @torch.no_grad()
+    def generate(self, st: VAULTv3State, first_tokens: torch.Tensor, n_steps: int) -> torch.Tensor:
+        """Greedy decode n_steps tokens on the device starting from first_tokens [B]; returns int32 [B, n_steps]."""
+        first = self._ids(first_tokens.reshape(-1))
+        out = torch.empty(st.batch, n_steps, dtype=torch.int32, device=self.device)
+        _lib.check(_lib.lib().v3g_generate(st._h, C.c_void_p(first.data_ptr()), n_steps, C.c_void_p(out.data_ptr()),
+                                           n_steps, _stream()), "v3g_generate")
+        if st.seg_active:
+            st.check()
+        return out
+
+    # ---- kernel-level access (tests, kernel sweep)
+    def dequant(self, tensor_id: int, rows: int, cols: int) -> torch.Tensor:
+        out = torch.empty(rows, cols, dtype=torch.float32, device=self.device)
+        _lib.check(_lib.lib().v3g_dequant(self._h, tensor_id, C.c_void_p(out.data_ptr()), _stream()), "v3g_dequant")
+        return out
+
+    def gemv(self, tensor_id: int, x: torch.Tensor, rows: int) -> torch.Tensor:
+        x = x.to(device=self.device, dtype=torch.float32).contiguous()
+        B = x.shape[0]
+        y = torch.empty(B, rows, dtype=torch.float32, device=self.device)
+        _lib.check(_lib.lib().v3g_gemv(self._h, tensor_id, C.c_void_p(x.data_ptr()), B, C.c_void_p(y.data_ptr()),
+                                       _stream()), "v3g_gemv")
+        return y
+
+
+__all__ = ["VAULTv3ForCausalLM", "VAULTv3State", "VAULTv3Config", "VLT3Error"]

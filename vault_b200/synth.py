@@ -16,7 +16,7 @@ from typing import Callable, Dict, Optional, Tuple
 import numpy as np
 
 from .config import VAULTv3Config
-from .vlt3 import LAYER_KINDS, byte_to_unicode, write_vlt3
+from .vlt3 import LAYER_KINDS, PreEncoded, byte_to_unicode, write_vlt3
 
 
 def make_tokenizer_dir(path: str, vocab_size: int, extra_tokens: Optional[Dict[str, int]] = None) -> Dict[str, int]:
@@ -120,6 +120,81 @@ def write_synthetic_vlt3(path: str, cfg: VAULTv3Config, fmt: str, seed: int, tok
         make_tokenizer_dir(tokenizer_dir, cfg.vocab_size,
                            None if cfg.vocab_size >= 151646 else SMALL_EXTRA_TOKENS)
     return write_vlt3(path, lazy_state(cfg, seed, **kw), cfg, tokenizer_dir, fmt, model_name=model_name)
+
+
+def _torch_encoder(name: str, shape, seed: int, idx: int, std: float, device: str):
+    """PreEncoded tensor generated and quantized with torch on `device` (same block rules as quantize_q8_0 /
+    quantize_q4_0 / RNE bf16; the random stream differs from the numpy generator, so files are seed-stable but not
+    byte-identical to write_synthetic_vlt3)."""
+    import torch
+
+    def encode(dt: int) -> bytes:
+        g = torch.Generator(device=device).manual_seed(seed * 1000003 + idx)
+        if _is_gain(name):
+            x = torch.ones(shape, device=device)
+        elif name == "seg_scorer.ln.bias":
+            x = torch.zeros(shape, device=device)
+        else:
+            x = torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std
+        return encode_torch(x, dt)
+
+    return PreEncoded(shape, encode)
+
+
+def encode_torch(x, dt: int) -> bytes:
+    """Encode an fp32 torch tensor to VLT3 payload bytes (rules of tools/vlt3.py:102-149, 177-186)."""
+    import torch
+    from .vlt3 import BF16, F16, F32, Q4_0, Q8_0, QK
+
+    if dt == F32:
+        return x.float().contiguous().cpu().numpy().astype("<f4").tobytes()
+    if dt == F16:
+        return x.half().contiguous().cpu().numpy().astype("<f2").tobytes()
+    if dt == BF16:
+        return x.to(torch.bfloat16).contiguous().view(torch.int16).cpu().numpy().astype("<i2").tobytes()
+    xb = x.reshape(-1, QK).float()
+    nb = xb.shape[0]
+    if dt == Q8_0:
+        d = xb.abs().amax(dim=1) / 127.0
+        inv = torch.where(d > 0, 1.0 / torch.where(d > 0, d, torch.ones_like(d)), torch.zeros_like(d))
+        q = torch.clamp(torch.round(xb * inv[:, None]), -127, 127).to(torch.int8)
+        out = torch.empty(nb, 34, dtype=torch.uint8, device=x.device)
+        out[:, :2] = d.half().view(torch.uint8).view(nb, 2)
+        out[:, 2:] = q.view(torch.uint8)
+        return out.cpu().numpy().tobytes()
+    if dt == Q4_0:
+        ratios = [-1.0 / 8.0, -0.98 / 8.0, -0.96 / 8.0, -0.94 / 8.0, -0.92 / 8.0, -0.89 / 8.0, 1.0 / 7.5, 0.96 / 7.5]
+        mx = xb.gather(1, xb.abs().argmax(dim=1, keepdim=True))[:, 0]
+        best_err = torch.full((nb,), float("inf"), device=x.device)
+        best_d = torch.zeros(nb, dtype=torch.float16, device=x.device)
+        best_q = torch.full((nb, QK), 8, dtype=torch.uint8, device=x.device)
+        nz = mx != 0
+        for r in ratios:
+            d16 = (mx * torch.tensor(r, dtype=torch.float32)).half()
+            d32 = d16.float()
+            inv = torch.where(d32 != 0, 1.0 / torch.where(d32 != 0, d32, torch.ones_like(d32)), torch.zeros_like(d32))
+            qi = torch.clamp(torch.round(xb * inv[:, None] + 8.0), 0, 15).to(torch.uint8)
+            err = ((qi.float() - 8.0) * d32[:, None] - xb).square().sum(dim=1)
+            better = nz & (err < best_err)
+            best_err = torch.where(better, err, best_err)
+            best_d = torch.where(better, d16, best_d)
+            best_q = torch.where(better[:, None], qi, best_q)
+        out = torch.empty(nb, 18, dtype=torch.uint8, device=x.device)
+        out[:, :2] = best_d.view(torch.uint8).view(nb, 2)
+        out[:, 2:] = best_q[:, :QK // 2] | (best_q[:, QK // 2:] << 4)
+        return out.cpu().numpy().tobytes()
+    raise ValueError(dt)
+
+
+def write_synthetic_vlt3_fast(path: str, cfg: VAULTv3Config, fmt: str, seed: int, device: str = "cuda",
+                              std: float = 0.02, model_name: str = "VAULT-v3-synthetic") -> Dict:
+    """Full-size synthetic export with tensors drawn and quantized by torch on `device` (seconds on a GPU).
+    Weights N(0, std), norm gains 1, scorer LayerNorm bias 0 (the BASELINE synthetic models)."""
+    tokenizer_dir = os.path.join(os.path.dirname(os.path.abspath(path)), "synthetic_tokenizer")
+    make_tokenizer_dir(tokenizer_dir, cfg.vocab_size, None if cfg.vocab_size >= 151646 else SMALL_EXTRA_TOKENS)
+    state = {name: _torch_encoder(name, shape, seed, idx, std, device)
+             for idx, (name, shape) in enumerate(tensor_shapes(cfg).items())}
+    return write_vlt3(path, state, cfg, tokenizer_dir, fmt, model_name=model_name)
 
 
 def full_config(**overrides) -> VAULTv3Config:

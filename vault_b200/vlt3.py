@@ -96,6 +96,15 @@ class VLT3Error(ValueError):
     """Malformed or unsafe VLT3 file (same role as tools/vlt3.py:411 VLT3Error)."""
 
 
+class PreEncoded:
+    """A tensor the writer does not hold as floats: `encode(dtype)` returns its payload bytes for the storage type
+    the writer picked (lets large synthetic models be generated and quantized elsewhere, e.g. on a GPU)."""
+
+    def __init__(self, shape, encode):
+        self.shape = tuple(shape)
+        self.encode = encode
+
+
 def tensor_id(name: str) -> int:
     if name in _GLOBAL_BY_NAME:
         return _GLOBAL_BY_NAME[name]
@@ -365,13 +374,22 @@ def write_vlt3(path: str, state: Dict[str, "np.ndarray"], cfg, tokenizer_dir: st
         arr = state[nm]
         if callable(arr):
             arr = arr()
-        arr = arr.detach().float().cpu().numpy() if hasattr(arr, "detach") else np.asarray(arr, dtype=np.float32)
         dt = choose_dtype(nm, fmt, n_layers)
-        if dt in (Q8_0, Q4_0) and arr.shape[-1] % QK:
-            dt = BF16
-        data = encode_array(arr, dt)
-        dims = list(arr.shape) + [1] * (4 - arr.ndim)
-        entries.append(dict(id=tensor_id(nm), dtype=dt, ndim=arr.ndim, dims=dims, nbytes=len(data),
+        if isinstance(arr, PreEncoded):
+            shape = tuple(arr.shape)
+            if dt in (Q8_0, Q4_0) and shape[-1] % QK:
+                dt = BF16
+            data = arr.encode(dt)
+        else:
+            arr = arr.detach().float().cpu().numpy() if hasattr(arr, "detach") else np.asarray(arr, dtype=np.float32)
+            shape = arr.shape
+            if dt in (Q8_0, Q4_0) and arr.shape[-1] % QK:
+                dt = BF16
+            data = encode_array(arr, dt)
+        if len(data) != nbytes_for(dt, int(np.prod(shape))):
+            raise VLT3Error(f"{nm}: encoded size mismatch")
+        dims = list(shape) + [1] * (4 - len(shape))
+        entries.append(dict(id=tensor_id(nm), dtype=dt, ndim=len(shape), dims=dims, nbytes=len(data),
                             crc=zlib.crc32(data), name=nm))
         payloads.append(data)
     tok_blob, ids = build_tokenizer_blob(tokenizer_dir)
