@@ -54,7 +54,8 @@ enum {
 /* device status bits reported by v3g_status */
 enum {
     V3G_STATUS_RESONANCE = 1, /* shingle-resonance bias would be active (src/vault_v3_model.py:1643-1716); not run */
-    V3G_STATUS_BOUNDS = 2
+    V3G_STATUS_BOUNDS = 2,    /* a token id or position left its valid range (clamped; the step's output is invalid) */
+    V3G_STATUS_TIMEOUT = 4    /* a grid barrier of the persistent decode kernel gave up waiting (output invalid) */
 };
 
 /* v3g_state_init flags */
@@ -62,7 +63,8 @@ enum {
     V3G_STATE_PER_SEQ_MEMORY = 1, /* batch > 1: give every sequence its own auto-pin + segment memory (the reference
                                      runs those only at batch 1, src/vault_v3_model.py:1944,2222) */
     V3G_STATE_NO_AUTOPIN = 2,     /* keep n_pin = n_sink (runtime/vault3_host.c --no-autopin) */
-    V3G_STATE_NO_GRAPHS = 4       /* launch kernels directly instead of replaying captured CUDA graphs */
+    V3G_STATE_NO_GRAPHS = 4,      /* launch kernels directly instead of replaying captured CUDA graphs */
+    V3G_STATE_NO_PERSISTENT = 8   /* run a step as one kernel per layer phase instead of the persistent kernel */
 };
 
 typedef struct v3g_model v3g_model;

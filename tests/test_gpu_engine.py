@@ -71,14 +71,22 @@ def test_gemv_matches_fp64(name, batch, case_files):
         assert err < (6e-3 if name.endswith(("bf16", "f32")) else 1.5e-3), (key, err)
 
 
+def _stream(m, ids, **state_kw):
+    st = m.new_state(ids.shape[0], **state_kw)
+    out = np.stack([m.step(ids[:, t], st).cpu().numpy() for t in range(ids.shape[1])], axis=1)
+    st.check()
+    return out
+
+
+@pytest.mark.parametrize("persistent", [True, False], ids=["persistent", "per_phase"])
 @pytest.mark.parametrize("name", sorted(CASES))
-def test_step_logits_match_reference(name, case_files, golden_dir):
+def test_step_logits_match_reference(name, persistent, case_files, golden_dir):
     spec = CASES[name]
     cfg = case_config(spec)
     m = engine(case_files, name)
     g = _golden(golden_dir, name)
     ids = torch.from_numpy(case_ids(spec, cfg))
-    out = m.forward(ids).cpu().numpy()
+    out = _stream(m, ids, persistent=persistent)
     ref = g["step_logits"]
     err = np.abs(out - ref).max()
     top1 = (out.argmax(-1) == ref.argmax(-1)).mean()
@@ -116,6 +124,17 @@ def test_bank_state_matches_reference(name, case_files, golden_dir):
     assert si.n_pin == int(g["final_n_pin"])
     assert mem_pos.tolist() == g["final_mem_pos"].tolist()
     assert np.abs(mem_score - g["final_mem_score"]).max() < 5e-2
+
+
+@pytest.mark.parametrize("name", ["mini_gqa_q8_0", "mini_gqa_q4_0", "mini_gqa_bf16", "tiny_seg_f32"])
+def test_persistent_matches_per_phase_kernels(name, case_files):
+    """The persistent kernel and the per-phase kernels compute the same sums (only the k-split order differs)."""
+    spec = CASES[name]
+    m = engine(case_files, name)
+    ids = torch.from_numpy(case_ids(spec, case_config(spec)))[:, :48]
+    a = _stream(m, ids, persistent=True)
+    b = _stream(m, ids, persistent=False)
+    assert np.abs(a - b).max() <= 1e-3 * max(1.0, float(np.abs(b).max())), np.abs(a - b).max()
 
 
 def test_generate_matches_stepwise_argmax(case_files):

@@ -2,17 +2,22 @@
 //
 // Device data layouts
 // -------------------
-// Weight matrices are re-tiled once at load time ("repack") into 8-row tiles whose bytes are already in
-// mma.sync m16n8k16 B-fragment order, so a decode GEMV streams each tile with one 16-byte load per lane and
-// feeds the tensor core without shared-memory staging:
-//   Q8_0 : 8 rows x 64 k  = 512 B int8 + 32 B fp16 scales   (544 B, 34/32 B per weight as in the file)
-//   Q4_0 : 8 rows x 128 k = 512 B nibbles + 64 B fp16 scales (576 B, 18/32 B per weight as in the file)
-//   BF16 / F16 : 8 rows x 32 k = 512 B
-//   F32  : 8 rows x 32 k, three bf16 planes hi/mid/lo whose sum is the fp32 weight exactly (1536 B)
-// Lane L = 4g + t of a warp owns tile row g and, for every 16-wide k step s of the tile, the k offsets
-// 16s + {2t, 2t+1, 2t+8, 2t+9}.  The tensor-core result hands lane (g,t) the outputs of tile rows 2t and 2t+1
-// for batch row g.  Fused QKV tiles list RoPE pairs (i, i + D/2) as adjacent rows and gate/up tiles interleave
-// gate_f and up_f, so each lane holds both operands of its RoPE rotation / SiLU product in registers.
+// Weight matrices are re-tiled once at load time ("repack") into 16-row tiles whose bytes are already in
+// mma.sync m16n8k16 A-fragment order (weights are the A operand, activations of up to 8 sequences the B
+// operand), so a decode GEMV streams each tile with one 16-byte load per lane and feeds the tensor core without
+// shared-memory staging:
+//   Q8_0 : 16 rows x 32 k (one block)  = 512 B codes + 32 B fp16 scales   (544 B, 34/32 B per weight as in the file)
+//   Q4_0 : 16 rows x 64 k (two blocks) = 512 B nibbles + 64 B fp16 scales (576 B, 18/32 B per weight as in the file)
+//   BF16 / F16 : 16 rows x 16 k = 512 B of fp16 (BF16 weights are stored as fp16 times a per-matrix power of two
+//                2^s chosen so that max|w| 2^s lies in [2^14, 2^15): exact for every |w| >= max|w| 2^-32)
+//   F32  : 16 rows x 16 k, three fp16 planes hi/mid/lo with w 2^s = hi + 2^-11 mid + 2^-22 lo exactly (1536 B)
+// Lane L = 4g + t of a warp owns tile rows g and g+8 and, for every 16-wide k step s of the tile, the k offsets
+// 16s + {2t, 2t+1, 2t+8, 2t+9}.  Q8_0 codes are stored biased (q + 128) so one byte-permute turns two of them into
+// the fp16 integers 1152 + q; Q4_0 nibbles n become 1024 + n with one mask; the constant offsets are removed after
+// the tensor core with the activation block sums.  The tensor-core result hands lane (g,t) the outputs of tile
+// rows g and g+8 for batch rows 2t and 2t+1.  Fused QKV tiles place RoPE partners (i, i + D/2) at tile rows
+// (r, r+8) and gate/up tiles place gate_f and up_f there, so each lane holds both operands of its RoPE rotation /
+// SiLU product in registers.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -24,12 +29,16 @@ namespace v3g {
 
 enum WFmt : int { FMT_F32 = 0, FMT_F16 = 1, FMT_BF16 = 2, FMT_Q8 = 8, FMT_Q4 = 9 };
 
-__host__ __device__ constexpr int tile_k(int fmt) { return fmt == FMT_Q8 ? 64 : (fmt == FMT_Q4 ? 128 : 32); }
+constexpr int TILE_ROWS = 16;
+__host__ __device__ constexpr int tile_k(int fmt) { return fmt == FMT_Q8 ? 32 : (fmt == FMT_Q4 ? 64 : 16); }
 __host__ __device__ constexpr int tile_bytes(int fmt) {
     return fmt == FMT_Q8 ? 544 : (fmt == FMT_Q4 ? 576 : (fmt == FMT_F32 ? 1536 : 512));
 }
-// fp16 activations for integer / fp16 weights, bf16 activations for bf16 / f32 weights (mma operand types match)
-__host__ __device__ constexpr bool x_is_bf16(int fmt) { return fmt == FMT_BF16 || fmt == FMT_F32; }
+// every tile format enters the tensor core as fp16 (kind f16 with fp32 accumulation); activations are fp16 too
+constexpr float F32_MID = 1.0f / 2048.0f, F32_LO = 1.0f / 4194304.0f;   // 2^-11, 2^-22 plane weights
+
+// KV cache element: fp16 (10 mantissa bits; K/V magnitudes stay far inside its range)
+typedef __half kv_t;
 
 enum RowMap : int { ROWS_IDENTITY = 0, ROWS_ROPE_PAIRS = 1, ROWS_GATE_UP = 2 };
 
@@ -41,6 +50,7 @@ struct MatW {
     int n_rtiles = 0, n_ktiles = 0;
     int rowmap = ROWS_IDENTITY;
     uint64_t file_bytes = 0;         // payload bytes of the source tensor(s) in the VLT3 file
+    float wscale = 1.f;              // tile values x wscale = weights (2^-s for BF16 / F32 tiles, else 1)
 };
 
 constexpr int MAX_LAYERS = 64;
@@ -49,9 +59,9 @@ constexpr int MAX_SINK = 512;
 constexpr int MAX_SEG_BUDGET = 16384;
 constexpr int GEMV_MB = 8;             // batch rows per GEMV pass (mma rows 0..7)
 constexpr int GEMV_THREADS = 256;
-constexpr int ATT_KEYS_PER_CTA = 128;  // split-KV chunk
+constexpr int ATT_KEYS_PER_CTA = 64;   // split-KV chunk
 constexpr int ATT_THREADS = 128;
-constexpr int GEMV_MAX_SMEM = 227 * 1024;
+constexpr int GEMV_MAX_SMEM = 220 * 1024;   // launch-time cap (below the 227 KB opt-in minus static smem)
 
 struct LayerW {
     MatW q, k, v, o, gu, down;
@@ -102,6 +112,7 @@ struct StepCtl {
 enum : int32_t {
     STATUS_RESONANCE = 1,    // shingle-resonance bias would be active: unsupported, results diverge from reference
     STATUS_BOUNDS = 2,       // an internal index check failed
+    STATUS_TIMEOUT = 4,      // a bounded grid-barrier wait gave up (results of the step are invalid)
 };
 
 struct StateDev {
@@ -132,6 +143,9 @@ struct StateDev {
     float *logits;               // [B][V]
     unsigned long long *amax;    // [B]
     float *sc_z;                 // [B][2][seg_hidden]
+    unsigned int *bar;           // grid-barrier counter of the persistent decode kernel (zeroed every step)
+    float *mk_part;              // persistent kernel: split row-tile partials [8 * n_sm warps][2][32][4]
+    uint32_t *mk_cnt;            // persistent kernel: per-row-tile arrival tickets
 };
 
 __device__ __forceinline__ uint64_t ring_off(const StateDev &s, int par, int kind, int g, int t) {
@@ -147,8 +161,8 @@ __device__ __forceinline__ uint64_t bank_off(const StateDev &s, int par, int kin
 __device__ __forceinline__ uint64_t bank_rot_off(const StateDev &s, int g, int j) {
     return s.off_bank_rot + ((uint64_t)g * s.seg_cap + j) * s.D * 2ull;
 }
-__device__ __forceinline__ __nv_bfloat16 *kvp(const StateDev &s, int layer, int b, uint64_t off) {
-    return reinterpret_cast<__nv_bfloat16 *>(s.kv + ((uint64_t)layer * s.B + b) * s.lb_stride + off);
+__device__ __forceinline__ kv_t *kvp(const StateDev &s, int layer, int b, uint64_t off) {
+    return reinterpret_cast<kv_t *>(s.kv + ((uint64_t)layer * s.B + b) * s.lb_stride + off);
 }
 
 __device__ __forceinline__ const float *rope_row(const ModelDev &m, int64_t pos) {
@@ -185,18 +199,69 @@ __device__ __forceinline__ uint32_t float_key(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-__device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float kv2f(kv_t v) { return __half2float(v); }
+__device__ __forceinline__ kv_t f2kv(float v) { return __float2half_rn(v); }
+
+// Programmatic dependent launch: every kernel of a decode step is launched with programmatic stream serialization,
+// so it may start while its predecessor drains.  Before griddep_wait() a kernel touches only immutable data
+// (weights); griddep_wait() returns once the predecessor grid has completed and its writes are visible.
+// Launched without the attribute, both are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// host: launch `k` with the programmatic-serialization attribute (pdl = true) on stream st
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(bool pdl, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
+// element (tile row r, k) of a re-tiled matrix as fp32 (exact inverse of the repack); wscale = MatW::wscale
+__device__ __forceinline__ float tile_value(const uint8_t *tiles, int fmt, int n_ktiles, float wscale, int p, int k) {
+    const int TK = tile_k(fmt);
+    const int rt = p / TILE_ROWS, r = p % TILE_ROWS, kt = k / TK, kk = k % TK;
+    const int g = r & 7, s = kk >> 4, w16 = kk & 15;
+    const int t = (w16 & 7) >> 1, half = w16 & 1;
+    const int reg = ((r >> 3) & 1) | ((w16 & 8) ? 2 : 0);
+    const int lane = 4 * g + t, e = 2 * reg + half;
+    const uint8_t *tb = tiles + ((size_t)rt * n_ktiles + kt) * tile_bytes(fmt);
+    if (fmt == FMT_Q8 || fmt == FMT_Q4) {
+        const int blk = kk >> 5;
+        const uint32_t sw = fmt == FMT_Q8 ? *reinterpret_cast<const uint32_t *>(tb + 512 + g * 4)
+                                          : *reinterpret_cast<const uint32_t *>(tb + 512 + g * 8 + 4 * blk);
+        const float d = __half2float(__ushort_as_half((uint16_t)(r < 8 ? (sw & 0xFFFF) : (sw >> 16))));
+        if (fmt == FMT_Q8) return (float)((int)tb[lane * 16 + 8 * s + e] - 128) * d;
+        const uint32_t word = *reinterpret_cast<const uint32_t *>(tb + lane * 16 + 4 * s);
+        return (float)((int)((word >> (4 * reg + 16 * half)) & 15u) - 8) * d;
+    }
+    const int off = lane * 16 + 2 * e;
+    const float hi = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(tb + off)));
+    if (fmt != FMT_F32) return hi * wscale;
+    const float mid = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(tb + 512 + off)));
+    const float lo = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(tb + 1024 + off)));
+    return ((hi + mid * F32_MID) + lo * F32_LO) * wscale;
+}
 
 // logical (tile-order) row p of a re-tiled matrix -> (source matrix, source row); false for padding rows
 __host__ __device__ __forceinline__ bool map_tile_row(int rowmap, int head_dim, int src_rows, int p, int &src,
                                                       int &row) {
     src = 0;
-    if (rowmap == ROWS_ROPE_PAIRS) {
-        const int D = head_dim, head = p / D, w = p % D, j = w >> 3, r = w & 7;
-        row = head * D + 4 * j + (r >> 1) + ((r & 1) ? D / 2 : 0);
-    } else if (rowmap == ROWS_GATE_UP) {
-        src = p & 1;
-        row = p >> 1;
+    if (rowmap == ROWS_ROPE_PAIRS) {   // tile j of a head: rows 8j..8j+7 then their partners 8j+D/2..
+        const int D = head_dim, head = p / D, w = p % D, j = w >> 4, r = w & 15;
+        row = head * D + 8 * j + (r & 7) + ((r & 8) ? D / 2 : 0);
+    } else if (rowmap == ROWS_GATE_UP) {   // tile rt: gate rows 8rt..8rt+7 then up rows 8rt..8rt+7
+        src = (p >> 3) & 1;
+        row = (p >> 4) * 8 + (p & 7);
     } else {
         row = p;
     }

@@ -274,9 +274,9 @@ extern "C" int v3g_load(v3g_model **out, const uint8_t *buf, uint64_t size, int 
         return rc;
     }
     const int grp = (int)(P.H / P.G);
-    if (grp > 8 || !(P.D == 16 || P.D == 32 || P.D == 64 || P.D == 128 || P.D == 256) || P.d % 32 || P.F % 32) {
+    if (grp > 8 || !(P.D == 16 || P.D == 32 || P.D == 64 || P.D == 128) || P.d % 32 || P.F % 32) {
         delete Pp;
-        return fail(V3G_E_UNSUPPORTED, "engine supports head_dim in {16,32,64,128,256}, <= 8 query heads per KV "
+        return fail(V3G_E_UNSUPPORTED, "engine supports head_dim in {16,32,64,128}, <= 8 query heads per KV "
                                        "head, d_model and d_ff multiples of 32");
     }
     for (uint32_t l = 0; l < P.L; ++l)
@@ -530,12 +530,12 @@ struct Layout {
     uint64_t kv_bytes;
     uint64_t off_seq, off_step, off_tok_in, off_tok_ring, off_sc_ring, off_seg_ring, off_mem_pos, off_mem_score,
         off_mem_tok, off_mem_seg, off_mem_src, off_ema, off_feat, off_x, off_attn, off_h, off_qc, off_qf, off_part,
-        off_cnt, off_logits, off_amax, off_scz;
+        off_cnt, off_logits, off_amax, off_scz, off_bar, off_mk_part, off_mk_cnt;
     uint64_t total;
-    int max_splits, seg_cap, feat_dim;
+    int max_splits, seg_cap, feat_dim, mk_cnt_cap;
 };
 
-Layout make_layout(const ModelDev &md, int B, int seg_cap) {
+Layout make_layout(const ModelDev &md, int B, int seg_cap, int n_sm) {
     Layout L{};
     auto al = [](uint64_t v) { return (v + 255) & ~255ull; };
     const uint64_t row = (uint64_t)md.D * 2, G = md.G;
@@ -580,6 +580,12 @@ Layout make_layout(const ModelDev &md, int B, int seg_cap) {
     L.off_logits = take((uint64_t)B * md.vocab * 4);
     L.off_amax = take((uint64_t)B * 8);
     L.off_scz = take((uint64_t)B * 2 * std::max(1, md.seg_hidden) * 4);
+    L.off_bar = take(64);
+    if (B <= GEMV_MB) {   // persistent decode kernel scratch (one pass of <= 8 rows)
+        L.off_mk_part = take((uint64_t)8 * n_sm * 2 * 32 * 4 * 4);
+        L.mk_cnt_cap = (md.vocab + 2 * md.F + md.H * md.D + 2 * md.G * md.D + md.d) / 16 + 16;
+        L.off_mk_cnt = take((uint64_t)L.mk_cnt_cap * 4);
+    }
     L.total = cur;
     return L;
 }
@@ -589,7 +595,7 @@ Layout make_layout(const ModelDev &md, int B, int seg_cap) {
 extern "C" size_t v3g_state_arena_size(const v3g_model *m, uint32_t batch, uint32_t max_seg_budget) {
     if (!m || batch == 0 || batch > 4096 || max_seg_budget > MAX_SEG_BUDGET) return 0;
     const int cap = m->host.seg_n_feat > 0 ? (int)max_seg_budget : 0;
-    return (size_t)make_layout(m->host, (int)batch, cap).total;
+    return (size_t)make_layout(m->host, (int)batch, cap, m->n_sm).total;
 }
 
 extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_arena, size_t arena_size, uint32_t batch,
@@ -601,7 +607,7 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
     if (max_seg_budget > MAX_SEG_BUDGET) return fail(V3G_E_LIMIT, "segment budget above 16384");
     const ModelDev &md = m->host;
     const int cap = md.seg_n_feat > 0 ? (int)max_seg_budget : 0;
-    const Layout L = make_layout(md, (int)batch, cap);
+    const Layout L = make_layout(md, (int)batch, cap, m->n_sm);
     if (arena_size < L.total) return fail(V3G_E_ARENA, "arena too small");
     v3g_state *s = new v3g_state();
     s->m = m;
@@ -651,12 +657,23 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
     sd.logits = reinterpret_cast<float *>(A + L.off_logits);
     sd.amax = reinterpret_cast<unsigned long long *>(A + L.off_amax);
     sd.sc_z = reinterpret_cast<float *>(A + L.off_scz);
+    sd.bar = reinterpret_cast<unsigned int *>(A + L.off_bar);
+    sd.mk_part = L.mk_cnt_cap ? reinterpret_cast<float *>(A + L.off_mk_part) : nullptr;
+    sd.mk_cnt = L.mk_cnt_cap ? reinterpret_cast<uint32_t *>(A + L.off_mk_cnt) : nullptr;
+    s->mk_cnt_cap = L.mk_cnt_cap;
     if (cudaSetDevice(m->device) != cudaSuccess || cudaMalloc(&s->dev, sizeof(StateDev)) != cudaSuccess ||
         cudaMemcpy(s->dev, &sd, sizeof(StateDev), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaStreamCreateWithFlags(&s->cap_stream, cudaStreamNonBlocking) != cudaSuccess) {
         if (s->dev) cudaFree(s->dev);
         delete s;
         return fail(V3G_E_CUDA, "state descriptor setup failed");
+    }
+    if (!(flags & V3G_STATE_NO_PERSISTENT)) {
+        const cudaError_t em = build_mega(m, s);
+        if (em != cudaSuccess) {
+            v3g_state_free(s);
+            return fail(V3G_E_CUDA, std::string("persistent kernel setup: ") + cudaGetErrorString(em));
+        }
     }
     int rc = v3g_state_reset(s, nullptr);
     if (rc != V3G_OK) {
@@ -685,6 +702,7 @@ extern "C" void v3g_state_free(v3g_state *s) {
     drop_graphs(s);
     if (s->cap_stream) cudaStreamDestroy(s->cap_stream);
     if (s->dev) cudaFree(s->dev);
+    if (s->mk_phases) cudaFree(s->mk_phases);
     delete s;
 }
 

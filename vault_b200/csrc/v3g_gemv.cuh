@@ -1,31 +1,38 @@
 // Decode GEMV: y[b, :] = W x[b, :] for up to 8 batch rows per pass, weights streamed once from HBM.
 //
-// Each CTA (8 warps) owns 8/WK row tiles; the WK warps of a row tile split its k tiles, so every matrix shape is
-// spread over >= ~148 CTAs.  The activation rows are normalised (optional RMSNorm) and converted once per CTA into
-// shared memory as fp16 (with a per-row power-of-two scale that keeps them in fp16 range) or bf16.  Weight tiles
-// are read with 16-byte streaming loads straight into mma.sync B fragments: int8 / nibble codes become exact fp16
-// integers with one byte-permute (or mask) and one packed subtract, the tensor core multiplies them with the
-// activations and accumulates in fp32, and each 32-wide block sum is scaled by its fp16 scale in fp32.  Partial
-// sums of the WK warps are reduced in shared memory in a fixed order (deterministic), then a fused epilogue
-// consumes (y[row 2t], y[row 2t+1]) pairs in registers.
+// Weights are the A operand of mma.sync m16n8k16 (16-row tiles, see v3g.cuh), activations the B operand (batch
+// rows = the 8 columns).  Each CTA (8 warps) owns 8/WK row tiles and the WK warps of a row tile split its k tiles.
+// A warp issues the loads of its first weight tiles before it waits for the previous kernel (programmatic
+// dependent launch) and before the activation prologue, then streams double-buffered batches of tiles.  The
+// prologue converts the activation rows once per CTA into shared memory -- fp16 with a per-row power-of-two scale
+// -- and, for integer weights, the fp32 sum of every 32-wide block of the converted activations.  Every tile
+// format is fp16 on the tensor core (BF16 / F32 weights as scaled fp16 planes, see v3g.cuh); integer codes enter
+// it as exact fp16 integers
+// C + q (C = 1152 for Q8_0 via one byte-permute, C = 1032 for Q4_0 via one mask); each block result is corrected
+// by -C * blocksum and scaled by its fp16 block scale in fp32.  Partial sums of the WK warps are reduced in shared
+// memory in a fixed order (deterministic), then a fused epilogue consumes (y[row g], y[row g+8]) in registers.
 #pragma once
 #include "v3g.cuh"
 
 namespace v3g {
 
 constexpr int PRO_PLAIN = 0, PRO_RMSNORM = 1;
+constexpr int GEMV_U = 4;   // tiles per batch (two batches in flight)
 
 struct GemvSeg {
     const uint8_t *tiles;
-    int fmt, n_rtiles, n_ktiles;
+    int n_rtiles, n_ktiles;
+    float wscale;     // MatW::wscale of this segment (applied with the activation scale)
 };
 
 struct GemvArgs {
     GemvSeg seg[3];
     int n_seg;
+    int seg_base;     // segment index reported to the epilogue for seg[0]
     int total_rtiles;
     int K;            // logical K
-    int kpx;          // smem row pitch of the converted activations (elements)
+    int kpx;          // smem row pitch of the converted activations (elements) = padded K + 8
+    int nblk;         // 32-wide blocks of the padded K (block sums)
     int B;            // batch rows in this pass (<= GEMV_MB)
     int b0;           // first batch row of this pass
     int wk;           // warps per row tile
@@ -34,213 +41,290 @@ struct GemvArgs {
     int prologue;
     const float *norm_w;
     float eps;
-    int xbf16;
+    float *feat;      // optional copy of the raw input rows (scorer features), row b at feat + (b0 + b) * feat_ld
+    int feat_ld;
 };
 
-__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+__host__ __device__ constexpr bool fmt_int(int fmt) { return fmt == FMT_Q8 || fmt == FMT_Q4; }
+__host__ __device__ constexpr float fmt_offset(int fmt) { return fmt == FMT_Q8 ? 1152.f : 1032.f; }
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
     asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
-    uint32_t r;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-    return r;
-}
-// two signed int8 (bytes lo_sel / hi_sel of w) -> exact fp16x2 integers
-__device__ __forceinline__ uint32_t q8_pair(uint32_t u_biased, uint32_t sel) {
-    return hsub2_u32(__byte_perm(u_biased, 0x64646464u, sel), 0x64806480u);   // (1024 + (q+128)) - 1152
-}
-__device__ __forceinline__ uint32_t q4_pair(uint32_t w, int shift) {
-    return hsub2_u32(((w >> shift) & 0x000F000Fu) | 0x64006400u, 0x64086408u);  // (1024 + n) - 1032
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ float2 h2f2(uint32_t h) {
     __half2 v = *reinterpret_cast<__half2 *>(&h);
     return __half22float2(v);
 }
+// two +128-biased codes (bytes selected by `sel`) -> fp16x2 {1024 + u} = {1152 + q}, exact
+__device__ __forceinline__ uint32_t q8_pair(uint32_t w, uint32_t sel) { return __byte_perm(w, 0x64646464u, sel); }
+// nibbles at bits [sh, sh+4) and [sh+16, sh+20) -> fp16x2 {1024 + n} = {1032 + (n - 8)}, exact
+template <int SH>
+__device__ __forceinline__ uint32_t q4_pair(uint32_t w) {
+    return ((w >> SH) & 0x000F000Fu) | 0x64006400u;
+}
 
-// Accumulate one warp's share of a row tile: nkt consecutive k tiles starting at tile pointer `tp` whose first
-// k index is kt0 * tile_k.  xr: this lane's activation row in smem (nullptr when its batch row g >= B).
-template <int FMT, int U>
-__device__ __forceinline__ void gemv_tiles(const uint8_t *tp, int kt0, int nkt, const uint16_t *xr, int lane,
-                                           float &acc0, float &acc1) {
-    constexpr int TK = tile_k(FMT), TB = tile_bytes(FMT);
+struct TileRegs {
+    uint4 q;        // codes / hi plane
+    uint2 s;        // block scales (Q8: .x; Q4: .x, .y)
+    uint4 m, l;     // mid / lo planes (F32)
+};
+
+template <int FMT>
+__device__ __forceinline__ void load_tile(TileRegs &r, const uint8_t *tb, int lane) {
+    r.q = ldg_stream16(tb + lane * 16);
+    if constexpr (FMT == FMT_Q8) {
+        r.s.x = __ldg(reinterpret_cast<const unsigned int *>(tb + 512 + (lane >> 2) * 4));
+    } else if constexpr (FMT == FMT_Q4) {
+        r.s = __ldg(reinterpret_cast<const uint2 *>(tb + 512 + (lane >> 2) * 8));
+    } else if constexpr (FMT == FMT_F32) {
+        r.m = ldg_stream16(tb + 512 + lane * 16);
+        r.l = ldg_stream16(tb + 1024 + lane * 16);
+    }
+}
+
+// activation fragment of k step starting at kk for this lane (zero when its batch row g >= B)
+__device__ __forceinline__ void bfrag(const uint16_t *xr, int kk, int t, uint32_t &b0, uint32_t &b1) {
+    if (xr) {
+        b0 = *reinterpret_cast<const uint32_t *>(xr + kk + 2 * t);
+        b1 = *reinterpret_cast<const uint32_t *>(xr + kk + 2 * t + 8);
+    } else {
+        b0 = 0u;
+        b1 = 0u;
+    }
+}
+
+template <int FMT>
+__device__ __forceinline__ void compute_tile(const TileRegs &r, int kt, const uint16_t *xr, const float *bsum, int t,
+                                             float (&acc)[4]) {
+    constexpr int TK = tile_k(FMT);
+    const int kb = kt * TK;
+    const uint32_t w[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
+    if constexpr (FMT == FMT_Q8) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+            uint32_t b0, b1;
+            bfrag(xr, kb + 16 * s, t, b0, b1);
+            mma16816(d, q8_pair(w[2 * s], 0x4140u), q8_pair(w[2 * s], 0x4342u), q8_pair(w[2 * s + 1], 0x4140u),
+                     q8_pair(w[2 * s + 1], 0x4342u), b0, b1);
+        }
+        const float2 S = *reinterpret_cast<const float2 *>(bsum + kt * GEMV_MB + 2 * t);   // batch 2t, 2t+1
+        const float2 ds = h2f2(r.s.x);                                                   // rows g, g+8
+        acc[0] = fmaf(ds.x, fmaf(-1152.f, S.x, d[0]), acc[0]);
+        acc[1] = fmaf(ds.x, fmaf(-1152.f, S.y, d[1]), acc[1]);
+        acc[2] = fmaf(ds.y, fmaf(-1152.f, S.x, d[2]), acc[2]);
+        acc[3] = fmaf(ds.y, fmaf(-1152.f, S.y, d[3]), acc[3]);
+    } else if constexpr (FMT == FMT_Q4) {
+        const uint32_t sc[2] = {r.s.x, r.s.y};
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk) {
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ss = 0; ss < 2; ++ss) {
+                const int s = 2 * blk + ss;
+                uint32_t b0, b1;
+                bfrag(xr, kb + 16 * s, t, b0, b1);
+                mma16816(d, q4_pair<0>(w[s]), q4_pair<4>(w[s]), q4_pair<8>(w[s]), q4_pair<12>(w[s]), b0, b1);
+            }
+            const float2 S = *reinterpret_cast<const float2 *>(bsum + (2 * kt + blk) * GEMV_MB + 2 * t);
+            const float2 ds = h2f2(sc[blk]);
+            acc[0] = fmaf(ds.x, fmaf(-1032.f, S.x, d[0]), acc[0]);
+            acc[1] = fmaf(ds.x, fmaf(-1032.f, S.y, d[1]), acc[1]);
+            acc[2] = fmaf(ds.y, fmaf(-1032.f, S.x, d[2]), acc[2]);
+            acc[3] = fmaf(ds.y, fmaf(-1032.f, S.y, d[3]), acc[3]);
+        }
+    } else if constexpr (FMT == FMT_F32) {   // planes accumulate apart, then hi + 2^-11 mid + 2^-22 lo
+        uint32_t b0, b1;
+        bfrag(xr, kb, t, b0, b1);
+        float dm[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(acc, w[0], w[1], w[2], w[3], b0, b1);
+        mma16816(dm, r.m.x, r.m.y, r.m.z, r.m.w, b0, b1);
+        mma16816(dl, r.l.x, r.l.y, r.l.z, r.l.w, b0, b1);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] = fmaf(dm[i], F32_MID, fmaf(dl[i], F32_LO, acc[i]));
+    } else {
+        uint32_t b0, b1;
+        bfrag(xr, kb, t, b0, b1);
+        mma16816(acc, w[0], w[1], w[2], w[3], b0, b1);
+    }
+}
+
+template <int FMT>
+__device__ __forceinline__ void prefetch_tiles(TileRegs (&pre)[GEMV_U], const uint8_t *tp, int nkt, int lane) {
+#pragma unroll
+    for (int u = 0; u < GEMV_U; ++u)
+        if (u < nkt) load_tile<FMT>(pre[u], tp + (size_t)u * tile_bytes(FMT), lane);
+}
+
+// stream nkt tiles starting at tp (the first GEMV_U already in `pre`), double-buffered
+template <int FMT>
+__device__ __forceinline__ void stream_tiles(TileRegs (&pre)[GEMV_U], const uint8_t *tp, int kt0, int nkt,
+                                             const uint16_t *xr, const float *bsum, int lane, float (&acc)[4]) {
+    constexpr int TB = tile_bytes(FMT);
     const int t = lane & 3;
-    for (int i = 0; i < nkt; i += U) {
-        uint4 q[U];
-        uint4 sc[U];
+    for (int i = 0; i < nkt; i += GEMV_U) {
+        TileRegs nxt[GEMV_U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (i + u < nkt) {
-                const uint8_t *tb = tp + (size_t)(i + u) * TB;
-                q[u] = ldg_stream16(tb + lane * 16);
-                if constexpr (FMT == FMT_Q8) {
-                    uint2 s2 = ldg_stream8(tb + 512 + t * 8);
-                    sc[u] = make_uint4(s2.x, s2.y, 0u, 0u);
-                } else if constexpr (FMT == FMT_Q4) {
-                    sc[u] = ldg_stream16(tb + 512 + t * 16);
-                } else if constexpr (FMT == FMT_F32) {
-                    sc[u] = ldg_stream16(tb + 512 + lane * 16);               // mid plane
-                }
-            }
-        }
-        uint4 lo[U];
-        if constexpr (FMT == FMT_F32) {
+        for (int u = 0; u < GEMV_U; ++u)
+            if (i + GEMV_U + u < nkt) load_tile<FMT>(nxt[u], tp + (size_t)(i + GEMV_U + u) * TB, lane);
 #pragma unroll
-            for (int u = 0; u < U; ++u)
-                if (i + u < nkt) lo[u] = ldg_stream16(tp + (size_t)(i + u) * TB + 1024 + lane * 16);
-        }
+        for (int u = 0; u < GEMV_U; ++u)
+            if (i + u < nkt) compute_tile<FMT>(pre[u], kt0 + i + u, xr, bsum, t, acc);
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (i + u >= nkt) break;
-            const int kb = (kt0 + i + u) * TK;
-            const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
-            auto afrag = [&](int s, uint32_t &a0, uint32_t &a2) {
-                if (xr) {
-                    a0 = *reinterpret_cast<const uint32_t *>(xr + kb + 16 * s + 2 * t);
-                    a2 = *reinterpret_cast<const uint32_t *>(xr + kb + 16 * s + 2 * t + 8);
-                } else {
-                    a0 = 0u;
-                    a2 = 0u;
-                }
-            };
-            if constexpr (FMT == FMT_Q8) {
-                const uint32_t sc2[2] = {sc[u].x, sc[u].y};
-#pragma unroll
-                for (int blk = 0; blk < 2; ++blk) {
-                    float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int ss = 0; ss < 2; ++ss) {
-                        const int s = 2 * blk + ss;
-                        uint32_t a0, a2;
-                        afrag(s, a0, a2);
-                        const uint32_t ub = w[s] ^ 0x80808080u;
-                        mma_f16(d, a0, a2, q8_pair(ub, 0x4140u), q8_pair(ub, 0x4342u));
-                    }
-                    const float2 ds = h2f2(sc2[blk]);
-                    acc0 = fmaf(ds.x, d[0], acc0);
-                    acc1 = fmaf(ds.y, d[1], acc1);
-                }
-            } else if constexpr (FMT == FMT_Q4) {
-                const uint32_t sc4[4] = {sc[u].x, sc[u].y, sc[u].z, sc[u].w};
-#pragma unroll
-                for (int blk = 0; blk < 4; ++blk) {
-                    float d[4] = {0.f, 0.f, 0.f, 0.f};
-                    uint32_t a0, a2;
-                    afrag(2 * blk, a0, a2);
-                    mma_f16(d, a0, a2, q4_pair(w[blk], 0), q4_pair(w[blk], 4));
-                    afrag(2 * blk + 1, a0, a2);
-                    mma_f16(d, a0, a2, q4_pair(w[blk], 8), q4_pair(w[blk], 12));
-                    const float2 ds = h2f2(sc4[blk]);
-                    acc0 = fmaf(ds.x, d[0], acc0);
-                    acc1 = fmaf(ds.y, d[1], acc1);
-                }
-            } else {
-                float d[4] = {acc0, acc1, 0.f, 0.f};
-#pragma unroll
-                for (int s = 0; s < 2; ++s) {
-                    uint32_t a0, a2;
-                    afrag(s, a0, a2);
-                    if constexpr (FMT == FMT_F16) {
-                        mma_f16(d, a0, a2, w[2 * s], w[2 * s + 1]);
-                    } else {
-                        mma_bf16(d, a0, a2, w[2 * s], w[2 * s + 1]);
-                        if constexpr (FMT == FMT_F32) {
-                            const uint32_t m[4] = {sc[u].x, sc[u].y, sc[u].z, sc[u].w};
-                            const uint32_t l[4] = {lo[u].x, lo[u].y, lo[u].z, lo[u].w};
-                            mma_bf16(d, a0, a2, m[2 * s], m[2 * s + 1]);
-                            mma_bf16(d, a0, a2, l[2 * s], l[2 * s + 1]);
-                        }
-                    }
-                }
-                acc0 = d[0];
-                acc1 = d[1];
-            }
-        }
+        for (int u = 0; u < GEMV_U; ++u) pre[u] = nxt[u];
     }
 }
 
-// Convert the pass's activation rows to 16-bit in shared memory; returns per-row output scale in s_scale[b].
-__device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_scale, float *s_red) {
-    const int tid = threadIdx.x, nt = blockDim.x;
-    for (int b = 0; b < a.B; ++b) {
-        const float *xr = a.x + (size_t)(a.b0 + b) * a.x_ld;
-        float ss = 0.f, mx = 0.f;
-        for (int k = tid; k < a.K; k += nt) {
-            const float v = xr[k];
-            ss = fmaf(v, v, ss);
-            mx = fmaxf(mx, fabsf(a.prologue == PRO_RMSNORM ? v * a.norm_w[k] : v));
+// 16 consecutive fp32 values of a row; four 16-byte loads in flight when the row is made of whole 16-byte-aligned
+// 32-blocks, else guarded scalar loads (zero past n).  L2 loads for activations (written by other SMs).
+template <bool L2>
+__device__ __forceinline__ void load16(const float *p, bool vec, int n, float (&v)[16]) {
+    if (vec) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 q = L2 ? __ldcg(reinterpret_cast<const float4 *>(p) + j) : __ldg(reinterpret_cast<const float4 *>(p) + j);
+            v[4 * j] = q.x;
+            v[4 * j + 1] = q.y;
+            v[4 * j + 2] = q.z;
+            v[4 * j + 3] = q.w;
         }
-        ss = warp_sum(ss);
-        mx = warp_max(mx);
-        if ((tid & 31) == 0) {
-            s_red[tid >> 5] = ss;
-            s_red[32 + (tid >> 5)] = mx;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            float S = 0.f, Mx = 0.f;
-            for (int w = 0; w < nt / 32; ++w) {
-                S += s_red[w];
-                Mx = fmaxf(Mx, s_red[32 + w]);
-            }
-            const float inv = (a.prologue == PRO_RMSNORM) ? 1.0f / sqrtf(S / (float)a.K + a.eps) : 1.0f;
-            float e = 0.f;
-            if (!a.xbf16 && Mx * inv > 0.f) {
-                int ex;
-                frexpf(Mx * inv, &ex);
-                e = (float)(ex - 14);   // largest |x| scaled into (2^13, 2^14]
-            }
-            s_red[64] = inv;
-            s_scale[b] = exp2f(e);
-            s_red[65] = exp2f(-e);
-        }
-        __syncthreads();
-        const float inv = s_red[64], sdown = s_red[65];
-        uint16_t *xo = xs + b * a.kpx;
-        for (int k = tid; k < a.kpx; k += nt) {
-            float v = 0.f;
-            if (k < a.K) {
-                v = xr[k] * inv;
-                if (a.prologue == PRO_RMSNORM) v *= a.norm_w[k];
-            }
-            if (a.xbf16) {
-                __nv_bfloat16 h = __float2bfloat16_rn(v);
-                xo[k] = *reinterpret_cast<uint16_t *>(&h);
-            } else {
-                __half h = __float2half_rn(v * sdown);
-                xo[k] = *reinterpret_cast<uint16_t *>(&h);
-            }
-        }
-        __syncthreads();
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = j < n ? (L2 ? __ldcg(p + j) : __ldg(p + j)) : 0.f;
     }
 }
 
-template <class Epi>
+// Convert the pass's activation rows once per CTA into shared memory: RMSNorm (optional), fp16 with a per-row
+// power-of-two scale (largest |x| scaled into (2^13, 2^14]); s_scale[b] receives the scale to undo and, with
+// BSUM, bsum[blk * 8 + b] the fp32 sum of converted 32-wide block blk of row b.  Work items are half blocks (16
+// values; the two halves of a block sit in adjacent lanes): one stats pass and one convert pass, each with all of
+// a thread's loads in flight at once.
+template <bool BSUM>
+__device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_scale, float *s_red, float *bsum) {
+    const int tid = threadIdx.x, nt = blockDim.x, nw = nt / 32;
+    const bool norm = a.prologue == PRO_RMSNORM;
+    const bool vec = (a.K & 31) == 0 && (a.x_ld & 3) == 0;
+    const int nb = (a.K + 31) >> 5, nh = 2 * nb, items = a.B * nh;
+    float ss[GEMV_MB], mx[GEMV_MB];
+#pragma unroll
+    for (int b = 0; b < GEMV_MB; ++b) {
+        ss[b] = 0.f;
+        mx[b] = 0.f;
+    }
+    for (int it = tid; it < items; it += nt) {
+        const int b = it / nh, h = it - b * nh, n = a.K - h * 16;
+        float v[16], w[16];
+        load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, v);
+        if (norm) load16<false>(a.norm_w + h * 16, vec, n, w);
+        float s2 = 0.f, m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            s2 = fmaf(v[j], v[j], s2);
+            m = fmaxf(m, fabsf(norm ? v[j] * w[j] : v[j]));
+        }
+#pragma unroll
+        for (int bb = 0; bb < GEMV_MB; ++bb)
+            if (bb == b) {
+                ss[bb] += s2;
+                mx[bb] = fmaxf(mx[bb], m);
+            }
+    }
+#pragma unroll
+    for (int b = 0; b < GEMV_MB; ++b) {
+        if (b < a.B) {
+            const float S = warp_sum(ss[b]), M = warp_max(mx[b]);
+            if ((tid & 31) == 0) {
+                s_red[b * 8 + (tid >> 5)] = S;
+                s_red[64 + b * 8 + (tid >> 5)] = M;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid < a.B) {
+        float S = 0.f, Mx = 0.f;
+        for (int w = 0; w < nw; ++w) {
+            S += s_red[tid * 8 + w];
+            Mx = fmaxf(Mx, s_red[64 + tid * 8 + w]);
+        }
+        const float inv = norm ? 1.0f / sqrtf(S / (float)a.K + a.eps) : 1.0f;
+        float e = 0.f;
+        if (Mx * inv > 0.f) {
+            int ex;
+            frexpf(Mx * inv, &ex);
+            e = (float)(ex - 14);   // largest |x| scaled into (2^13, 2^14]
+        }
+        s_red[128 + tid] = inv * exp2f(-e);   // multiplier applied before rounding to 16 bits
+        s_scale[tid] = exp2f(e);
+    }
+    __syncthreads();
+    for (int base = 0; base < items; base += nt) {   // warp-uniform trip count (block sums pair adjacent lanes)
+        const int it = base + tid;
+        const bool act = it < items;
+        const int b = act ? it / nh : 0, h = act ? it - b * nh : 0, n = a.K - h * 16;
+        float bs = 0.f;
+        if (act) {
+            const float *xr = a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16;
+            float v[16], w[16];
+            load16<true>(xr, vec, n, v);
+            if (norm) load16<false>(a.norm_w + h * 16, vec, n, w);
+            if (a.feat && blockIdx.x == 0) {
+                float *f = a.feat + (size_t)(a.b0 + b) * a.feat_ld + h * 16;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (j < n) f[j] = v[j];
+            }
+            const float mul = s_red[128 + b];
+            uint32_t hw[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float x0 = (norm ? v[2 * j] * w[2 * j] : v[2 * j]) * mul;
+                const float x1 = (norm ? v[2 * j + 1] * w[2 * j + 1] : v[2 * j + 1]) * mul;
+                const __half2 hv = __floats2half2_rn(x0, x1);
+                const float2 back = __half22float2(hv);
+                bs += back.x + back.y;
+                hw[j] = *reinterpret_cast<const uint32_t *>(&hv);
+            }
+            uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)b * a.kpx + h * 16);
+            dst[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            dst[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+        }
+        if (BSUM) {
+            bs += __shfl_xor_sync(0xffffffffu, bs, 1);
+            if (act && (h & 1) == 0) bsum[(h >> 1) * GEMV_MB + b] = bs;
+        }
+    }
+    // zero the padding columns and the block sums of absent rows / padding blocks
+    const int kp = a.kpx, pad = kp - nb * 32;
+    for (int idx = tid; idx < a.B * pad; idx += nt) xs[(size_t)(idx / pad) * kp + nb * 32 + idx % pad] = 0;
+    if (BSUM)
+        for (int idx = tid; idx < a.nblk * GEMV_MB; idx += nt) {
+            const int blk = idx / GEMV_MB, b = idx - blk * GEMV_MB;
+            if (b >= a.B || blk >= nb) bsum[idx] = 0.f;
+        }
+    __syncthreads();
+}
+
+template <int FA, int FB, class Epi>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi) {
+    constexpr bool BSUM = fmt_int(FA) || fmt_int(FB);
     extern __shared__ __align__(16) uint8_t smem[];
-    float *s_red = reinterpret_cast<float *>(smem);                  // 96 floats
-    float *s_scale = s_red + 96;                                     // GEMV_MB
-    float *s_part = s_scale + GEMV_MB;                               // [8 warps][32 lanes][2]
-    uint16_t *xs = reinterpret_cast<uint16_t *>(s_part + 8 * 32 * 2);
-    gemv_prologue(a, xs, s_scale, s_red);
+    float *s_red = reinterpret_cast<float *>(smem);                  // 136 floats
+    float *s_scale = s_red + 136;                                    // GEMV_MB
+    float *s_part = s_scale + GEMV_MB;                               // [8 warps][32 lanes][4]
+    float *bsum = s_part + 8 * 32 * 4;                               // [nblk][GEMV_MB]
+    uint16_t *xs = reinterpret_cast<uint16_t *>(bsum + (BSUM ? a.nblk * GEMV_MB : 0));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rtc = 8 / a.wk;
     const int rs = warp / a.wk, kw = warp % a.wk;
     const int gr = blockIdx.x * rtc + rs;
-    float acc0 = 0.f, acc1 = 0.f;
-    int si = 0, rt = gr;
     const bool active = gr < a.total_rtiles;
+    int si = 0, rt = gr, k0 = 0, nkt = 0;
+    const uint8_t *tp = nullptr;
     if (active) {
         while (si < a.n_seg - 1 && rt >= a.seg[si].n_rtiles) {
             rt -= a.seg[si].n_rtiles;
@@ -248,42 +332,62 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
         }
         const GemvSeg &sg = a.seg[si];
         const int KT = sg.n_ktiles;
-        const int k0 = (kw * KT) / a.wk, k1 = ((kw + 1) * KT) / a.wk;
+        k0 = (kw * KT) / a.wk;
+        nkt = ((kw + 1) * KT) / a.wk - k0;
+        tp = sg.tiles + ((size_t)rt * KT + k0) * (si == 0 ? tile_bytes(FA) : tile_bytes(FB));
+    }
+    // weights do not depend on earlier kernels: start streaming before waiting for them
+    TileRegs pre[GEMV_U];
+    if (active) {
+        if (si == 0) prefetch_tiles<FA>(pre, tp, nkt, lane);
+        else prefetch_tiles<FB>(pre, tp, nkt, lane);
+    }
+    griddep_wait();
+    griddep_launch();
+    gemv_prologue<BSUM>(a, xs, s_scale, s_red, bsum);
+
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (active) {
         const int g = lane >> 2;
         const uint16_t *xr = g < a.B ? xs + g * a.kpx : nullptr;
-        const uint8_t *tp = sg.tiles + ((size_t)rt * KT + k0) * tile_bytes(sg.fmt);
-        switch (sg.fmt) {
-            case FMT_Q8: gemv_tiles<FMT_Q8, 4>(tp, k0, k1 - k0, xr, lane, acc0, acc1); break;
-            case FMT_Q4: gemv_tiles<FMT_Q4, 4>(tp, k0, k1 - k0, xr, lane, acc0, acc1); break;
-            case FMT_BF16: gemv_tiles<FMT_BF16, 4>(tp, k0, k1 - k0, xr, lane, acc0, acc1); break;
-            case FMT_F16: gemv_tiles<FMT_F16, 4>(tp, k0, k1 - k0, xr, lane, acc0, acc1); break;
-            default: gemv_tiles<FMT_F32, 2>(tp, k0, k1 - k0, xr, lane, acc0, acc1); break;
-        }
+        if (si == 0) stream_tiles<FA>(pre, tp, k0, nkt, xr, bsum, lane, acc);
+        else stream_tiles<FB>(pre, tp, k0, nkt, xr, bsum, lane, acc);
     }
     if (a.wk > 1) {
-        s_part[(warp * 32 + lane) * 2 + 0] = acc0;
-        s_part[(warp * 32 + lane) * 2 + 1] = acc1;
+        *reinterpret_cast<float4 *>(&s_part[(warp * 32 + lane) * 4]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
         __syncthreads();
         if (kw == 0) {
-            acc0 = 0.f;
-            acc1 = 0.f;
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
             for (int w = 0; w < a.wk; ++w) {
-                acc0 += s_part[((warp + w) * 32 + lane) * 2 + 0];
-                acc1 += s_part[((warp + w) * 32 + lane) * 2 + 1];
+                const float4 p = *reinterpret_cast<const float4 *>(&s_part[((warp + w) * 32 + lane) * 4]);
+                acc[0] += p.x;
+                acc[1] += p.y;
+                acc[2] += p.z;
+                acc[3] += p.w;
             }
         }
     }
     if (active && kw == 0) {
         const int g = lane >> 2, t = lane & 3;
-        if (g < a.B) epi(si, rt, t, a.b0 + g, acc0 * s_scale[g], acc1 * s_scale[g]);
+        const int sg = si + a.seg_base;
+        const float ws = a.seg[si].wscale;
+        if (2 * t < a.B) {
+            const float sc = s_scale[2 * t] * ws;
+            epi(sg, rt, g, a.b0 + 2 * t, acc[0] * sc, acc[2] * sc);
+        }
+        if (2 * t + 1 < a.B) {
+            const float sc = s_scale[2 * t + 1] * ws;
+            epi(sg, rt, g, a.b0 + 2 * t + 1, acc[1] * sc, acc[3] * sc);
+        }
     }
 }
 
-inline size_t gemv_smem_bytes(int B, int kpx) {
-    return (96 + GEMV_MB + 8 * 32 * 2) * sizeof(float) + (size_t)B * kpx * sizeof(uint16_t);
+inline size_t gemv_smem_bytes(const GemvArgs &a, bool bsum) {
+    return (136 + GEMV_MB + 8 * 32 * 4 + (bsum ? a.nblk * GEMV_MB : 0)) * sizeof(float) +
+           (size_t)a.B * a.kpx * sizeof(uint16_t);
 }
 
 // Host helper: choose the k split so the launch covers the GPU, fill the launch parameters.
-void gemv_plan(GemvArgs &a, int n_sm, int &grid, size_t &smem);
+void gemv_plan(GemvArgs &a, const int *fmts, int n_sm, int &grid, size_t &smem);
 
 }  // namespace v3g

@@ -40,6 +40,12 @@ struct v3g_state {
     cudaGraphExec_t graphs[4] = {nullptr, nullptr, nullptr, nullptr};  // [boundary][with lm head]
     uint64_t graph_B_pos[4] = {0, 0, 0, 0};
     int use_graphs = 1;
+    int use_pdl = 1;                 // programmatic dependent launch between the kernels of a step
+    // persistent decode kernel (all layers + lm head in one cooperative launch)
+    int use_mega = 0;
+    void *mk_phases = nullptr;       // device MkPhase[mk_n]; the last entry is the lm head
+    int mk_n = 0, mk_grid = 0, mk_slots = 0, mk_xr = 0, mk_cnt_cap = 0;
+    size_t mk_smem = 0;
     std::string last_error;
 };
 
@@ -54,6 +60,11 @@ cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool wa
 cudaError_t launch_prefix_refresh(const v3g_model *m, v3g_state *s, cudaStream_t st);
 cudaError_t launch_state_reset(const v3g_model *m, v3g_state *s, cudaStream_t st);
 cudaError_t init_kernel_attrs();
+// persistent decode kernel set-up for a state (sets s->use_mega when the model / batch qualify)
+cudaError_t build_mega(const v3g_model *m, v3g_state *s);
+cudaError_t launch_mega(const v3g_model *m, v3g_state *s, bool want_lm, cudaStream_t st);
+cudaError_t launch_attention(const v3g_model *m, v3g_state *s, int layer, bool pdl, cudaStream_t st);
+cudaError_t launch_argmax_finish(const v3g_model *m, v3g_state *s, bool want_lm, bool pdl, cudaStream_t st);
 cudaError_t launch_gemv_mapped(const v3g_model *m, const MatW &w, const float *x, int B, float *y, cudaStream_t st);
 cudaError_t launch_gemv_store(const v3g_model *m, const MatW &w, const float *x, int B, float *y, cudaStream_t st);
 }  // namespace v3g

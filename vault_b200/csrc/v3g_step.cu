@@ -20,31 +20,9 @@ __device__ __forceinline__ int ring_par(int64_t pos, int W) { return (int)((pos 
 
 __device__ __forceinline__ bool seg_active(const SeqCtl &q) { return q.seg_on && q.seg_budget > 0; }
 
-// element (row, k) of a re-tiled matrix with identity row order
-__device__ float tile_elem(const MatW &w, int row, int k) {
-    const int TK = tile_k(w.fmt);
-    const int rt = row >> 3, g = row & 7, kt = k / TK, kk = k % TK;
-    const int s = kk >> 4, w16 = kk & 15;
-    const int t = (w16 & 7) >> 1, e = (w16 & 1) + ((w16 & 8) ? 2 : 0);
-    const uint8_t *tb = w.tiles + ((size_t)rt * w.n_ktiles + kt) * tile_bytes(w.fmt);
-    const int lane = 4 * g + t;
-    if (w.fmt == FMT_Q8 || w.fmt == FMT_Q4) {
-        const int nblk = TK / 32, blk = kk >> 5;
-        const uint16_t sb = *reinterpret_cast<const uint16_t *>(tb + 512 + (g >> 1) * (2 * nblk * 2) +
-                                                                 (2 * blk + (g & 1)) * 2);
-        const float d = __half2float(__ushort_as_half(sb));
-        if (w.fmt == FMT_Q8) return (float)(int8_t)tb[lane * 16 + 4 * s + e] * d;
-        const int nib = ((e & 2) ? 1 : 0) | ((s & 1) << 1) | ((e & 1) << 2);
-        const uint32_t word = *reinterpret_cast<const uint32_t *>(tb + lane * 16 + 4 * (s >> 1));
-        return (float)((int)((word >> (4 * nib)) & 15u) - 8) * d;
-    }
-    const int off = lane * 16 + 2 * (4 * s + e);
-    const uint16_t v = *reinterpret_cast<const uint16_t *>(tb + off);
-    if (w.fmt == FMT_F16) return __half2float(__ushort_as_half(v));
-    if (w.fmt == FMT_BF16) return __uint_as_float((uint32_t)v << 16);
-    const uint16_t mv = *reinterpret_cast<const uint16_t *>(tb + 512 + off);
-    const uint16_t lv = *reinterpret_cast<const uint16_t *>(tb + 1024 + off);
-    return (__uint_as_float((uint32_t)v << 16) + __uint_as_float((uint32_t)mv << 16)) + __uint_as_float((uint32_t)lv << 16);
+// element (row, k) of the tied embedding (identity row order)
+__device__ __forceinline__ float tile_elem(const MatW &w, int row, int k) {
+    return tile_value(w.tiles, w.fmt, w.n_ktiles, w.wscale, row, k);
 }
 
 // ChatML system-prompt auto-pin state machine for one token (src/vault_v3_model.py:2224-2252)
@@ -86,6 +64,8 @@ __device__ __forceinline__ int read_token(const ModelDev &m, const StateDev &s, 
 
 // boundary steps: auto-pin must run before the eviction (it sets n_pin used by t_start and the sink rotation)
 __global__ void k_pin(const ModelDev *mp, const StateDev *sp) {
+    griddep_wait();
+    griddep_launch();
     const StateDev &s = *sp;
     const int b = blockIdx.x;
     if (threadIdx.x == 0) auto_pin_update(*mp, s.seq[b], s.step->pos, read_token(*mp, s, b));
@@ -94,6 +74,8 @@ __global__ void k_pin(const ModelDev *mp, const StateDev *sp) {
 // token bookkeeping + segment ids + embedding (src/vault_v3_model.py:2257-2283)
 template <bool PIN>
 __global__ void k_begin(const ModelDev *mp, const StateDev *sp) {
+    griddep_wait();
+    griddep_launch();
     const ModelDev &m = *mp;
     const StateDev &s = *sp;
     const int b = blockIdx.x;
@@ -136,6 +118,8 @@ __global__ void k_begin(const ModelDev *mp, const StateDev *sp) {
             }
         }
         s_tok = tok;
+        s.amax[b] = 0ull;
+        if (b == 0) *s.bar = 0u;   // grid-barrier counter of this step's persistent decode kernel
     }
     __syncthreads();
     const int tok = s_tok;
@@ -149,9 +133,10 @@ struct EpiQKV {
     const StateDev *s;
     int layer;
     const float *bq, *bk, *bv;
-    __device__ void operator()(int seg, int rt, int t, int b, float y0, float y1) const {
+    // lane holds tile rows (g, g+8) = RoPE partners (i, i + D/2) of one head
+    __device__ void operator()(int seg, int rt, int g, int b, float y0, float y1) const {
         const int D = m->D, W = m->W, hd = D / 2;
-        const int head = rt / (D / 8), j = rt % (D / 8), i = 4 * j + t;
+        const int head = rt / (D / TILE_ROWS), j = rt % (D / TILE_ROWS), i = 8 * j + g;
         const int r0 = head * D + i, r1 = r0 + hd;
         const int64_t pos = s->step->pos;
         const int c = (int)(pos % W), par = ring_par(pos, W);
@@ -170,58 +155,59 @@ struct EpiQKV {
             }
         } else if (seg == 1) {
             const float a = y0 + bk[r0], bb = y1 + bk[r1];
-            __nv_bfloat16 *kr = kvp(*s, layer, b, ring_off(*s, par, KIND_KRAW, head, c));
-            __nv_bfloat16 *ko = kvp(*s, layer, b, ring_off(*s, par, KIND_KROT, head, c));
-            kr[i] = __float2bfloat16_rn(a);
-            kr[i + hd] = __float2bfloat16_rn(bb);
-            ko[i] = __float2bfloat16_rn(a * cs - bb * sn);
-            ko[i + hd] = __float2bfloat16_rn(bb * cs + a * sn);
+            kv_t *kr = kvp(*s, layer, b, ring_off(*s, par, KIND_KRAW, head, c));
+            kv_t *ko = kvp(*s, layer, b, ring_off(*s, par, KIND_KROT, head, c));
+            kr[i] = f2kv(a);
+            kr[i + hd] = f2kv(bb);
+            ko[i] = f2kv(a * cs - bb * sn);
+            ko[i + hd] = f2kv(bb * cs + a * sn);
             if (pos < s->sink_cap) {
-                __nv_bfloat16 *sk = kvp(*s, layer, b, sink_off(*s, SINK_KRAW, head, (int)pos));
-                sk[i] = __float2bfloat16_rn(a);
-                sk[i + hd] = __float2bfloat16_rn(bb);
+                kv_t *sk = kvp(*s, layer, b, sink_off(*s, SINK_KRAW, head, (int)pos));
+                sk[i] = f2kv(a);
+                sk[i + hd] = f2kv(bb);
             }
         } else {
             const float a = y0 + bv[r0], bb = y1 + bv[r1];
-            __nv_bfloat16 *vv = kvp(*s, layer, b, ring_off(*s, par, KIND_V, head, c));
-            vv[i] = __float2bfloat16_rn(a);
-            vv[i + hd] = __float2bfloat16_rn(bb);
+            kv_t *vv = kvp(*s, layer, b, ring_off(*s, par, KIND_V, head, c));
+            vv[i] = f2kv(a);
+            vv[i + hd] = f2kv(bb);
             if (pos < s->sink_cap) {
-                __nv_bfloat16 *sv = kvp(*s, layer, b, sink_off(*s, SINK_V, head, (int)pos));
-                sv[i] = __float2bfloat16_rn(a);
-                sv[i + hd] = __float2bfloat16_rn(bb);
+                kv_t *sv = kvp(*s, layer, b, sink_off(*s, SINK_V, head, (int)pos));
+                sv[i] = f2kv(a);
+                sv[i + hd] = f2kv(bb);
             }
         }
     }
 };
 
-struct EpiResid {   // x[b, row] += y
+struct EpiResid {   // x[b, row] += y   (identity row order: tile rows g, g+8)
     float *x;
     int ld, rows;
-    __device__ void operator()(int, int rt, int t, int b, float y0, float y1) const {
-        const int r = 8 * rt + 2 * t;
-        if (r < rows) x[(size_t)b * ld + r] += y0;
-        if (r + 1 < rows) x[(size_t)b * ld + r + 1] += y1;
+    __device__ void operator()(int, int rt, int g, int b, float y0, float y1) const {
+        const int r = TILE_ROWS * rt + g;
+        // L1-bypassing read: inside the persistent kernel other SMs updated x in earlier phases
+        if (r < rows) x[(size_t)b * ld + r] = __ldcg(&x[(size_t)b * ld + r]) + y0;
+        if (r + 8 < rows) x[(size_t)b * ld + r + 8] = __ldcg(&x[(size_t)b * ld + r + 8]) + y1;
     }
 };
 
 struct EpiGateUp {  // h[b, f] = silu(gate_f) * up_f   (src/vault_v3_model.py:1149-1150)
     float *h;
     int F;
-    __device__ void operator()(int, int rt, int t, int b, float g, float u) const {
-        const int f = 4 * rt + t;
-        if (f < F) h[(size_t)b * F + f] = g / (1.0f + expf(-g)) * u;
+    __device__ void operator()(int, int rt, int g, int b, float gt, float u) const {
+        const int f = 8 * rt + g;
+        if (f < F) h[(size_t)b * F + f] = gt / (1.0f + expf(-gt)) * u;
     }
 };
 
 struct EpiStoreMapped {   // y[b, source row] = value (undoes the RoPE-pair / gate-up row order of the tiles)
     float *y;
     int ld, rowmap, head_dim, src_rows;
-    __device__ void operator()(int, int rt, int t, int b, float y0, float y1) const {
+    __device__ void operator()(int, int rt, int g, int b, float y0, float y1) const {
         int src, row;
-        if (map_tile_row(rowmap, head_dim, src_rows, 8 * rt + 2 * t, src, row))
+        if (map_tile_row(rowmap, head_dim, src_rows, TILE_ROWS * rt + g, src, row))
             y[(size_t)b * ld + src * src_rows + row] = y0;
-        if (map_tile_row(rowmap, head_dim, src_rows, 8 * rt + 2 * t + 1, src, row))
+        if (map_tile_row(rowmap, head_dim, src_rows, TILE_ROWS * rt + g + 8, src, row))
             y[(size_t)b * ld + src * src_rows + row] = y1;
     }
 };
@@ -229,169 +215,22 @@ struct EpiStoreMapped {   // y[b, source row] = value (undoes the RoPE-pair / ga
 struct EpiStore {   // y[b, row] = value
     float *y;
     int ld, rows;
-    __device__ void operator()(int, int rt, int t, int b, float y0, float y1) const {
-        const int r = 8 * rt + 2 * t;
+    __device__ void operator()(int, int rt, int g, int b, float y0, float y1) const {
+        const int r = TILE_ROWS * rt + g;
         if (r < rows) y[(size_t)b * ld + r] = y0;
-        if (r + 1 < rows) y[(size_t)b * ld + r + 1] = y1;
+        if (r + 8 < rows) y[(size_t)b * ld + r + 8] = y1;
     }
 };
 
-// copy of the residual stream entering a scorer feature layer (src/vault_v3_model.py:2287-2288)
-__global__ void k_copy_feat(const StateDev *sp, int d, int fi) {
-    const StateDev &s = *sp;
-    const int b = blockIdx.x;
-    if (!seg_active(s.seq[b])) return;
-    for (int k = threadIdx.x; k < d; k += blockDim.x) s.feat[(size_t)b * s.feat_dim + fi * d + k] = s.x[(size_t)b * d + k];
-}
-
 // ------------------------------------------------------------------------------------------ attention
-// Split-KV decode attention for one layer.  grid = (max_splits, G, B); each CTA scores ATT_KEYS_PER_CTA keys of
-// the concatenation [sink S | bank M | prev W | cur c+1] for the `grp` query heads sharing KV head g, writes an
-// unnormalised partial (o, m, l), and the last CTA of (b, g) merges the partials in split order.
-template <int D>
-__global__ void __launch_bounds__(ATT_THREADS) k_attention(const ModelDev *mp, const StateDev *sp, int layer,
-                                                           float scale) {
-    const ModelDev &m = *mp;
-    const StateDev &s = *sp;
-    const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-    const int W = m.W, H = m.H, grp = H / m.G;
-    const int64_t pos = s.step->pos;
-    const int c = (int)(pos % W), par = ring_par(pos, W);
-    const SeqCtl &q = s.seq[b];
-    const int n_sk = pos >= 2 * W ? q.n_pin : 0;
-    const int n_seg = (pos >= 2 * W && seg_active(q)) ? q.mem_cnt : 0;
-    const int n_prev = pos >= W ? W : 0;
-    const int n_cur = c + 1;
-    const int total = n_sk + n_seg + n_prev + n_cur;
-    const int n_splits = (total + ATT_KEYS_PER_CTA - 1) / ATT_KEYS_PER_CTA;
-    if (split >= n_splits) return;
-    const int j0 = split * ATT_KEYS_PER_CTA, j1 = min(total, j0 + ATT_KEYS_PER_CTA), nk = j1 - j0;
-
-    __shared__ float s_qf[8][D], s_qc[8][D];
-    __shared__ float s_p[8][ATT_KEYS_PER_CTA];
-    __shared__ float s_m[8], s_l[8];
-    __shared__ int s_last;
-    const int tid = threadIdx.x;
-    for (int idx = tid; idx < grp * D; idx += blockDim.x) {
-        const int hr = idx / D, dd = idx % D;
-        const size_t qo = ((size_t)b * H + g * grp + hr) * D + dd;
-        s_qc[hr][dd] = s.q_cur[qo];
-        s_qf[hr][dd] = pos >= W ? s.q_far[qo] : 0.f;
-    }
-    __syncthreads();
-    // scores: one thread per key
-    for (int jj = tid; jj < nk; jj += blockDim.x) {
-        const int j = j0 + jj;
-        const __nv_bfloat16 *kp;
-        bool far = true;
-        if (j < n_sk) kp = kvp(s, layer, b, sink_off(s, SINK_KROT, g, j));
-        else if (j < n_sk + n_seg) kp = kvp(s, layer, b, bank_rot_off(s, g, j - n_sk));
-        else if (j < n_sk + n_seg + n_prev) kp = kvp(s, layer, b, ring_off(s, par ^ 1, KIND_KROT, g, j - n_sk - n_seg));
-        else {
-            kp = kvp(s, layer, b, ring_off(s, par, KIND_KROT, g, j - n_sk - n_seg - n_prev));
-            far = false;
-        }
-        float acc[8];
-#pragma unroll
-        for (int hr = 0; hr < 8; ++hr) acc[hr] = 0.f;
-        const float(*qs)[D] = far ? s_qf : s_qc;
-#pragma unroll 4
-        for (int d0 = 0; d0 < D; d0 += 8) {
-            const uint4 raw = *reinterpret_cast<const uint4 *>(kp + d0);
-            const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
-            float kf[8];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(k2[e]);
-                kf[2 * e] = f.x;
-                kf[2 * e + 1] = f.y;
-            }
-#pragma unroll
-            for (int hr = 0; hr < 8; ++hr) {
-                if (hr < grp) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[hr] = fmaf(qs[hr][d0 + e], kf[e], acc[hr]);
-                }
-            }
-        }
-        for (int hr = 0; hr < grp; ++hr) s_p[hr][jj] = acc[hr] * scale;
-    }
-    __syncthreads();
-    // softmax pieces per head (warp w handles heads w, w+4)
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int hr = warp; hr < grp; hr += blockDim.x / 32) {
-        float mx = -INFINITY;
-        for (int jj = lane; jj < nk; jj += 32) mx = fmaxf(mx, s_p[hr][jj]);
-        mx = warp_max(mx);
-        float l = 0.f;
-        for (int jj = lane; jj < nk; jj += 32) {
-            const float p = expf(s_p[hr][jj] - mx);
-            s_p[hr][jj] = p;
-            l += p;
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            s_m[hr] = mx;
-            s_l[hr] = l;
-        }
-    }
-    __syncthreads();
-    // o[hr][d] = sum_j p[hr][j] v[j][d]; thread layout: dims x key-phase
-    float *part = s.att_part + ((((size_t)b * m.G + g) * s.max_splits + split) * grp) * (D + 2);
-    for (int dd = tid; dd < D; dd += blockDim.x) {
-        float o[8];
-#pragma unroll
-        for (int hr = 0; hr < 8; ++hr) o[hr] = 0.f;
-        for (int jj = 0; jj < nk; ++jj) {
-            const int j = j0 + jj;
-            const __nv_bfloat16 *vp;
-            if (j < n_sk) vp = kvp(s, layer, b, sink_off(s, SINK_V, g, j));
-            else if (j < n_sk + n_seg) vp = kvp(s, layer, b, bank_off(s, q.bank_par, BANK_V, g, j - n_sk));
-            else if (j < n_sk + n_seg + n_prev) vp = kvp(s, layer, b, ring_off(s, par ^ 1, KIND_V, g, j - n_sk - n_seg));
-            else vp = kvp(s, layer, b, ring_off(s, par, KIND_V, g, j - n_sk - n_seg - n_prev));
-            const float v = bf2f(vp[dd]);
-#pragma unroll
-            for (int hr = 0; hr < 8; ++hr)
-                if (hr < grp) o[hr] = fmaf(s_p[hr][jj], v, o[hr]);
-        }
-        for (int hr = 0; hr < grp; ++hr) part[hr * (D + 2) + dd] = o[hr];
-    }
-    if (tid < grp) {
-        part[tid * (D + 2) + D] = s_m[tid];
-        part[tid * (D + 2) + D + 1] = s_l[tid];
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const uint32_t ticket = atomicAdd(&s.att_cnt[b * m.G + g], 1u);
-        s_last = ticket == (uint32_t)(n_splits - 1);
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const float *p0 = s.att_part + (((size_t)b * m.G + g) * s.max_splits) * grp * (D + 2);
-    for (int idx = tid; idx < grp * D; idx += blockDim.x) {
-        const int hr = idx / D, dd = idx % D;
-        float M = -INFINITY;
-        for (int sp2 = 0; sp2 < n_splits; ++sp2) M = fmaxf(M, p0[((size_t)sp2 * grp + hr) * (D + 2) + D]);
-        float L = 0.f, O = 0.f;
-        for (int sp2 = 0; sp2 < n_splits; ++sp2) {
-            const float *pp = p0 + ((size_t)sp2 * grp + hr) * (D + 2);
-            const float w = expf(pp[D] - M);
-            L = fmaf(pp[D + 1], w, L);
-            O = fmaf(pp[dd], w, O);
-        }
-        s.attn[((size_t)b * H + g * grp + hr) * D + dd] = O / L;
-    }
-    if (tid == 0) s.att_cnt[b * m.G + g] = 0u;
-}
-
 // ------------------------------------------------------------------------------------------ chunk boundary
 // Segment-memory eviction for the chunk leaving the window (src/vault_v3_model.py:1865-1921,
 // runtime/vault3.c:1833-1915): spoof expansion, per-segment max score with the 1e-6 * segment-id tiebreak,
 // exact top-B by (score desc, position asc) over old bank + candidates, chronological compaction.  One CTA per
 // sequence; the selection counts, for every entry, the entries that beat it (deterministic, no sort).
 __global__ void __launch_bounds__(1024) k_bank_merge(const ModelDev *mp, const StateDev *sp) {
+    griddep_wait();
+    griddep_launch();
     const ModelDev &m = *mp;
     const StateDev &s = *sp;
     const int b = blockIdx.x;
@@ -515,6 +354,8 @@ __global__ void __launch_bounds__(1024) k_bank_merge(const ModelDev *mp, const S
 
 // gather the new bank rows (raw key and value) into the other bank buffer for every layer
 __global__ void k_bank_gather(const ModelDev *mp, const StateDev *sp) {
+    griddep_wait();
+    griddep_launch();
     const ModelDev &m = *mp;
     const StateDev &s = *sp;
     const int layer = blockIdx.y, b = blockIdx.z;
@@ -530,10 +371,10 @@ __global__ void k_bank_gather(const ModelDev *mp, const StateDev *sp) {
     for (int r = warp; r < rows; r += (gridDim.x * blockDim.x) >> 5) {
         const int kind = r & 1, g = (r >> 1) % m.G, j = (r >> 1) / m.G;
         const int src = s.mem_src[(size_t)b * s.seg_cap + j];
-        const __nv_bfloat16 *from;
+        const kv_t *from;
         if (src >= 0) from = kvp(s, layer, b, bank_off(s, op, kind == 0 ? BANK_KRAW : BANK_V, g, src));
         else from = kvp(s, layer, b, ring_off(s, p2, kind == 0 ? KIND_KRAW : KIND_V, g, -src - 1));
-        __nv_bfloat16 *to = kvp(s, layer, b, bank_off(s, np_, kind == 0 ? BANK_KRAW : BANK_V, g, j));
+        kv_t *to = kvp(s, layer, b, bank_off(s, np_, kind == 0 ? BANK_KRAW : BANK_V, g, j));
         for (int d0 = lane * 8; d0 < D; d0 += 256)
             *reinterpret_cast<uint4 *>(to + d0) = *reinterpret_cast<const uint4 *>(from + d0);
     }
@@ -541,6 +382,8 @@ __global__ void k_bank_gather(const ModelDev *mp, const StateDev *sp) {
 
 // bank keys -> positions -M..-1, sinks -> -(M+S)..-(M+1) (src/vault_v3_model.py:1842-1856)
 __global__ void k_prefix_rot(const ModelDev *mp, const StateDev *sp) {
+    griddep_wait();
+    griddep_launch();
     const ModelDev &m = *mp;
     const StateDev &s = *sp;
     const int layer = blockIdx.y, b = blockIdx.z;
@@ -551,8 +394,8 @@ __global__ void k_prefix_rot(const ModelDev *mp, const StateDev *sp) {
     const int n = (M + S) * m.G * hd;
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += gridDim.x * blockDim.x) {
         const int i = idx % hd, r = idx / hd, g = r % m.G, j = r / m.G;
-        const __nv_bfloat16 *src;
-        __nv_bfloat16 *dst;
+        const kv_t *src;
+        kv_t *dst;
         int64_t p;
         if (j < M) {
             src = kvp(s, layer, b, bank_off(s, q.bank_par, BANK_KRAW, g, j));
@@ -565,15 +408,17 @@ __global__ void k_prefix_rot(const ModelDev *mp, const StateDev *sp) {
             p = (int64_t)jj - (M + S);
         }
         const float *rr = rope_row(m, p);
-        const float a = bf2f(src[i]), bb = bf2f(src[i + hd]);
-        dst[i] = __float2bfloat16_rn(a * rr[i] - bb * rr[hd + i]);
-        dst[i + hd] = __float2bfloat16_rn(bb * rr[i] + a * rr[hd + i]);
+        const float a = kv2f(src[i]), bb = kv2f(src[i + hd]);
+        dst[i] = f2kv(a * rr[i] - bb * rr[hd + i]);
+        dst[i + hd] = f2kv(bb * rr[i] + a * rr[hd + i]);
     }
 }
 
 // ------------------------------------------------------------------------------------------ segment scorer
 // fc1 of SegmentScorer on LayerNorm(f) and LayerNorm(f - 0.65 ema) (src/vault_v3_model.py:879-883, :2294-2305)
 __global__ void k_scorer_fc1(const ModelDev *mp, const StateDev *sp) {
+    griddep_wait();
+    griddep_launch();
     const ModelDev &m = *mp;
     const StateDev &s = *sp;
     const int b = blockIdx.y;
@@ -661,6 +506,8 @@ __device__ bool contains(const uint8_t *buf, int n, const char *lit, int ln) {
 
 // GELU + fc2, habituated score, EMA update, spoof quarantine (src/vault_v3_model.py:2294-2308, :1795-1817)
 __global__ void k_scorer_out(const ModelDev *mp, const StateDev *sp) {
+    griddep_wait();
+    griddep_launch();
     const ModelDev &m = *mp;
     const StateDev &s = *sp;
     const int b = blockIdx.x;
@@ -726,58 +573,6 @@ __global__ void k_scorer_out(const ModelDev *mp, const StateDev *sp) {
     }
 }
 
-// ------------------------------------------------------------------------------------------ end of step
-__global__ void k_argmax(const ModelDev *mp, const StateDev *sp, int32_t *next) {
-    const ModelDev &m = *mp;
-    const StateDev &s = *sp;
-    const int b = blockIdx.x, tid = threadIdx.x;
-    const float *lg = s.logits + (size_t)b * m.vocab;
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = tid; i < m.vocab; i += blockDim.x) {
-        const float v = lg[i];
-        if (v > best) {
-            best = v;
-            bi = i;
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > best || (ov == best && oi < bi)) {
-            best = ov;
-            bi = oi;
-        }
-    }
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    if ((tid & 31) == 0) {
-        sv[tid >> 5] = best;
-        si[tid >> 5] = bi;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        for (int w = 1; w < (int)blockDim.x / 32; ++w)
-            if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
-                best = sv[w];
-                bi = si[w];
-            }
-        if (bi == 0x7fffffff) bi = 0;
-        if (next) next[b] = bi;
-        s.tok_in[b] = bi;
-        const StepCtl &sc = *s.step;
-        if (sc.out_tokens) sc.out_tokens[(int64_t)b * sc.out_ld + sc.out_idx] = bi;
-    }
-}
-
-__global__ void k_advance(const StateDev *sp) {
-    StepCtl &sc = *sp->step;
-    sc.pos += 1;
-    if (sc.ids) sc.ids_idx += 1;
-    if (sc.out_tokens) sc.out_idx += 1;
-}
-
 __global__ void k_state_init(const ModelDev *mp, const StateDev *sp, int auto_pin, int seg_budget) {
     const ModelDev &m = *mp;
     const StateDev &s = *sp;
@@ -814,75 +609,128 @@ __global__ void k_state_init(const ModelDev *mp, const StateDev *sp, int auto_pi
 }
 
 // ------------------------------------------------------------------------------------------ host launchers
-template <class Epi>
-static cudaError_t run_gemv(const v3g_model *m, GemvArgs a, const Epi &epi, int Btot, cudaStream_t st) {
+// one GEMV launch description: kernel arguments plus the weight format of every segment
+struct GemvCall {
+    GemvArgs a;
+    int fmts[3];
+};
+
+template <int FA, int FB, class Epi>
+static cudaError_t launch_gemv_t(const v3g_model *m, GemvCall c, const Epi &epi, int Btot, cudaStream_t st, bool pdl) {
     for (int b0 = 0; b0 < Btot; b0 += GEMV_MB) {
-        a.b0 = b0;
-        a.B = Btot - b0 < GEMV_MB ? Btot - b0 : GEMV_MB;
+        c.a.b0 = b0;
+        c.a.B = Btot - b0 < GEMV_MB ? Btot - b0 : GEMV_MB;
         int grid;
         size_t smem;
-        gemv_plan(a, m->n_sm, grid, smem);
+        gemv_plan(c.a, c.fmts, m->n_sm, grid, smem);
         if (smem > GEMV_MAX_SMEM) return cudaErrorInvalidValue;
-        gemv_kernel<Epi><<<grid, GEMV_THREADS, smem, st>>>(a, epi);
+        cudaError_t e = launch_k(pdl, gemv_kernel<FA, FB, Epi>, dim3(grid), dim3(GEMV_THREADS), smem, st, c.a, epi);
+        if (e != cudaSuccess) return e;
     }
-    return cudaGetLastError();
+    return cudaSuccess;
 }
 
-static GemvArgs gemv_args(const MatW *const *mats, int n, const float *x, int x_ld, int K, int prologue,
-                          const float *norm_w, float eps) {
-    GemvArgs a{};
-    a.n_seg = n;
-    for (int i = 0; i < n; ++i) {
-        a.seg[i].tiles = mats[i]->tiles;
-        a.seg[i].fmt = mats[i]->fmt;
-        a.seg[i].n_rtiles = mats[i]->n_rtiles;
-        a.seg[i].n_ktiles = mats[i]->n_ktiles;
+// Pick the kernel instantiation for the segments' formats: one format, or Q4_0 queries with Q8_0 keys/values
+// (the hybrid file layout, tools/vlt3.py:312-330); any other mix runs one launch per segment.
+template <class Epi>
+static cudaError_t run_gemv(const v3g_model *m, const GemvCall &c, const Epi &epi, int Btot, cudaStream_t st,
+                           bool pdl = false) {
+    bool same = true, hybrid = c.fmts[0] == FMT_Q4;
+    for (int i = 1; i < c.a.n_seg; ++i) {
+        same = same && c.fmts[i] == c.fmts[0];
+        hybrid = hybrid && c.fmts[i] == FMT_Q8;
     }
-    a.K = K;
-    a.x = x;
-    a.x_ld = x_ld;
-    a.prologue = prologue;
-    a.norm_w = norm_w;
-    a.eps = eps;
-    a.xbf16 = x_is_bf16(mats[0]->fmt) ? 1 : 0;
-    return a;
+    if (same) {
+        switch (c.fmts[0]) {
+            case FMT_Q8: return launch_gemv_t<FMT_Q8, FMT_Q8>(m, c, epi, Btot, st, pdl);
+            case FMT_Q4: return launch_gemv_t<FMT_Q4, FMT_Q4>(m, c, epi, Btot, st, pdl);
+            case FMT_BF16: return launch_gemv_t<FMT_BF16, FMT_BF16>(m, c, epi, Btot, st, pdl);
+            case FMT_F16: return launch_gemv_t<FMT_F16, FMT_F16>(m, c, epi, Btot, st, pdl);
+            default: return launch_gemv_t<FMT_F32, FMT_F32>(m, c, epi, Btot, st, pdl);
+        }
+    }
+    if (hybrid) return launch_gemv_t<FMT_Q4, FMT_Q8>(m, c, epi, Btot, st, pdl);
+    for (int i = 0; i < c.a.n_seg; ++i) {
+        GemvCall one = c;
+        one.a.seg[0] = c.a.seg[i];
+        one.a.n_seg = 1;
+        one.a.seg_base = i;
+        one.fmts[0] = c.fmts[i];
+        cudaError_t e = run_gemv(m, one, epi, Btot, st, pdl);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+static GemvCall gemv_args(const MatW *const *mats, int n, const float *x, int x_ld, int K, int prologue,
+                          const float *norm_w, float eps) {
+    GemvCall c{};
+    c.a.n_seg = n;
+    for (int i = 0; i < n; ++i) {
+        c.a.seg[i].tiles = mats[i]->tiles;
+        c.a.seg[i].n_rtiles = mats[i]->n_rtiles;
+        c.a.seg[i].n_ktiles = mats[i]->n_ktiles;
+        c.a.seg[i].wscale = mats[i]->wscale;
+        c.fmts[i] = mats[i]->fmt;
+    }
+    c.a.K = K;
+    c.a.x = x;
+    c.a.x_ld = x_ld;
+    c.a.prologue = prologue;
+    c.a.norm_w = norm_w;
+    c.a.eps = eps;
+    return c;
 }
 
 cudaError_t launch_gemv_store(const v3g_model *m, const MatW &w, const float *x, int B, float *y, cudaStream_t st) {
     const MatW *mats[1] = {&w};
-    GemvArgs a = gemv_args(mats, 1, x, w.cols, w.cols, PRO_PLAIN, nullptr, 0.f);
+    GemvCall c = gemv_args(mats, 1, x, w.cols, w.cols, PRO_PLAIN, nullptr, 0.f);
     EpiStore epi{y, w.rows, w.rows};
-    return run_gemv(m, a, epi, B, st);
+    return run_gemv(m, c, epi, B, st);
 }
 
 cudaError_t launch_gemv_mapped(const v3g_model *m, const MatW &w, const float *x, int B, float *y, cudaStream_t st) {
     const MatW *mats[1] = {&w};
-    GemvArgs a = gemv_args(mats, 1, x, w.cols, w.cols, PRO_PLAIN, nullptr, 0.f);
+    GemvCall c = gemv_args(mats, 1, x, w.cols, w.cols, PRO_PLAIN, nullptr, 0.f);
     const int src_rows = w.rowmap == ROWS_GATE_UP ? w.rows / 2 : w.rows;
     EpiStoreMapped epi{y, w.rows, w.rowmap, m->host.D, src_rows};
-    return run_gemv(m, a, epi, B, st);
+    return run_gemv(m, c, epi, B, st);
 }
 
 // one-time kernel attributes (large dynamic shared memory); must not run during stream capture
-cudaError_t init_kernel_attrs() {
-    cudaError_t e = cudaSuccess;
+template <class Epi>
+static void set_gemv_attrs(cudaError_t &e, int optin) {
     auto set = [&](const void *f) {
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+        cudaFuncAttributes fa;
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, f);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
     };
-    set((const void *)gemv_kernel<EpiQKV>);
-    set((const void *)gemv_kernel<EpiResid>);
-    set((const void *)gemv_kernel<EpiGateUp>);
-    set((const void *)gemv_kernel<EpiStore>);
-    set((const void *)gemv_kernel<EpiStoreMapped>);
-    set((const void *)k_bank_merge);
+    set((const void *)gemv_kernel<FMT_Q8, FMT_Q8, Epi>);
+    set((const void *)gemv_kernel<FMT_Q4, FMT_Q4, Epi>);
+    set((const void *)gemv_kernel<FMT_Q4, FMT_Q8, Epi>);
+    set((const void *)gemv_kernel<FMT_BF16, FMT_BF16, Epi>);
+    set((const void *)gemv_kernel<FMT_F16, FMT_F16, Epi>);
+    set((const void *)gemv_kernel<FMT_F32, FMT_F32, Epi>);
+}
+
+cudaError_t init_kernel_attrs() {
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    set_gemv_attrs<EpiQKV>(e, optin);
+    set_gemv_attrs<EpiResid>(e, optin);
+    set_gemv_attrs<EpiGateUp>(e, optin);
+    set_gemv_attrs<EpiStore>(e, optin);
+    set_gemv_attrs<EpiStoreMapped>(e, optin);
+    cudaFuncAttributes fa;
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_bank_merge);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute((const void *)k_bank_merge, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 optin - (int)fa.sharedSizeBytes);
     return e;
 }
 
-template <int D>
-static void launch_attention(const v3g_model *m, v3g_state *s, int layer, cudaStream_t st) {
-    dim3 grid(s->host.max_splits, m->host.G, s->B);
-    k_attention<D><<<grid, ATT_THREADS, 0, st>>>(m->dev, s->dev, layer, (float)(1.0 / sqrt((double)D)));
-}
 
 cudaError_t launch_prefix_refresh(const v3g_model *m, v3g_state *s, cudaStream_t st) {
     k_prefix_rot<<<dim3(64, m->host.n_layers, s->B), 256, 0, st>>>(m->dev, s->dev);
@@ -896,75 +744,241 @@ cudaError_t launch_state_reset(const v3g_model *m, v3g_state *s, cudaStream_t st
     return cudaGetLastError();
 }
 
+}  // namespace v3g
+
+#include "v3g_mega.cuh"
+
+namespace v3g {
+
+// Phase table of the persistent decode kernel for this state; leaves use_mega = 0 when the batch does not fit one
+// pass (> 8 rows), a phase would mix 16-bit activation types, or the shared-memory plan leaves no ring.
+cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
+    const ModelDev &md = m->host;
+    const StateDev &sd = s->host;
+    s->use_mega = 0;
+    if (s->B > GEMV_MB || !sd.mk_part || !sd.mk_cnt) return cudaSuccess;
+    const bool any_seg = md.seg_n_feat > 0 && s->seg_cap > 0;
+    std::vector<MkPhase> ph;
+    size_t xr = 0;
+    int max_rt = 0;
+    bool ok = true;
+    auto add_gemv = [&](const MatW *const *mats, int n, const float *x, int x_ld, int K, int prologue,
+                        const float *norm_w, int epi, int layer, float *out, int out_ld, int out_rows) -> MkPhase & {
+        GemvCall c = gemv_args(mats, n, x, x_ld, K, prologue, norm_w, md.rms_eps);
+        c.a.B = s->B;
+        c.a.b0 = 0;
+        int grid;
+        size_t smem;
+        gemv_plan(c.a, c.fmts, m->n_sm, grid, smem);
+        MkPhase p{};
+        p.a = c.a;
+        bool bs = false;
+        int64_t tb = 0;
+        int rb = 0;
+        for (int i = 0; i < n; ++i) {
+            p.fmts[i] = c.fmts[i];
+            bs = bs || fmt_int(c.fmts[i]);
+            p.tbase[i] = tb;
+            p.rbase[i] = rb;
+            tb += (int64_t)c.a.seg[i].n_rtiles * c.a.seg[i].n_ktiles;
+            rb += c.a.seg[i].n_rtiles;
+        }
+        p.tbase[n] = tb;
+        max_rt = rb > max_rt ? rb : max_rt;
+        const size_t need = (size_t)(144 + (bs ? c.a.nblk * GEMV_MB : 0)) * 4 + (size_t)s->B * c.a.kpx * 2;
+        xr = need > xr ? need : xr;
+        p.kind = MK_GEMV;
+        p.epi = epi;
+        p.layer = layer;
+        p.out = out;
+        p.out_ld = out_ld;
+        p.out_rows = out_rows;
+        ph.push_back(p);
+        return ph.back();
+    };
+    for (int l = 0; l < md.n_layers; ++l) {
+        const LayerW &L = md.layers[l];
+        const MatW *qkv[3] = {&L.q, &L.k, &L.v};
+        MkPhase &q = add_gemv(qkv, 3, sd.x, md.d, md.d, PRO_RMSNORM, L.ln1, MK_EPI_QKV, l, nullptr, 0, 0);
+        q.bq = L.bq;
+        q.bk = L.bk;
+        q.bv = L.bv;
+        for (int fi = 0; fi < md.seg_n_feat && any_seg; ++fi)
+            if (md.seg_layers[fi] == l) {   // scorer features: residual stream entering this layer
+                q.a.feat = sd.feat + (size_t)fi * md.d;
+                q.a.feat_ld = sd.feat_dim;
+            }
+        MkPhase at{};
+        at.kind = MK_ATTN;
+        at.layer = l;
+        ph.push_back(at);
+        const MatW *o[1] = {&L.o};
+        add_gemv(o, 1, sd.attn, md.H * md.D, md.H * md.D, PRO_PLAIN, nullptr, MK_EPI_RESID, l, sd.x, md.d, md.d);
+        const MatW *gu[1] = {&L.gu};
+        add_gemv(gu, 1, sd.x, md.d, md.d, PRO_RMSNORM, L.ln2, MK_EPI_GATEUP, l, sd.hbuf, md.F, md.F);
+        const MatW *dn[1] = {&L.down};
+        add_gemv(dn, 1, sd.hbuf, md.F, md.F, PRO_PLAIN, nullptr, MK_EPI_RESID, l, sd.x, md.d, md.d);
+    }
+    const MatW *lm[1] = {&md.embed};
+    add_gemv(lm, 1, sd.x, md.d, md.d, PRO_RMSNORM, md.norm, MK_EPI_STORE, -1, sd.logits, md.vocab, md.vocab);
+    if (!ok || max_rt > s->mk_cnt_cap) return cudaSuccess;
+    const void *fn = nullptr;
+    size_t att = 0;
+    switch (md.D) {
+        case 16: att = sizeof(AttnSmem<16>); fn = (const void *)k_decode<16>; break;
+        case 32: att = sizeof(AttnSmem<32>); fn = (const void *)k_decode<32>; break;
+        case 64: att = sizeof(AttnSmem<64>); fn = (const void *)k_decode<64>; break;
+        case 128: att = sizeof(AttnSmem<128>); fn = (const void *)k_decode<128>; break;
+        default: return cudaSuccess;
+    }
+    xr = (std::max(xr, att) + 127) / 128 * 128;
+    int optin = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa{};
+    e = cudaFuncGetAttributes(&fa, fn);
+    if (e != cudaSuccess) return e;
+    const long avail = (long)optin - (long)fa.sharedSizeBytes - (long)xr;
+    const long per_slot = (long)MK_WARPS * (MK_SLOT_BYTES + 8);
+    int slots = avail > 0 ? (int)(avail / per_slot) : 0;
+    slots = slots > MK_MAX_SLOTS ? MK_MAX_SLOTS : slots;
+    if (slots < 2) return cudaSuccess;
+    const size_t smem = xr + (size_t)slots * per_slot;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, GEMV_THREADS, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaSuccess;
+    e = cudaMalloc(&s->mk_phases, ph.size() * sizeof(MkPhase));
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpy(s->mk_phases, ph.data(), ph.size() * sizeof(MkPhase), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return e;
+    s->mk_n = (int)ph.size();
+    s->mk_smem = smem;
+    s->mk_slots = slots;
+    s->mk_xr = (int)xr;
+    s->mk_grid = m->n_sm;
+    s->use_mega = 1;
+    return cudaSuccess;
+}
+
+// cooperative launch (every CTA co-resident, which the grid barriers need); without the lm head the last phase is
+// dropped
+cudaError_t launch_mega(const v3g_model *m, v3g_state *s, bool want_lm, cudaStream_t st) {
+    const int n = want_lm ? s->mk_n : s->mk_n - 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(s->mk_grid);
+    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.dynamicSmemBytes = s->mk_smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const ModelDev *mdv = m->dev;
+    const StateDev *sdv = s->dev;
+    const MkPhase *phases = static_cast<const MkPhase *>(s->mk_phases);
+    const float scale = (float)(1.0 / sqrt((double)m->host.D));
+    MkCfg mc;
+    mc.slots = s->mk_slots;
+    mc.xr_bytes = s->mk_xr;
+    mc.part = s->host.mk_part;
+    mc.cnt = s->host.mk_cnt;
+    switch (m->host.D) {
+        case 16: return cudaLaunchKernelEx(&cfg, k_decode<16>, mdv, sdv, phases, n, scale, mc);
+        case 32: return cudaLaunchKernelEx(&cfg, k_decode<32>, mdv, sdv, phases, n, scale, mc);
+        case 64: return cudaLaunchKernelEx(&cfg, k_decode<64>, mdv, sdv, phases, n, scale, mc);
+        default: return cudaLaunchKernelEx(&cfg, k_decode<128>, mdv, sdv, phases, n, scale, mc);
+    }
+}
+
+// Kernel sequence of one decode step.  Every launch after the first carries programmatic stream serialization:
+// the next kernel's CTAs start streaming their weights while the previous kernel drains (griddep_wait in each
+// kernel orders all state accesses).
 cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool want_lm, cudaStream_t st) {
     const ModelDev &md = m->host;
     const StateDev &sd = s->host;
+    const ModelDev *mdv = m->dev;
+    const StateDev *sdv = s->dev;
     const int B = s->B;
     const bool any_seg = md.seg_n_feat > 0 && s->seg_budget > 0;
+    const bool pdl = s->use_pdl != 0;
     cudaError_t e;
+#define V3G_TRY(x)                          \
+    do {                                    \
+        if ((e = (x)) != cudaSuccess) return e; \
+    } while (0)
     if (boundary) {
         // the boundary kernels check pos >= 2W on the device, so one captured graph serves every rollover
-        k_pin<<<B, 32, 0, st>>>(m->dev, s->dev);
+        V3G_TRY(launch_k(false, k_pin, dim3(B), dim3(32), 0, st, mdv, sdv));
         if (any_seg) {
             const size_t smem = (size_t)(2 * md.W + 3 * (sd.seg_cap + md.W)) * 4;
-            if (smem > 227 * 1024) return cudaErrorInvalidValue;
-            k_bank_merge<<<B, 1024, smem, st>>>(m->dev, s->dev);
-            k_bank_gather<<<dim3(16, md.n_layers, B), 256, 0, st>>>(m->dev, s->dev);
+            if (smem > (size_t)GEMV_MAX_SMEM) return cudaErrorInvalidValue;
+            V3G_TRY(launch_k(pdl, k_bank_merge, dim3(B), dim3(1024), smem, st, mdv, sdv));
+            V3G_TRY(launch_k(pdl, k_bank_gather, dim3(16, md.n_layers, B), dim3(256), 0, st, mdv, sdv));
         }
-        k_prefix_rot<<<dim3(64, md.n_layers, B), 256, 0, st>>>(m->dev, s->dev);
-        k_begin<false><<<B, 256, 0, st>>>(m->dev, s->dev);
+        V3G_TRY(launch_k(pdl, k_prefix_rot, dim3(64, md.n_layers, B), dim3(256), 0, st, mdv, sdv));
+        V3G_TRY(launch_k(pdl, k_begin<false>, dim3(B), dim3(256), 0, st, mdv, sdv));
     } else {
-        k_begin<true><<<B, 256, 0, st>>>(m->dev, s->dev);
+        V3G_TRY(launch_k(false, k_begin<true>, dim3(B), dim3(256), 0, st, mdv, sdv));
+    }
+    if (s->use_mega) {   // all layers + lm head in one persistent launch
+        V3G_TRY(launch_mega(m, s, want_lm, st));
+        if (any_seg) {
+            V3G_TRY(launch_k(pdl, k_scorer_fc1, dim3((md.seg_hidden + 7) / 8, B), dim3(256), 0, st, mdv, sdv));
+            V3G_TRY(launch_k(pdl, k_scorer_out, dim3(B), dim3(256), 0, st, mdv, sdv));
+        }
+        V3G_TRY(launch_argmax_finish(m, s, want_lm, pdl, st));
+        return cudaSuccess;
     }
     for (int l = 0; l < md.n_layers; ++l) {
         const LayerW &L = md.layers[l];
-        for (int fi = 0; fi < md.seg_n_feat && any_seg; ++fi)
-            if (md.seg_layers[fi] == l) k_copy_feat<<<B, 256, 0, st>>>(s->dev, md.d, fi);
         {
             const MatW *mats[3] = {&L.q, &L.k, &L.v};
-            GemvArgs a = gemv_args(mats, 3, sd.x, md.d, md.d, PRO_RMSNORM, L.ln1, md.rms_eps);
-            EpiQKV epi{m->dev, s->dev, l, L.bq, L.bk, L.bv};
-            if ((e = run_gemv(m, a, epi, B, st)) != cudaSuccess) return e;
+            GemvCall a = gemv_args(mats, 3, sd.x, md.d, md.d, PRO_RMSNORM, L.ln1, md.rms_eps);
+            for (int fi = 0; fi < md.seg_n_feat && any_seg; ++fi)
+                if (md.seg_layers[fi] == l) {   // scorer features: residual stream entering this layer
+                    a.a.feat = sd.feat + (size_t)fi * md.d;
+                    a.a.feat_ld = sd.feat_dim;
+                }
+            EpiQKV epi{mdv, sdv, l, L.bq, L.bk, L.bv};
+            V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
         }
-        switch (md.D) {
-            case 16: launch_attention<16>(m, s, l, st); break;
-            case 32: launch_attention<32>(m, s, l, st); break;
-            case 64: launch_attention<64>(m, s, l, st); break;
-            case 128: launch_attention<128>(m, s, l, st); break;
-            default: launch_attention<256>(m, s, l, st); break;
-        }
+        V3G_TRY(launch_attention(m, s, l, pdl, st));
         {
             const MatW *mats[1] = {&L.o};
-            GemvArgs a = gemv_args(mats, 1, sd.attn, md.H * md.D, md.H * md.D, PRO_PLAIN, nullptr, 0.f);
+            GemvCall a = gemv_args(mats, 1, sd.attn, md.H * md.D, md.H * md.D, PRO_PLAIN, nullptr, 0.f);
             EpiResid epi{sd.x, md.d, md.d};
-            if ((e = run_gemv(m, a, epi, B, st)) != cudaSuccess) return e;
+            V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
         }
         {
             const MatW *mats[1] = {&L.gu};
-            GemvArgs a = gemv_args(mats, 1, sd.x, md.d, md.d, PRO_RMSNORM, L.ln2, md.rms_eps);
+            GemvCall a = gemv_args(mats, 1, sd.x, md.d, md.d, PRO_RMSNORM, L.ln2, md.rms_eps);
             EpiGateUp epi{sd.hbuf, md.F};
-            if ((e = run_gemv(m, a, epi, B, st)) != cudaSuccess) return e;
+            V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
         }
         {
             const MatW *mats[1] = {&L.down};
-            GemvArgs a = gemv_args(mats, 1, sd.hbuf, md.F, md.F, PRO_PLAIN, nullptr, 0.f);
+            GemvCall a = gemv_args(mats, 1, sd.hbuf, md.F, md.F, PRO_PLAIN, nullptr, 0.f);
             EpiResid epi{sd.x, md.d, md.d};
-            if ((e = run_gemv(m, a, epi, B, st)) != cudaSuccess) return e;
+            V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
         }
     }
     if (any_seg) {
-        k_scorer_fc1<<<dim3((md.seg_hidden + 7) / 8, B), 256, 0, st>>>(m->dev, s->dev);
-        k_scorer_out<<<B, 256, 0, st>>>(m->dev, s->dev);
+        V3G_TRY(launch_k(pdl, k_scorer_fc1, dim3((md.seg_hidden + 7) / 8, B), dim3(256), 0, st, mdv, sdv));
+        V3G_TRY(launch_k(pdl, k_scorer_out, dim3(B), dim3(256), 0, st, mdv, sdv));
     }
     if (want_lm) {
         const MatW *mats[1] = {&md.embed};
-        GemvArgs a = gemv_args(mats, 1, sd.x, md.d, md.d, PRO_RMSNORM, md.norm, md.rms_eps);
+        GemvCall a = gemv_args(mats, 1, sd.x, md.d, md.d, PRO_RMSNORM, md.norm, md.rms_eps);
         EpiStore epi{sd.logits, md.vocab, md.vocab};
-        if ((e = run_gemv(m, a, epi, B, st)) != cudaSuccess) return e;
-        k_argmax<<<B, 1024, 0, st>>>(m->dev, s->dev, nullptr);
+        V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
     }
-    k_advance<<<1, 1, 0, st>>>(s->dev);
-    return cudaGetLastError();
+    V3G_TRY(launch_argmax_finish(m, s, want_lm, pdl, st));
+#undef V3G_TRY
+    return cudaSuccess;
 }
 
 }  // namespace v3g

@@ -52,7 +52,8 @@ class VAULTv3State:
     """Fixed-size streaming state held in a device arena (the reference's VAULTv3State / v3_state)."""
 
     def __init__(self, model: "VAULTv3ForCausalLM", batch: int = 1, seg_budget: Optional[int] = None,
-                 per_sequence_memory: bool = False, auto_pin: bool = True, graphs: bool = True):
+                 per_sequence_memory: bool = False, auto_pin: bool = True, graphs: bool = True,
+                 persistent: bool = True):
         self.model = model
         self.batch = int(batch)
         cfg = model.cfg
@@ -66,7 +67,8 @@ class VAULTv3State:
             raise ValueError("invalid state arguments")
         self.arena = torch.empty(int(size), dtype=torch.uint8, device=model.device)
         flags = (_lib.V3G_STATE_PER_SEQ_MEMORY if per_sequence_memory else 0) | \
-                (0 if auto_pin else _lib.V3G_STATE_NO_AUTOPIN) | (0 if graphs else _lib.V3G_STATE_NO_GRAPHS)
+                (0 if auto_pin else _lib.V3G_STATE_NO_AUTOPIN) | (0 if graphs else _lib.V3G_STATE_NO_GRAPHS) | \
+                (0 if persistent else _lib.V3G_STATE_NO_PERSISTENT)
         h = C.c_void_p()
         with torch.cuda.device(model.device):
             _lib.check(L.v3g_state_init(C.byref(h), model._h, C.c_void_p(self.arena.data_ptr()), int(size),
