@@ -144,8 +144,6 @@ struct StateDev {
     unsigned long long *amax;    // [B]
     float *sc_z;                 // [B][2][seg_hidden]
     unsigned int *bar;           // grid-barrier counter of the persistent decode kernel (zeroed every step)
-    float *mk_part;              // persistent kernel: split row-tile partials [8 * n_sm warps][2][32][4]
-    uint32_t *mk_cnt;            // persistent kernel: per-row-tile arrival tickets
 };
 
 __device__ __forceinline__ uint64_t ring_off(const StateDev &s, int par, int kind, int g, int t) {
@@ -181,6 +179,10 @@ __device__ __forceinline__ uint2 ldg_stream8(const void *p) {
     asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
     return r;
 }
+
+// barrier over the first n threads of the CTA (named barrier 1, n a multiple of 32): kernels whose every thread
+// takes part pass blockDim.x, the persistent decode kernel passes its consumer warps only
+__device__ __forceinline__ void sync_threads(int n) { asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -530,12 +530,12 @@ struct Layout {
     uint64_t kv_bytes;
     uint64_t off_seq, off_step, off_tok_in, off_tok_ring, off_sc_ring, off_seg_ring, off_mem_pos, off_mem_score,
         off_mem_tok, off_mem_seg, off_mem_src, off_ema, off_feat, off_x, off_attn, off_h, off_qc, off_qf, off_part,
-        off_cnt, off_logits, off_amax, off_scz, off_bar, off_mk_part, off_mk_cnt;
+        off_cnt, off_logits, off_amax, off_scz, off_bar;
     uint64_t total;
-    int max_splits, seg_cap, feat_dim, mk_cnt_cap;
+    int max_splits, seg_cap, feat_dim;
 };
 
-Layout make_layout(const ModelDev &md, int B, int seg_cap, int n_sm) {
+Layout make_layout(const ModelDev &md, int B, int seg_cap) {
     Layout L{};
     auto al = [](uint64_t v) { return (v + 255) & ~255ull; };
     const uint64_t row = (uint64_t)md.D * 2, G = md.G;
@@ -581,11 +581,6 @@ Layout make_layout(const ModelDev &md, int B, int seg_cap, int n_sm) {
     L.off_amax = take((uint64_t)B * 8);
     L.off_scz = take((uint64_t)B * 2 * std::max(1, md.seg_hidden) * 4);
     L.off_bar = take(64);
-    if (B <= GEMV_MB) {   // persistent decode kernel scratch (one pass of <= 8 rows)
-        L.off_mk_part = take((uint64_t)8 * n_sm * 2 * 32 * 4 * 4);
-        L.mk_cnt_cap = (md.vocab + 2 * md.F + md.H * md.D + 2 * md.G * md.D + md.d) / 16 + 16;
-        L.off_mk_cnt = take((uint64_t)L.mk_cnt_cap * 4);
-    }
     L.total = cur;
     return L;
 }
@@ -595,7 +590,7 @@ Layout make_layout(const ModelDev &md, int B, int seg_cap, int n_sm) {
 extern "C" size_t v3g_state_arena_size(const v3g_model *m, uint32_t batch, uint32_t max_seg_budget) {
     if (!m || batch == 0 || batch > 4096 || max_seg_budget > MAX_SEG_BUDGET) return 0;
     const int cap = m->host.seg_n_feat > 0 ? (int)max_seg_budget : 0;
-    return (size_t)make_layout(m->host, (int)batch, cap, m->n_sm).total;
+    return (size_t)make_layout(m->host, (int)batch, cap).total;
 }
 
 extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_arena, size_t arena_size, uint32_t batch,
@@ -607,7 +602,7 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
     if (max_seg_budget > MAX_SEG_BUDGET) return fail(V3G_E_LIMIT, "segment budget above 16384");
     const ModelDev &md = m->host;
     const int cap = md.seg_n_feat > 0 ? (int)max_seg_budget : 0;
-    const Layout L = make_layout(md, (int)batch, cap, m->n_sm);
+    const Layout L = make_layout(md, (int)batch, cap);
     if (arena_size < L.total) return fail(V3G_E_ARENA, "arena too small");
     v3g_state *s = new v3g_state();
     s->m = m;
@@ -658,9 +653,6 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
     sd.amax = reinterpret_cast<unsigned long long *>(A + L.off_amax);
     sd.sc_z = reinterpret_cast<float *>(A + L.off_scz);
     sd.bar = reinterpret_cast<unsigned int *>(A + L.off_bar);
-    sd.mk_part = L.mk_cnt_cap ? reinterpret_cast<float *>(A + L.off_mk_part) : nullptr;
-    sd.mk_cnt = L.mk_cnt_cap ? reinterpret_cast<uint32_t *>(A + L.off_mk_cnt) : nullptr;
-    s->mk_cnt_cap = L.mk_cnt_cap;
     if (cudaSetDevice(m->device) != cudaSuccess || cudaMalloc(&s->dev, sizeof(StateDev)) != cudaSuccess ||
         cudaMemcpy(s->dev, &sd, sizeof(StateDev), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaStreamCreateWithFlags(&s->cap_stream, cudaStreamNonBlocking) != cudaSuccess) {
@@ -703,6 +695,7 @@ extern "C" void v3g_state_free(v3g_state *s) {
     if (s->cap_stream) cudaStreamDestroy(s->cap_stream);
     if (s->dev) cudaFree(s->dev);
     if (s->mk_phases) cudaFree(s->mk_phases);
+    if (s->mk_lite) cudaFree(s->mk_lite);
     delete s;
 }
 

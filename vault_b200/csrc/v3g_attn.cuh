@@ -69,14 +69,14 @@ struct AttnSmem {
 // partials in split order into s.attn.  Returns false when the split is empty.
 template <int D>
 __device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float scale, int split, int g, int b,
-                          int64_t pos, AttnSmem<D> &sm) {
+                          int64_t pos, AttnSmem<D> &sm, int nt) {
     constexpr int KP = D + 8, CH = D / 8;
     const int H = m.H, grp = H / m.G;
     const KeySpan ks = key_span(m, s, b, pos);
     const int n_splits = (ks.total + ATT_KPC - 1) / ATT_KPC;
     if (split >= n_splits) return false;
     const int j0 = split * ATT_KPC, nk = min(ATT_KPC, ks.total - j0);
-    const int tid = threadIdx.x, nt = blockDim.x;
+    const int tid = threadIdx.x;
     for (int c = tid; c < nk * CH; c += nt) {
         const int j = c / CH, part = c - j * CH;
         bool far;
@@ -94,7 +94,7 @@ __device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float
         sm.q[0][hr][dd] = pos >= m.W ? __ldcg(&s.q_far[qo]) : 0.f;
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
+    sync_threads(nt);
     // scores: threads (2j, 2j+1) take the two halves of key j
     for (int base = 0; base < 2 * ATT_KPC; base += nt) {
         const int j = (base + tid) >> 1, half = tid & 1;
@@ -139,7 +139,7 @@ __device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float
             if (hr < grp && half == 0 && j < nk) sm.p[hr][j] = tot * scale;
         }
     }
-    __syncthreads();
+    sync_threads(nt);
     const int warp = tid >> 5, lane = tid & 31;
     for (int hr = warp; hr < grp; hr += nt / 32) {
         float mx = -INFINITY;
@@ -157,7 +157,18 @@ __device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float
             sm.l[hr] = l;
         }
     }
-    __syncthreads();
+    sync_threads(nt);
+    if (n_splits == 1) {   // the whole span in one item: normalise and write the head outputs directly
+        for (int idx = tid; idx < grp * D; idx += nt) {
+            const int hr = idx / D, dd = idx - hr * D;
+            float o = 0.f;
+#pragma unroll 8
+            for (int j = 0; j < nk; ++j) o = fmaf(sm.p[hr][j], kv2f(sm.v[j * D + dd]), o);
+            s.attn[((size_t)b * H + g * grp + hr) * D + dd] = o / sm.l[hr];
+        }
+        sync_threads(nt);
+        return true;
+    }
     float *part = s.att_part + ((((size_t)b * m.G + g) * s.max_splits + split) * grp) * (D + 2);
     for (int idx = tid; idx < grp * D; idx += nt) {
         const int hr = idx / D, dd = idx - hr * D;
@@ -171,9 +182,9 @@ __device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float
         part[tid * (D + 2) + D + 1] = sm.l[tid];
     }
     __threadfence();
-    __syncthreads();
+    sync_threads(nt);
     if (tid == 0) sm.last = atomicAdd(&s.att_cnt[b * m.G + g], 1u) == (uint32_t)(n_splits - 1);
-    __syncthreads();
+    sync_threads(nt);
     if (sm.last) {
         __threadfence();
         const float *p0 = s.att_part + (((size_t)b * m.G + g) * s.max_splits) * grp * (D + 2);
@@ -192,7 +203,7 @@ __device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float
         }
         if (tid == 0) s.att_cnt[b * m.G + g] = 0u;
     }
-    __syncthreads();
+    sync_threads(nt);
     return true;
 }
 

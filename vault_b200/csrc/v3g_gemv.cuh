@@ -201,11 +201,13 @@ __device__ __forceinline__ void load16(const float *p, bool vec, int n, float (&
 // Convert the pass's activation rows once per CTA into shared memory: RMSNorm (optional), fp16 with a per-row
 // power-of-two scale (largest |x| scaled into (2^13, 2^14]); s_scale[b] receives the scale to undo and, with
 // BSUM, bsum[blk * 8 + b] the fp32 sum of converted 32-wide block blk of row b.  Work items are half blocks (16
-// values; the two halves of a block sit in adjacent lanes): one stats pass and one convert pass, each with all of
-// a thread's loads in flight at once.
-template <bool BSUM>
-__device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_scale, float *s_red, float *bsum) {
-    const int tid = threadIdx.x, nt = blockDim.x, nw = nt / 32;
+// values; the two halves of a block sit in adjacent lanes): one stats pass and one convert pass.  A thread keeps
+// its first items in registers between the passes -- CACHE of them without RMSNorm, one item and its norm weights
+// (in the last cache slot) with it -- so such rows cost one round trip to L2.
+template <bool BSUM, int CACHE = 0>
+__device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_scale, float *s_red, float *bsum,
+                                     int nt) {
+    const int tid = threadIdx.x, nw = nt / 32;
     const bool norm = a.prologue == PRO_RMSNORM;
     const bool vec = (a.K & 31) == 0 && (a.x_ld & 3) == 0;
     const int nb = (a.K + 31) >> 5, nh = 2 * nb, items = a.B * nh;
@@ -215,11 +217,11 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         ss[b] = 0.f;
         mx[b] = 0.f;
     }
-    for (int it = tid; it < items; it += nt) {
-        const int b = it / nh, h = it - b * nh, n = a.K - h * 16;
-        float v[16], w[16];
-        load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, v);
-        if (norm) load16<false>(a.norm_w + h * 16, vec, n, w);
+    constexpr int NC = CACHE > 1 ? CACHE : 2;
+    float vc[NC][16];
+    float (&wc)[16] = vc[NC - 1];               // norm weights of the first item (RMSNorm)
+    const int ncache = CACHE == 0 ? 0 : (norm ? 1 : CACHE);
+    auto stats = [&](int b, const float (&v)[16], const float (&w)[16]) {
         float s2 = 0.f, m = 0.f;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -232,6 +234,27 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
                 ss[bb] += s2;
                 mx[bb] = fmaxf(mx[bb], m);
             }
+    };
+#pragma unroll
+    for (int k = 0; k < CACHE; ++k) {   // cached items: loads of all of them in flight together
+        const int it = tid + k * nt;
+        if (k < ncache && it < items) {
+            const int b = it / nh, h = it - b * nh, n = a.K - h * 16;
+            load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, vc[k]);
+            if (k == 0 && norm) load16<false>(a.norm_w + h * 16, vec, n, wc);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < CACHE; ++k) {
+        const int it = tid + k * nt;
+        if (k < ncache && it < items) stats(it / nh, vc[k], wc);
+    }
+    for (int it = tid + ncache * nt; it < items; it += nt) {
+        const int b = it / nh, h = it - b * nh, n = a.K - h * 16;
+        float v[16], w[16];
+        load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, v);
+        if (norm) load16<false>(a.norm_w + h * 16, vec, n, w);
+        stats(b, v, w);
     }
 #pragma unroll
     for (int b = 0; b < GEMV_MB; ++b) {
@@ -243,7 +266,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
             }
         }
     }
-    __syncthreads();
+    sync_threads(nt);
     if (tid < a.B) {
         float S = 0.f, Mx = 0.f;
         for (int w = 0; w < nw; ++w) {
@@ -260,17 +283,10 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         s_red[128 + tid] = inv * exp2f(-e);   // multiplier applied before rounding to 16 bits
         s_scale[tid] = exp2f(e);
     }
-    __syncthreads();
-    for (int base = 0; base < items; base += nt) {   // warp-uniform trip count (block sums pair adjacent lanes)
-        const int it = base + tid;
-        const bool act = it < items;
-        const int b = act ? it / nh : 0, h = act ? it - b * nh : 0, n = a.K - h * 16;
+    sync_threads(nt);
+    auto convert = [&](bool act, int b, int h, int n, const float (&v)[16], const float (&w)[16]) {
         float bs = 0.f;
         if (act) {
-            const float *xr = a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16;
-            float v[16], w[16];
-            load16<true>(xr, vec, n, v);
-            if (norm) load16<false>(a.norm_w + h * 16, vec, n, w);
             if (a.feat && blockIdx.x == 0) {
                 float *f = a.feat + (size_t)(a.b0 + b) * a.feat_ld + h * 16;
 #pragma unroll
@@ -292,20 +308,43 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
             dst[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
             dst[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
         }
-        if (BSUM) {
+        if (BSUM) {   // the two halves of a block sit in adjacent lanes (warp-uniform call)
             bs += __shfl_xor_sync(0xffffffffu, bs, 1);
             if (act && (h & 1) == 0) bsum[(h >> 1) * GEMV_MB + b] = bs;
         }
+    };
+    int base = 0;
+#pragma unroll
+    for (int k = 0; k < CACHE; ++k) {
+        if (k >= ncache || base >= items) break;
+        const int it = base + tid;
+        const bool act = it < items;
+        const int b = act ? it / nh : 0, h = act ? it - b * nh : 0, n = a.K - h * 16;
+        convert(act, b, h, n, vc[k], wc);
+        base += nt;
     }
-    // zero the padding columns and the block sums of absent rows / padding blocks
+    for (; base < items; base += nt) {   // warp-uniform trip count
+        const int it = base + tid;
+        const bool act = it < items;
+        const int b = act ? it / nh : 0, h = act ? it - b * nh : 0, n = a.K - h * 16;
+        float v[16], w[16];
+        if (act) {
+            load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, v);
+            if (norm) load16<false>(a.norm_w + h * 16, vec, n, w);
+        }
+        convert(act, b, h, n, v, w);
+    }
+    // zero the padding columns, row B (read by the lanes of absent batch rows) and the block sums of absent rows /
+    // padding blocks
     const int kp = a.kpx, pad = kp - nb * 32;
     for (int idx = tid; idx < a.B * pad; idx += nt) xs[(size_t)(idx / pad) * kp + nb * 32 + idx % pad] = 0;
+    for (int idx = tid; idx < kp / 2; idx += nt) reinterpret_cast<uint32_t *>(xs + (size_t)a.B * kp)[idx] = 0u;
     if (BSUM)
         for (int idx = tid; idx < a.nblk * GEMV_MB; idx += nt) {
             const int blk = idx / GEMV_MB, b = idx - blk * GEMV_MB;
             if (b >= a.B || blk >= nb) bsum[idx] = 0.f;
         }
-    __syncthreads();
+    sync_threads(nt);
 }
 
 template <int FA, int FB, class Epi>
@@ -344,7 +383,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
     }
     griddep_wait();
     griddep_launch();
-    gemv_prologue<BSUM>(a, xs, s_scale, s_red, bsum);
+    gemv_prologue<BSUM>(a, xs, s_scale, s_red, bsum, blockDim.x);
 
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     if (active) {
@@ -384,7 +423,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
 
 inline size_t gemv_smem_bytes(const GemvArgs &a, bool bsum) {
     return (136 + GEMV_MB + 8 * 32 * 4 + (bsum ? a.nblk * GEMV_MB : 0)) * sizeof(float) +
-           (size_t)a.B * a.kpx * sizeof(uint16_t);
+           (size_t)(a.B + 1) * a.kpx * sizeof(uint16_t);
 }
 
 // Host helper: choose the k split so the launch covers the GPU, fill the launch parameters.

@@ -44,7 +44,10 @@ struct v3g_state {
     // persistent decode kernel (all layers + lm head in one cooperative launch)
     int use_mega = 0;
     void *mk_phases = nullptr;       // device MkPhase[mk_n]; the last entry is the lm head
-    int mk_n = 0, mk_grid = 0, mk_slots = 0, mk_xr = 0, mk_cnt_cap = 0;
+    void *mk_lite = nullptr;         // device MkLite[mk_n] (chunk-stream table)
+    void *mk_fn = nullptr;           // kernel instantiation for this model's head size and tile formats
+    int mk_n = 0, mk_grid = 0, mk_slots = 0, mk_xr = 0;
+    int mk_ph_off = 0, mk_lite_off = 0, mk_part_off = 0, mk_ring_off = 0, mk_bar_off = 0;
     size_t mk_smem = 0;
     std::string last_error;
 };

@@ -1,21 +1,25 @@
 // Persistent decode kernel: every layer of one decode step (and the lm head) in ONE cooperative launch, one CTA
-// of 8 warps per SM, phases separated by bounded grid barriers.
+// per SM (8 consumer warps + 1 producer warp), phases separated by bounded grid barriers.
 //
 // Phase list (host-built, per state): for every layer [QKV GEMV, attention, O GEMV, gate/up GEMV, down GEMV], then
 // the lm-head GEMV.  A GEMV phase is a flat sequence of T weight tiles (segment by segment, row tile by row tile,
-// k tile by k tile -- exactly the order of the tile buffers in HBM), cut into equal contiguous ranges, one per
-// warp of the grid.  Every warp therefore streams one contiguous byte range per phase, all SMs stay busy even when
-// a matrix has fewer row tiles than the GPU has SMs, and the load is balanced to one tile.
+// k tile by k tile -- exactly the order of the tile buffers in HBM).  CTA c owns the whole row tiles
+// [c NR / G, (c+1) NR / G) and its 8 consumer warps cut the CTA's contiguous tile range into equal pieces, so
+// every warp streams one contiguous byte range per phase and no row tile is ever split between SMs.
 //
 // Weight bytes reach shared memory through bulk asynchronous copies (cp.async.bulk, completion on an mbarrier) into
-// a per-warp ring of `slots` chunk buffers.  Lane 0 of each warp is that warp's producer: it keeps slots-1 chunks
-// in flight ahead of its own consumption, and because weights never change the producer runs ahead ACROSS phase
-// boundaries -- while a CTA waits at a grid barrier or runs attention, its copies for the next GEMV phase keep
-// HBM busy.  No weight bytes pass through registers until the tile is consumed.
+// a ring of `slots` chunk buffers per consumer warp.  The producer warp issues every copy (lane i feeds consumer
+// warp i; a full / empty mbarrier pair per slot), so consumers only wait, compute and release; because weights
+// never change the producer runs ahead ACROSS phase boundaries -- while the consumers wait at a grid barrier, run a
+// prologue or attention, the copies for the coming GEMV phases keep HBM busy.  The chunk streams are walked from a
+// compact per-phase table held in shared memory, so no bookkeeping touches global memory.
 //
-// Row tiles that one warp covers completely go straight to the fused epilogue.  A row tile split between warps
-// (at most at both ends of a warp's range) is written as a partial to a per-warp slot; the last warp to arrive
-// (atomic ticket per row tile) sums the partials in warp order -- deterministic -- and runs the epilogue.
+// The kernel is compiled per pair of tile formats (FA, FB): every segment of every GEMV phase uses one of the two
+// (all Q8_0; Hybrid-Q4_0 = Q4_0 + Q8_0; all BF16; all F16; all F32), so the inner loops carry no format switch.
+//
+// Row tiles that one warp covers completely go straight to the fused epilogue.  A row tile split between warps of
+// the CTA is finished at the end of the phase: every warp leaves its partial in shared memory and the warp where
+// the row tile starts sums the pieces in warp order (deterministic) and runs the epilogue.
 //
 // Attention phases spread the (sequence, KV head, key chunk) work items over the CTAs (v3g_attn.cuh).
 // This header is included at the end of v3g_step.cu, after the epilogue functors it instantiates.
@@ -27,27 +31,52 @@ namespace v3g {
 
 enum : int { MK_GEMV = 0, MK_ATTN = 1 };
 enum : int { MK_EPI_QKV = 0, MK_EPI_RESID = 1, MK_EPI_GATEUP = 2, MK_EPI_STORE = 3 };
-constexpr int MK_WARPS = GEMV_THREADS / 32;
+constexpr int MK_WARPS = GEMV_THREADS / 32;            // consumer warps
+constexpr int MK_CT = MK_WARPS * 32;                    // consumer threads (named-barrier count)
+constexpr int MK_THREADS = MK_CT + 32;                  // + the producer warp
 constexpr int MK_MAX_SLOTS = 16;
-constexpr int MK_SLOT_BYTES = 2304;       // 4 Q4_0 / Q8_0 / BF16 tiles or 1 F32 tile; multiple of 16
+constexpr int MK_CHUNK = 4;                             // tiles per chunk (F32: 1)
+constexpr int MK_SLOT_BYTES = MK_CHUNK * 576;           // 4 Q4_0 / Q8_0 / 16-bit tiles or 1 F32 tile
 constexpr uint32_t MK_WAIT_LIMIT = 1u << 22;
 
-struct MkPhase {
+__host__ __device__ constexpr int mk_cap(int fmt) { return fmt == FMT_F32 ? 1 : MK_CHUNK; }
+
+// full description of one phase (read by the CTA from a shared-memory copy while the phase runs)
+struct alignas(16) MkPhase {
     GemvArgs a;
     int fmts[3];
     int kind, epi, layer;
-    int64_t tbase[4];     // flat tile index where segment s starts; tbase[n_seg] = T
+    int tbase[4];         // flat tile index where segment s starts; tbase[n_seg] = T
     int rbase[3];         // flat row-tile index where segment s starts (ticket counters)
     const float *bq, *bk, *bv;
     float *out;
     int out_ld, out_rows;
 };
 
+// chunk-stream view of one phase; the whole table lives in shared memory for the kernel's lifetime
+struct MkLite {
+    const uint8_t *tiles[3];
+    int tbase[4];
+    int rbase[4];         // flat row-tile index where segment s starts; rbase[n_seg] = row tiles of the phase
+    int kt[3];            // k tiles per row tile of segment s
+    int8_t kind, n_seg;
+    int8_t fmt[3];
+    int8_t pad[7];
+};
+static_assert(sizeof(MkLite) == 80, "MkLite is one 80-byte record");
+
 struct MkCfg {
-    int slots;            // ring depth per warp
-    int xr_bytes;         // bytes of the activation / attention region at the start of dynamic shared memory
-    float *part;          // [n_warps][2][32 lanes][4] split row-tile partials
-    uint32_t *cnt;        // [max row tiles] arrival tickets (zero between uses)
+    int slots;            // ring depth per consumer warp
+    int xr_bytes;         // activation / attention region at the start of dynamic shared memory
+    int ph_off, lite_off, part_off, ring_off, bar_off;   // shared-memory offsets (bytes); bar_off: full, then empty
+    const MkLite *lite;   // global copy of the lite table (n_phases records)
+};
+
+// shared-memory record of the split row tiles of one phase: per warp, a head piece (row tile begun by an earlier
+// warp) and a tail piece (row tile begun here, continued by later warps)
+struct MkPart {
+    float v[MK_WARPS][2][32][4];
+    int head_row[MK_WARPS];   // flat row tile of the head piece, -1 when none, -2 when the warp has no tiles
 };
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -55,29 +84,31 @@ struct MkCfg {
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+// expect `bytes` on bar and copy them global -> shared (no multicast: a plain CTA-local bulk copy)
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
 }
 
-// expect `bytes` on bar and copy them global -> shared (no multicast: a plain CTA-local bulk copy)
-__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(done)
+                 : "r"(bar), "r"(parity)
                  : "memory");
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
+    return done != 0;
 }
 
 // bounded wait for the completion of phase `parity` of bar; false when the limit ran out
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    const uint32_t a = smem_u32(bar);
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     for (uint32_t i = 0; i < MK_WAIT_LIMIT; ++i) {
         uint32_t done;
         asm volatile(
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
             : "=r"(done)
-            : "r"(a), "r"(parity)
+            : "r"(bar), "r"(parity)
             : "memory");
         if (done) return true;
     }
@@ -87,236 +118,434 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
 // ---------------------------------------------------------------------------------------------------------------
 // per-warp chunk stream over all GEMV phases
 // ---------------------------------------------------------------------------------------------------------------
-struct MkCursor {
-    int p;                // phase of the next chunk (n_phases when exhausted)
-    int64_t t, t1;        // next flat tile and end of this warp's range in phase p
+struct MkCur {
+    int p, si;            // phase (n_phases when exhausted) and segment of the next chunk
+    int t, t1, send;      // next flat tile, end of this warp's range in phase p, end of the run in segment si
+    int tl;               // tile index of t inside segment si
+    int r, kt, KT;        // row tile / k tile of tl, k tiles per row tile
+    int fmt;
+    const uint8_t *tiles; // tile buffer of segment si
 };
 
-struct MkChunk {
-    const uint8_t *src;
-    int bytes, n, fmt, si;
-    int64_t tl0;          // tile index of the first tile inside segment si
-};
+// flat tile index of the first tile of flat row tile R
+__device__ __forceinline__ int mk_row_tile(const MkLite &L, int R) {
+    int si = 0;
+    while (si + 1 < L.n_seg && R >= L.rbase[si + 1]) ++si;
+    return L.tbase[si] + (R - L.rbase[si]) * L.kt[si];
+}
 
-// warps that take part in a phase of T tiles (every one of them gets >= 1 tile)
-__device__ __forceinline__ int mk_nw(int64_t T, int NW) { return T < (int64_t)NW ? (int)T : NW; }
+// tile range [t0, t1) of consumer warp wi of CTA c (of G) in phase L
+__device__ __forceinline__ void mk_range(const MkLite &L, int c, int G, int wi, int &t0, int &t1) {
+    const int NR = L.rbase[L.n_seg];
+    const int lo = mk_row_tile(L, (int)((int64_t)c * NR / G)), hi = mk_row_tile(L, (int)((int64_t)(c + 1) * NR / G));
+    t0 = lo + (int)((int64_t)wi * (hi - lo) / MK_WARPS);
+    t1 = lo + (int)((int64_t)(wi + 1) * (hi - lo) / MK_WARPS);
+}
 
-__device__ __forceinline__ void mk_enter(const MkPhase *ph, int n_phases, int w, int NW, MkCursor &c, int p) {
+__device__ __forceinline__ void mk_seg(const MkLite &L, MkCur &c) {
+    c.send = L.tbase[c.si + 1] < c.t1 ? L.tbase[c.si + 1] : c.t1;
+    c.tl = c.t - L.tbase[c.si];
+    c.KT = L.kt[c.si];
+    c.r = c.tl / c.KT;
+    c.kt = c.tl - c.r * c.KT;
+    c.fmt = L.fmt[c.si];
+    c.tiles = L.tiles[c.si];
+}
+
+__device__ __forceinline__ void mk_enter(const MkLite *lite, int n_phases, int cta, int G, int wi, MkCur &c, int p) {
     for (; p < n_phases; ++p) {
-        const MkPhase &P = ph[p];
-        if (P.kind != MK_GEMV) continue;
-        const int64_t T = P.tbase[P.a.n_seg];
-        const int nw = mk_nw(T, NW);
-        if (w >= nw) continue;
+        const MkLite &L = lite[p];
+        if (L.kind != MK_GEMV) continue;
+        int t0, t1;
+        mk_range(L, cta, G, wi, t0, t1);
+        if (t0 >= t1) continue;
         c.p = p;
-        c.t = (int64_t)w * T / nw;
-        c.t1 = (int64_t)(w + 1) * T / nw;
+        c.t = t0;
+        c.t1 = t1;
+        c.si = 0;
+        while (c.si + 1 < L.n_seg && c.t >= L.tbase[c.si + 1]) ++c.si;
+        mk_seg(L, c);
         return;
     }
     c.p = n_phases;
-    c.t = c.t1 = 0;
 }
 
-// next chunk of the cursor's stream (requires c.p < n_phases); advances the cursor
-__device__ __forceinline__ MkChunk mk_next(const MkPhase *ph, int n_phases, int w, int NW, MkCursor &c) {
-    const MkPhase &P = ph[c.p];
-    int si = 0;
-    while (si + 1 < P.a.n_seg && c.t >= P.tbase[si + 1]) ++si;
-    MkChunk k;
-    k.fmt = P.fmts[si];
-    k.si = si;
-    const int tb = tile_bytes(k.fmt);
-    const int64_t seg_end = P.tbase[si + 1] < c.t1 ? P.tbase[si + 1] : c.t1;
-    const int64_t cap = MK_SLOT_BYTES / tb;
-    k.n = (int)(seg_end - c.t < cap ? seg_end - c.t : cap);
-    k.tl0 = c.t - P.tbase[si];
-    k.src = P.a.seg[si].tiles + k.tl0 * tb;
-    k.bytes = k.n * tb;
-    c.t += k.n;
-    if (c.t >= c.t1) mk_enter(ph, n_phases, w, NW, c, c.p + 1);
-    return k;
+__device__ __forceinline__ int mk_chunk_n(const MkCur &c) {
+    const int cap = mk_cap(c.fmt);
+    return c.send - c.t < cap ? c.send - c.t : cap;
 }
 
-// ---------------------------------------------------------------------------------------------------------------
-// split row tiles
-// ---------------------------------------------------------------------------------------------------------------
-// warp (among nw over T tiles) whose range holds flat tile t
-__device__ __forceinline__ int mk_owner(int64_t t, int64_t T, int nw) { return (int)(((t + 1) * nw - 1) / T); }
-
-// y = this warp's (scaled) sums of row tile (si, r); complete row tiles go to the epilogue, split ones through the
-// partial slots and the ticket of the row tile
-template <class Epi>
-__device__ __forceinline__ void mk_flush(const MkPhase &P, const Epi &epi, const MkCfg &cfg, int si, int64_t r,
-                                         float (&y)[4], int w, int nw, int64_t t0w, int64_t t1w, int lane) {
-    const int g = lane >> 2, t = lane & 3, B = P.a.B;
-    const int KT = P.a.seg[si].n_ktiles;
-    const int64_t rs = P.tbase[si] + r * KT, re = rs + KT;
-    if (!(t0w <= rs && re <= t1w)) {
-        const int slot = rs <= t0w ? 0 : 1;
-        float *pp = cfg.part + (((size_t)w * 2 + slot) * 32 + lane) * 4;
-        *reinterpret_cast<float4 *>(pp) = make_float4(y[0], y[1], y[2], y[3]);
-        __threadfence();
-        __syncwarp();
-        const int64_t T = P.tbase[P.a.n_seg];
-        const int wa = mk_owner(rs, T, nw), wb = mk_owner(re - 1, T, nw);
-        uint32_t *cnt = cfg.cnt + P.rbase[si] + r;
-        uint32_t ticket = 0;
-        if (lane == 0) ticket = atomicAdd(cnt, 1u);
-        ticket = __shfl_sync(0xffffffffu, ticket, 0);
-        if (ticket != (uint32_t)(wb - wa)) return;
-        __threadfence();
-        y[0] = y[1] = y[2] = y[3] = 0.f;
-        for (int v = wa; v <= wb; ++v) {
-            const int64_t sv = (int64_t)v * T / nw;
-            const int sl = (v == wa && sv < rs) ? 1 : 0;
-            const float4 q = __ldcg(reinterpret_cast<const float4 *>(cfg.part + (((size_t)v * 2 + sl) * 32 + lane) * 4));
-            y[0] += q.x;
-            y[1] += q.y;
-            y[2] += q.z;
-            y[3] += q.w;
+// move the cursor past the n tiles of its current chunk
+__device__ __forceinline__ void mk_advance(const MkLite *lite, int n_phases, int cta, int G, int wi, MkCur &c, int n) {
+    c.t += n;
+    if (c.t >= c.t1) {
+        mk_enter(lite, n_phases, cta, G, wi, c, c.p + 1);
+    } else if (c.t >= c.send) {
+        ++c.si;
+        mk_seg(lite[c.p], c);
+    } else {
+        c.tl += n;
+        c.kt += n;
+        while (c.kt >= c.KT) {
+            c.kt -= c.KT;
+            ++c.r;
         }
-        if (lane == 0) *cnt = 0u;
     }
-    const int rt = (int)r;
-    if (2 * t < B) epi(si, rt, g, 2 * t, y[0], y[2]);
-    if (2 * t + 1 < B) epi(si, rt, g, 2 * t + 1, y[1], y[3]);
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// row-tile results
+// ---------------------------------------------------------------------------------------------------------------
+template <class Epi>
+__device__ __forceinline__ void mk_emit(const Epi &epi, int B, int si, int r, int lane, float y0, float y1, float y2,
+                                        float y3) {
+    const int g = lane >> 2, t = lane & 3;
+    if (2 * t < B) epi(si, r, g, 2 * t, y0, y2);
+    if (2 * t + 1 < B) epi(si, r, g, 2 * t + 1, y1, y3);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// tile arithmetic on shared-memory chunks
+// ---------------------------------------------------------------------------------------------------------------
+// Activation rows: xq = row min(g, B) of the converted activations + 2t (row B is zero), so absent batch rows
+// contribute nothing without a select.  bq = bsum + 2t.  Both are indexed by the k tile.
+
+// one tile at tb (shared memory) with k tile kt, accumulated into acc (rows g, g+8 x batch 2t, 2t+1)
 template <int FMT>
-__device__ __forceinline__ void mk_tile(const uint8_t *tb, int kt, const uint16_t *xr, const float *bsum, int lane,
+__device__ __forceinline__ void mk_tile(const uint8_t *tb, int kt, const uint16_t *xq, const float *bq, int lane,
                                         float (&acc)[4]) {
-    TileRegs r;
-    r.q = *reinterpret_cast<const uint4 *>(tb + lane * 16);
+    constexpr int TK = tile_k(FMT);
+    const int g = lane >> 2;
+    const uint4 q = *reinterpret_cast<const uint4 *>(tb + lane * 16);
+    const uint16_t *xk = xq + kt * TK;
     if constexpr (FMT == FMT_Q8) {
-        r.s.x = *reinterpret_cast<const uint32_t *>(tb + 512 + (lane >> 2) * 4);
+        const uint32_t sc = *reinterpret_cast<const uint32_t *>(tb + 512 + g * 4);
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+            mma16816(d, q8_pair(w[2 * s], 0x4140u), q8_pair(w[2 * s], 0x4342u), q8_pair(w[2 * s + 1], 0x4140u),
+                     q8_pair(w[2 * s + 1], 0x4342u), *reinterpret_cast<const uint32_t *>(xk + 16 * s),
+                     *reinterpret_cast<const uint32_t *>(xk + 16 * s + 8));
+        const float2 S = *reinterpret_cast<const float2 *>(bq + kt * GEMV_MB);
+        const float2 ds = h2f2(sc);
+        acc[0] = fmaf(ds.x, fmaf(-1152.f, S.x, d[0]), acc[0]);
+        acc[1] = fmaf(ds.x, fmaf(-1152.f, S.y, d[1]), acc[1]);
+        acc[2] = fmaf(ds.y, fmaf(-1152.f, S.x, d[2]), acc[2]);
+        acc[3] = fmaf(ds.y, fmaf(-1152.f, S.y, d[3]), acc[3]);
     } else if constexpr (FMT == FMT_Q4) {
-        r.s = *reinterpret_cast<const uint2 *>(tb + 512 + (lane >> 2) * 8);
-    } else if constexpr (FMT == FMT_F32) {
-        r.m = *reinterpret_cast<const uint4 *>(tb + 512 + lane * 16);
-        r.l = *reinterpret_cast<const uint4 *>(tb + 1024 + lane * 16);
+        const uint2 sc = *reinterpret_cast<const uint2 *>(tb + 512 + g * 8);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w}, scw[2] = {sc.x, sc.y};
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk) {
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ss = 0; ss < 2; ++ss) {
+                const int s = 2 * blk + ss;
+                mma16816(d, q4_pair<0>(w[s]), q4_pair<4>(w[s]), q4_pair<8>(w[s]), q4_pair<12>(w[s]),
+                         *reinterpret_cast<const uint32_t *>(xk + 16 * s),
+                         *reinterpret_cast<const uint32_t *>(xk + 16 * s + 8));
+            }
+            const float2 S = *reinterpret_cast<const float2 *>(bq + (2 * kt + blk) * GEMV_MB);
+            const float2 ds = h2f2(scw[blk]);
+            acc[0] = fmaf(ds.x, fmaf(-1032.f, S.x, d[0]), acc[0]);
+            acc[1] = fmaf(ds.x, fmaf(-1032.f, S.y, d[1]), acc[1]);
+            acc[2] = fmaf(ds.y, fmaf(-1032.f, S.x, d[2]), acc[2]);
+            acc[3] = fmaf(ds.y, fmaf(-1032.f, S.y, d[3]), acc[3]);
+        }
+    } else if constexpr (FMT == FMT_F32) {   // planes accumulate apart, then hi + 2^-11 mid + 2^-22 lo
+        const uint4 m = *reinterpret_cast<const uint4 *>(tb + 512 + lane * 16);
+        const uint4 l = *reinterpret_cast<const uint4 *>(tb + 1024 + lane * 16);
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xk), b1 = *reinterpret_cast<const uint32_t *>(xk + 8);
+        float dm[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(acc, q.x, q.y, q.z, q.w, b0, b1);
+        mma16816(dm, m.x, m.y, m.z, m.w, b0, b1);
+        mma16816(dl, l.x, l.y, l.z, l.w, b0, b1);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] = fmaf(dm[i], F32_MID, fmaf(dl[i], F32_LO, acc[i]));
+    } else {   // fp16 tiles (F16 files, BF16 weights stored as scaled fp16)
+        mma16816(acc, q.x, q.y, q.z, q.w, *reinterpret_cast<const uint32_t *>(xk),
+                 *reinterpret_cast<const uint32_t *>(xk + 8));
     }
-    compute_tile<FMT>(r, kt, xr, bsum, lane & 3, acc);
 }
 
-// per-warp ring state (identical in every lane)
+// a full chunk whose MK_CHUNK tiles lie in one row tile: every shared load first, then the tensor-core chains
+template <int FMT>
+__device__ __forceinline__ void mk_chunk_fast(const uint8_t *sb, int kt, const uint16_t *xq, const float *bq, int lane,
+                                              float (&acc)[4]) {
+    constexpr int TB = tile_bytes(FMT), TK = tile_k(FMT), NS = TK / 16, N = MK_CHUNK;
+    const int g = lane >> 2;
+    const uint16_t *xk = xq + kt * TK;
+    uint4 q[N];
+    uint2 sc[N];
+    uint32_t b0[N][NS], b1[N][NS];
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        q[i] = *reinterpret_cast<const uint4 *>(sb + i * TB + lane * 16);
+        if constexpr (FMT == FMT_Q8) sc[i].x = *reinterpret_cast<const uint32_t *>(sb + i * TB + 512 + g * 4);
+        if constexpr (FMT == FMT_Q4) sc[i] = *reinterpret_cast<const uint2 *>(sb + i * TB + 512 + g * 8);
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+            b0[i][s] = *reinterpret_cast<const uint32_t *>(xk + i * TK + 16 * s);
+            b1[i][s] = *reinterpret_cast<const uint32_t *>(xk + i * TK + 16 * s + 8);
+        }
+    }
+    if constexpr (FMT == FMT_Q8) {
+        float d[N][4];
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.f;
+            const uint32_t w[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
+#pragma unroll
+            for (int s = 0; s < 2; ++s)
+                mma16816(d[i], q8_pair(w[2 * s], 0x4140u), q8_pair(w[2 * s], 0x4342u), q8_pair(w[2 * s + 1], 0x4140u),
+                         q8_pair(w[2 * s + 1], 0x4342u), b0[i][s], b1[i][s]);
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const float2 S = *reinterpret_cast<const float2 *>(bq + (kt + i) * GEMV_MB);
+            const float2 ds = h2f2(sc[i].x);
+            acc[0] = fmaf(ds.x, fmaf(-1152.f, S.x, d[i][0]), acc[0]);
+            acc[1] = fmaf(ds.x, fmaf(-1152.f, S.y, d[i][1]), acc[1]);
+            acc[2] = fmaf(ds.y, fmaf(-1152.f, S.x, d[i][2]), acc[2]);
+            acc[3] = fmaf(ds.y, fmaf(-1152.f, S.y, d[i][3]), acc[3]);
+        }
+    } else if constexpr (FMT == FMT_Q4) {
+        float d[N][2][4];
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const uint32_t w[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                d[i][blk][0] = d[i][blk][1] = d[i][blk][2] = d[i][blk][3] = 0.f;
+#pragma unroll
+                for (int ss = 0; ss < 2; ++ss) {
+                    const int s = 2 * blk + ss;
+                    mma16816(d[i][blk], q4_pair<0>(w[s]), q4_pair<4>(w[s]), q4_pair<8>(w[s]), q4_pair<12>(w[s]),
+                             b0[i][s], b1[i][s]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const uint32_t scw[2] = {sc[i].x, sc[i].y};
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                const float2 S = *reinterpret_cast<const float2 *>(bq + (2 * (kt + i) + blk) * GEMV_MB);
+                const float2 ds = h2f2(scw[blk]);
+                acc[0] = fmaf(ds.x, fmaf(-1032.f, S.x, d[i][blk][0]), acc[0]);
+                acc[1] = fmaf(ds.x, fmaf(-1032.f, S.y, d[i][blk][1]), acc[1]);
+                acc[2] = fmaf(ds.y, fmaf(-1032.f, S.x, d[i][blk][2]), acc[2]);
+                acc[3] = fmaf(ds.y, fmaf(-1032.f, S.y, d[i][blk][3]), acc[3]);
+            }
+        }
+    } else {   // fp16 tiles: independent accumulators, summed at the end
+        float d[N][4];
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.f;
+            mma16816(d[i], q[i].x, q[i].y, q[i].z, q[i].w, b0[i][0], b1[i][0]);
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            acc[0] += d[i][0];
+            acc[1] += d[i][1];
+            acc[2] += d[i][2];
+            acc[3] += d[i][3];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// consumer warps
+// ---------------------------------------------------------------------------------------------------------------
 struct MkRing {
-    uint8_t *buf;         // slots * MK_SLOT_BYTES
-    uint64_t *bar;        // slots mbarriers
+    const uint8_t *buf;   // slot 0 of this warp's ring (slots * MK_SLOT_BYTES)
+    uint32_t full, empty; // shared addresses of this warp's first full / empty mbarrier
     int slots;
-    uint32_t issued, consumed;
-    MkCursor prod, cons;
-    bool dead;            // a wait ran out: stop copying and computing (the step is reported invalid)
-    uint32_t d0, d1;      // chunks [d0, d1) were in flight when the ring died
+    int slot;             // slot of the next chunk
+    uint32_t phase;       // parity of the next chunk's use of its slot
+    MkCur cons;
+    bool dead;            // a wait ran out: stop computing (the step is reported invalid)
 };
 
-__device__ __forceinline__ void mk_issue(MkRing &R, const MkPhase *ph, int n_phases, int w, int NW, int lane) {
-    if (R.dead || R.prod.p >= n_phases) return;
-    const MkChunk k = mk_next(ph, n_phases, w, NW, R.prod);
-    const int s = (int)(R.issued % (uint32_t)R.slots);
-    if (lane == 0) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // our generic reads of the slot come first
-        bulk_load(R.buf + (size_t)s * MK_SLOT_BYTES, k.src, (uint32_t)k.bytes, R.bar + s);
-    }
-    ++R.issued;
-}
-
-template <class Epi>
-__device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkRing &R, const MkPhase *ph,
-                                           int n_phases, int p, int w, int NW, const MkCfg &cfg, const uint16_t *xr,
-                                           const float *bsum, const float *s_scale, int *status, int lane) {
-    const int64_t T = P.tbase[P.a.n_seg];
-    const int nw = mk_nw(T, NW);
-    if (w >= nw) return;
-    const int64_t t0w = (int64_t)w * T / nw, t1w = (int64_t)(w + 1) * T / nw;
+// One GEMV phase for one consumer warp.  Every consumer warp of the CTA calls it (the closing combine synchronises
+// them); warps without tiles in the phase only take part in the combine.
+template <int FA, int FB, class Epi>
+__device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkRing &R, const MkLite *lite,
+                                           int n_phases, int p, int cta, int G, int wi, const uint16_t *xq,
+                                           const float *bq, const float *s_scale, MkPart &part, int *status,
+                                           int lane) {
     const int t = lane & 3, B = P.a.B;
     const float sc0 = 2 * t < B ? s_scale[2 * t] : 0.f, sc1 = 2 * t + 1 < B ? s_scale[2 * t + 1] : 0.f;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int cur_si = -1;
-    int64_t cur_r = -1;
+    int cur_si = -1, cur_r = -1;
+    int tail_si = -1, tail_r = -1;   // split row tile begun in this warp, finished after the phase
+    int t0w = 0, t1w = 0;
+    mk_range(lite[p], cta, G, wi, t0w, t1w);
+    if (lane == 0) part.head_row[wi] = t0w < t1w ? -1 : -2;
+    auto flush = [&]() {   // the finished piece of row tile (cur_si, cur_r)
+        const float ws = P.a.seg[cur_si].wscale, s0 = sc0 * ws, s1 = sc1 * ws;
+        const float y0 = acc[0] * s0, y1 = acc[1] * s1, y2 = acc[2] * s0, y3 = acc[3] * s1;
+        const int KT = P.a.seg[cur_si].n_ktiles;
+        const int rs = P.tbase[cur_si] + cur_r * KT, re = rs + KT;
+        if (rs >= t0w && re <= t1w) {
+            mk_emit(epi, B, cur_si, cur_r, lane, y0, y1, y2, y3);
+            return;
+        }
+        const int slot = rs < t0w ? 0 : 1;
+        *reinterpret_cast<float4 *>(part.v[wi][slot][lane]) = make_float4(y0, y1, y2, y3);
+        if (slot == 0) {
+            if (lane == 0) part.head_row[wi] = P.rbase[cur_si] + cur_r;
+        } else {
+            tail_si = cur_si;
+            tail_r = cur_r;
+        }
+    };
     while (R.cons.p == p) {
-        const MkChunk k = mk_next(ph, n_phases, w, NW, R.cons);
-        const int s = (int)(R.consumed % (uint32_t)R.slots);
-        const uint32_t par = (R.consumed / (uint32_t)R.slots) & 1u;
-        if (!R.dead && !mbar_wait(R.bar + s, par)) {
+        const int n = mk_chunk_n(R.cons), si = R.cons.si, KT = R.cons.KT;
+        int r = R.cons.r, kt = R.cons.kt;
+        const bool fa = FA == FB || R.cons.fmt == FA;
+        if (!R.dead && !mbar_wait(R.full + R.slot * 8, R.phase)) {
             R.dead = true;
-            R.d0 = R.consumed;
-            R.d1 = R.issued;
             if (lane == 0) atomicOr(status, STATUS_TIMEOUT);
         }
-        const uint8_t *sb = R.buf + (size_t)s * MK_SLOT_BYTES;
-        const int KT = P.a.seg[k.si].n_ktiles;
-        int64_t r = k.tl0 / KT;
-        int kt = (int)(k.tl0 - r * KT);
-        const int tb = tile_bytes(k.fmt);
-        for (int i = 0; i < k.n; ++i) {
-            if (r != cur_r || k.si != cur_si) {
-                if (cur_r >= 0) {
-                    const float ws = P.a.seg[cur_si].wscale;
-                    float y[4] = {acc[0] * sc0 * ws, acc[1] * sc1 * ws, acc[2] * sc0 * ws, acc[3] * sc1 * ws};
-                    mk_flush(P, epi, cfg, cur_si, cur_r, y, w, nw, t0w, t1w, lane);
-                }
-                cur_r = r;
-                cur_si = k.si;
-                acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-            }
-            if (!R.dead) {
-                const uint8_t *tp = sb + (size_t)i * tb;
-                switch (k.fmt) {   // warp-uniform
-                    case FMT_Q8: mk_tile<FMT_Q8>(tp, kt, xr, bsum, lane, acc); break;
-                    case FMT_Q4: mk_tile<FMT_Q4>(tp, kt, xr, bsum, lane, acc); break;
-                    case FMT_BF16: mk_tile<FMT_BF16>(tp, kt, xr, bsum, lane, acc); break;
-                    case FMT_F16: mk_tile<FMT_F16>(tp, kt, xr, bsum, lane, acc); break;
-                    default: mk_tile<FMT_F32>(tp, kt, xr, bsum, lane, acc); break;
-                }
-            }
-            if (++kt == KT) {
-                kt = 0;
-                ++r;
-            }
+        const uint8_t *sb = R.buf + R.slot * MK_SLOT_BYTES;
+        if (r != cur_r || si != cur_si) {
+            if (cur_r >= 0) flush();
+            cur_r = r;
+            cur_si = si;
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
         }
-        ++R.consumed;
-        __syncwarp();
-        mk_issue(R, ph, n_phases, w, NW, lane);   // refill the slot just read
+        if (!R.dead) {
+            if (n == MK_CHUNK && kt + MK_CHUNK <= KT && (fa ? FA : FB) != FMT_F32) {   // one row, whole chunk
+                if (fa) mk_chunk_fast<FA == FMT_F32 ? FMT_Q8 : FA>(sb, kt, xq, bq, lane, acc);
+                else mk_chunk_fast<FB == FMT_F32 ? FMT_Q8 : FB>(sb, kt, xq, bq, lane, acc);
+            } else {
+                for (int i = 0; i < n; ++i) {   // chunk ends a range / segment, or crosses row tiles
+                    if (i > 0 && kt == 0) {
+                        flush();
+                        cur_r = ++r;
+                        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+                    }
+                    if (fa) mk_tile<FA>(sb + i * tile_bytes(FA), kt, xq, bq, lane, acc);
+                    else mk_tile<FB>(sb + i * tile_bytes(FB), kt, xq, bq, lane, acc);
+                    if (++kt == KT) kt = 0;
+                }
+            }
+            __syncwarp();   // every tile byte of the slot is in registers: release it to the producer
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(R.empty + R.slot * 8) : "memory");
+        }
+        if (++R.slot == R.slots) {
+            R.slot = 0;
+            R.phase ^= 1u;
+        }
+        mk_advance(lite, n_phases, cta, G, wi, R.cons, n);
     }
-    if (cur_r >= 0) {
-        const float ws = P.a.seg[cur_si].wscale;
-        float y[4] = {acc[0] * sc0 * ws, acc[1] * sc1 * ws, acc[2] * sc0 * ws, acc[3] * sc1 * ws};
-        mk_flush(P, epi, cfg, cur_si, cur_r, y, w, nw, t0w, t1w, lane);
+    if (cur_r >= 0) flush();
+    sync_threads(MK_CT);   // every piece of every split row tile is in shared memory
+    if (tail_r >= 0) {     // this warp began the row tile: add the later warps' pieces in order, then the epilogue
+        const int row = P.rbase[tail_si] + tail_r;
+        float4 y = *reinterpret_cast<const float4 *>(part.v[wi][1][lane]);
+        for (int v = wi + 1; v < MK_WARPS; ++v) {
+            const int hr = part.head_row[v];
+            if (hr == -2) continue;   // a warp without tiles inside the row tile
+            if (hr != row) break;
+            const float4 q = *reinterpret_cast<const float4 *>(part.v[v][0][lane]);
+            y.x += q.x;
+            y.y += q.y;
+            y.z += q.z;
+            y.w += q.w;
+        }
+        mk_emit(epi, B, tail_si, tail_r, lane, y.x, y.y, y.z, y.w);
     }
 }
 
+template <int FA, int FB>
 __device__ __forceinline__ void mk_consume_epi(const MkPhase &P, const ModelDev *mp, const StateDev *sp, MkRing &R,
-                                               const MkPhase *ph, int n_phases, int p, int w, int NW,
-                                               const MkCfg &cfg, const uint16_t *xr, const float *bsum,
-                                               const float *s_scale, int *status, int lane) {
+                                               const MkLite *lite, int n_phases, int p, int cta, int G, int wi,
+                                               const uint16_t *xq, const float *bq, const float *s_scale,
+                                               MkPart &part, int *status, int lane) {
     switch (P.epi) {
         case MK_EPI_QKV: {
             EpiQKV e{mp, sp, P.layer, P.bq, P.bk, P.bv};
-            mk_consume(P, e, R, ph, n_phases, p, w, NW, cfg, xr, bsum, s_scale, status, lane);
+            mk_consume<FA, FB>(P, e, R, lite, n_phases, p, cta, G, wi, xq, bq, s_scale, part, status, lane);
             break;
         }
         case MK_EPI_RESID: {
             EpiResid e{P.out, P.out_ld, P.out_rows};
-            mk_consume(P, e, R, ph, n_phases, p, w, NW, cfg, xr, bsum, s_scale, status, lane);
+            mk_consume<FA, FB>(P, e, R, lite, n_phases, p, cta, G, wi, xq, bq, s_scale, part, status, lane);
             break;
         }
         case MK_EPI_GATEUP: {
             EpiGateUp e{P.out, P.out_rows};
-            mk_consume(P, e, R, ph, n_phases, p, w, NW, cfg, xr, bsum, s_scale, status, lane);
+            mk_consume<FA, FB>(P, e, R, lite, n_phases, p, cta, G, wi, xq, bq, s_scale, part, status, lane);
             break;
         }
         default: {
             EpiStore e{P.out, P.out_ld, P.out_rows};
-            mk_consume(P, e, R, ph, n_phases, p, w, NW, cfg, xr, bsum, s_scale, status, lane);
+            mk_consume<FA, FB>(P, e, R, lite, n_phases, p, cta, G, wi, xq, bq, s_scale, part, status, lane);
             break;
         }
     }
 }
 
-// bounded grid barrier: every CTA arrives once per phase on a counter zeroed at the start of the step; a wait
-// that exceeds its iteration limit records STATUS_TIMEOUT and returns (the step's results are then invalid)
+// ---------------------------------------------------------------------------------------------------------------
+// producer warp: lane i streams consumer warp i's chunks into its ring, a slot as soon as the consumer released it
+// (empty barrier), until the stream ends; then waits (bounded) until its last copies have landed
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void mk_produce(const MkLite *lite, int n_phases, int c, int G, const MkCfg &cfg,
+                                           uint8_t *smem, int *status) {
+    const int lane = threadIdx.x & 31;
+    if (lane >= MK_WARPS) return;
+    const int S = cfg.slots;
+    const uint32_t buf = smem_u32(smem + cfg.ring_off + (size_t)lane * S * MK_SLOT_BYTES);
+    const uint32_t full = smem_u32(smem + cfg.bar_off) + (uint32_t)(lane * S * 8);
+    const uint32_t empty = full + (uint32_t)(MK_WARPS * S * 8);
+    MkCur cur;
+    mk_enter(lite, n_phases, c, G, lane, cur, 0);
+    uint32_t slot = 0, round = 0, idle = 0;
+    while (cur.p < n_phases) {
+        if (round > 0 && !mbar_test(empty + slot * 8, (round - 1) & 1u)) {   // slot still in use
+            if (++idle > MK_WAIT_LIMIT) {
+                atomicOr(status, STATUS_TIMEOUT);
+                break;
+            }
+            __nanosleep(32);
+            continue;
+        }
+        idle = 0;
+        const int n = mk_chunk_n(cur);
+        const int tb = tile_bytes(cur.fmt);
+        bulk_load(buf + slot * MK_SLOT_BYTES, cur.tiles + (size_t)cur.tl * tb, (uint32_t)(n * tb), full + slot * 8);
+        mk_advance(lite, n_phases, c, G, lane, cur, n);
+        if (++slot == (uint32_t)S) {
+            slot = 0;
+            ++round;
+        }
+    }
+    // the last use of every slot: wait until its copy has landed
+    for (uint32_t sl = 0; sl < (uint32_t)S; ++sl) {
+        if (round == 0 && sl >= slot) continue;   // never used
+        const uint32_t use = sl < slot ? round : round - 1;
+        mbar_wait(full + sl * 8, use & 1u);
+    }
+}
+
+// asynchronous copy of phases[p] into a shared-memory slot (consumer threads 0 .. sizeof/16 - 1)
+__device__ __forceinline__ void mk_fetch_phase(const MkPhase *phases, int p, int n_phases, MkPhase *dst) {
+    constexpr int N16 = (int)(sizeof(MkPhase) / 16);
+    static_assert(N16 <= MK_CT, "one 16-byte piece per consumer thread");
+    if (p < n_phases && (int)threadIdx.x < N16)
+        cp_async16(reinterpret_cast<uint8_t *>(dst) + threadIdx.x * 16,
+                   reinterpret_cast<const uint8_t *>(phases + p) + threadIdx.x * 16);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// bounded grid barrier over the consumer warps: every CTA arrives once per phase on a counter zeroed at the start
+// of the step; a wait that exceeds its iteration limit records STATUS_TIMEOUT and returns (results then invalid)
 __device__ __forceinline__ void mk_grid_sync(unsigned int *bar, unsigned int target, int *status) {
-    __syncthreads();
+    sync_threads(MK_CT);
     if (threadIdx.x == 0) {
         __threadfence();
         atomicAdd(bar, 1u);
@@ -328,66 +557,81 @@ __device__ __forceinline__ void mk_grid_sync(unsigned int *bar, unsigned int tar
                 atomicOr(status, STATUS_TIMEOUT);
                 break;
             }
-            __nanosleep(32);
         }
         __threadfence();
     }
-    __syncthreads();
+    sync_threads(MK_CT);
 }
 
-template <int D>
-__global__ void __launch_bounds__(GEMV_THREADS, 1) k_decode(const ModelDev *mp, const StateDev *sp,
-                                                            const MkPhase *phases, int n_phases, float scale,
-                                                            MkCfg cfg) {
+template <int D, int FA, int FB>
+__global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, const StateDev *sp,
+                                                          const MkPhase *phases, int n_phases, float scale,
+                                                          MkCfg cfg) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int c = blockIdx.x, G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int NW = G * MK_WARPS, w = c * MK_WARPS + warp;
-    MkRing R;
-    R.slots = cfg.slots;
-    R.buf = smem + cfg.xr_bytes + (size_t)warp * cfg.slots * MK_SLOT_BYTES;
-    R.bar = reinterpret_cast<uint64_t *>(smem + cfg.xr_bytes + (size_t)MK_WARPS * cfg.slots * MK_SLOT_BYTES) +
-            warp * cfg.slots;
-    R.issued = R.consumed = R.d0 = R.d1 = 0;
-    R.dead = false;
-    if (lane == 0)
-        for (int s = 0; s < R.slots; ++s) mbar_init(R.bar + s, 1);
+    MkPhase *ph_s = reinterpret_cast<MkPhase *>(smem + cfg.ph_off);
+    MkLite *lite = reinterpret_cast<MkLite *>(smem + cfg.lite_off);
+    // the lite table (immutable), the first two phase descriptors and the ring barriers
+    for (int i = threadIdx.x; i < n_phases * (int)(sizeof(MkLite) / 16); i += blockDim.x)
+        cp_async16(reinterpret_cast<uint8_t *>(lite) + i * 16, reinterpret_cast<const uint8_t *>(cfg.lite) + i * 16);
+    if (warp < MK_WARPS) {
+        mk_fetch_phase(phases, 0, n_phases, ph_s);
+        mk_fetch_phase(phases, 1, n_phases, ph_s + 1);
+    }
+    const uint32_t bars = smem_u32(smem + cfg.bar_off);
+    for (int i = threadIdx.x; i < 2 * MK_WARPS * cfg.slots; i += blockDim.x)
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bars + i * 8) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    __syncwarp();
-    mk_enter(phases, n_phases, w, NW, R.prod, 0);
-    R.cons = R.prod;
-    // weights are immutable: start streaming before the previous kernel's results are needed
-    for (int s = 0; s < R.slots; ++s) mk_issue(R, phases, n_phases, w, NW, lane);
-    griddep_wait();
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
     const StateDev &st = *sp;
     int *status = &st.step->status;
+    if (warp == MK_WARPS) {   // weights are immutable: the producer streams from the very start
+        mk_produce(lite, n_phases, c, G, cfg, smem, status);
+        return;
+    }
+    MkRing R;
+    R.slots = cfg.slots;
+    R.buf = smem + cfg.ring_off + (size_t)warp * cfg.slots * MK_SLOT_BYTES;
+    R.full = bars + (uint32_t)(warp * cfg.slots * 8);
+    R.empty = R.full + (uint32_t)(MK_WARPS * cfg.slots * 8);
+    R.slot = 0;
+    R.phase = 0;
+    R.dead = false;
+    mk_enter(lite, n_phases, c, G, warp, R.cons, 0);
+    MkPart &part = *reinterpret_cast<MkPart *>(smem + cfg.part_off);
+    griddep_wait();
     const int64_t pos = __ldcg(&st.step->pos);
+    const int n_kv = mp->G, ms = st.max_splits, Bst = st.B;
+    unsigned int *gbar = st.bar;
+    constexpr bool BSUM = fmt_int(FA) || fmt_int(FB);
     float *s_red = reinterpret_cast<float *>(smem);
     float *s_scale = s_red + 136;
     float *bsum = s_scale + GEMV_MB;
     for (int p = 0; p < n_phases; ++p) {
-        const MkPhase &P = phases[p];
+        const MkPhase &P = ph_s[p & 1];
         if (P.kind == MK_ATTN) {
-            const int n_kv = mp->G, ms = st.max_splits;
-            const int n_items = st.B * n_kv * ms;
+            const int n_items = Bst * n_kv * ms;
             for (int i = c; i < n_items; i += G) {
                 const int split = i % ms, g = (i / ms) % n_kv, b = i / (ms * n_kv);
-                attn_item<D>(*mp, st, P.layer, scale, split, g, b, pos, *reinterpret_cast<AttnSmem<D> *>(smem));
+                attn_item<D>(*mp, st, P.layer, scale, split, g, b, pos, *reinterpret_cast<AttnSmem<D> *>(smem), MK_CT);
             }
         } else {
-            bool bs = false;
-            for (int i = 0; i < P.a.n_seg; ++i) bs = bs || fmt_int(P.fmts[i]);
-            uint16_t *xs = reinterpret_cast<uint16_t *>(bsum + (bs ? P.a.nblk * GEMV_MB : 0));
-            if (bs) gemv_prologue<true>(P.a, xs, s_scale, s_red, bsum);
-            else gemv_prologue<false>(P.a, xs, s_scale, s_red, bsum);
-            const int g = lane >> 2;
-            const uint16_t *xr = g < P.a.B ? xs + g * P.a.kpx : nullptr;
-            mk_consume_epi(P, mp, sp, R, phases, n_phases, p, w, NW, cfg, xr, bsum, s_scale, status, lane);
+            uint16_t *xs = reinterpret_cast<uint16_t *>(bsum + (BSUM ? P.a.nblk * GEMV_MB : 0));
+            gemv_prologue<BSUM, 3>(P.a, xs, s_scale, s_red, bsum, MK_CT);
+            const int g = lane >> 2, t = lane & 3;
+            const uint16_t *xq = xs + (g < P.a.B ? g : P.a.B) * P.a.kpx + 2 * t;
+            mk_consume_epi<FA, FB>(P, mp, sp, R, lite, n_phases, p, c, G, warp, xq, bsum + 2 * t, s_scale, part,
+                                   status, lane);
         }
-        if (p + 1 < n_phases) mk_grid_sync(st.bar, (unsigned int)(p + 1) * (unsigned int)G, status);
+        if (p + 1 < n_phases) {
+            asm volatile("cp.async.wait_all;" ::: "memory");   // descriptor p + 1 is in place after the barrier
+            mk_grid_sync(gbar, (unsigned int)(p + 1) * (unsigned int)G, status);
+            mk_fetch_phase(phases, p + 2, n_phases, ph_s + (p & 1));   // slot of phase p, now unused
+        }
     }
-    // every issued chunk was consumed unless a wait ran out; then wait (bounded) for what was still in flight
-    for (uint32_t q = R.d0; q < R.d1; ++q) mbar_wait(R.bar + q % (uint32_t)R.slots, (q / (uint32_t)R.slots) & 1u);
+    asm volatile("cp.async.wait_all;" ::: "memory");
     griddep_launch();
 }
 

@@ -750,13 +750,37 @@ cudaError_t launch_state_reset(const v3g_model *m, v3g_state *s, cudaStream_t st
 
 namespace v3g {
 
+typedef void (*MkKernel)(const ModelDev *, const StateDev *, const MkPhase *, int, float, MkCfg);
+
+template <int D>
+static MkKernel mk_kernel_d(int fa, int fb) {
+    if (fa == FMT_Q8 && fb == FMT_Q8) return k_decode<D, FMT_Q8, FMT_Q8>;
+    if (fa == FMT_Q4 && fb == FMT_Q8) return k_decode<D, FMT_Q4, FMT_Q8>;
+    if (fa == FMT_Q4 && fb == FMT_Q4) return k_decode<D, FMT_Q4, FMT_Q4>;
+    if (fa == FMT_BF16 && fb == FMT_BF16) return k_decode<D, FMT_BF16, FMT_BF16>;
+    if (fa == FMT_F16 && fb == FMT_F16) return k_decode<D, FMT_F16, FMT_F16>;
+    if (fa == FMT_F32 && fb == FMT_F32) return k_decode<D, FMT_F32, FMT_F32>;
+    return nullptr;
+}
+
+// persistent decode kernel instantiation for a head size and format pair (nullptr when none)
+static MkKernel mk_kernel(int D, int fa, int fb) {
+    switch (D) {
+        case 16: return mk_kernel_d<16>(fa, fb);
+        case 32: return mk_kernel_d<32>(fa, fb);
+        case 64: return mk_kernel_d<64>(fa, fb);
+        case 128: return mk_kernel_d<128>(fa, fb);
+        default: return nullptr;
+    }
+}
+
 // Phase table of the persistent decode kernel for this state; leaves use_mega = 0 when the batch does not fit one
 // pass (> 8 rows), a phase would mix 16-bit activation types, or the shared-memory plan leaves no ring.
 cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
     const ModelDev &md = m->host;
     const StateDev &sd = s->host;
     s->use_mega = 0;
-    if (s->B > GEMV_MB || !sd.mk_part || !sd.mk_cnt) return cudaSuccess;
+    if (s->B > GEMV_MB) return cudaSuccess;
     const bool any_seg = md.seg_n_feat > 0 && s->seg_cap > 0;
     std::vector<MkPhase> ph;
     size_t xr = 0;
@@ -778,14 +802,15 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
         for (int i = 0; i < n; ++i) {
             p.fmts[i] = c.fmts[i];
             bs = bs || fmt_int(c.fmts[i]);
-            p.tbase[i] = tb;
+            p.tbase[i] = (int)tb;
             p.rbase[i] = rb;
             tb += (int64_t)c.a.seg[i].n_rtiles * c.a.seg[i].n_ktiles;
             rb += c.a.seg[i].n_rtiles;
         }
-        p.tbase[n] = tb;
+        ok = ok && tb < (int64_t)1 << 30;
+        p.tbase[n] = (int)tb;
         max_rt = rb > max_rt ? rb : max_rt;
-        const size_t need = (size_t)(144 + (bs ? c.a.nblk * GEMV_MB : 0)) * 4 + (size_t)s->B * c.a.kpx * 2;
+        const size_t need = (size_t)(144 + (bs ? c.a.nblk * GEMV_MB : 0)) * 4 + (size_t)(s->B + 1) * c.a.kpx * 2;
         xr = need > xr ? need : xr;
         p.kind = MK_GEMV;
         p.epi = epi;
@@ -821,44 +846,91 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
     }
     const MatW *lm[1] = {&md.embed};
     add_gemv(lm, 1, sd.x, md.d, md.d, PRO_RMSNORM, md.norm, MK_EPI_STORE, -1, sd.logits, md.vocab, md.vocab);
-    if (!ok || max_rt > s->mk_cnt_cap) return cudaSuccess;
-    const void *fn = nullptr;
+    if (!ok) return cudaSuccess;
+    // the kernel's format pair: every segment of every GEMV phase must be FA or FB
+    bool has[16] = {};
+    for (const MkPhase &q : ph)
+        if (q.kind == MK_GEMV)
+            for (int i = 0; i < q.a.n_seg; ++i) has[q.fmts[i]] = true;
+    int nf = 0;
+    for (bool h : has) nf += h ? 1 : 0;
+    int fa, fb;
+    if (nf == 1) {
+        fa = fb = has[FMT_Q8] ? FMT_Q8 : has[FMT_Q4] ? FMT_Q4 : has[FMT_BF16] ? FMT_BF16 : has[FMT_F16] ? FMT_F16 : FMT_F32;
+    } else if (nf == 2 && has[FMT_Q4] && has[FMT_Q8]) {
+        fa = FMT_Q4;
+        fb = FMT_Q8;
+    } else {
+        return cudaSuccess;
+    }
+    const MkKernel fn = mk_kernel(md.D, fa, fb);
+    if (!fn) return cudaSuccess;
     size_t att = 0;
     switch (md.D) {
-        case 16: att = sizeof(AttnSmem<16>); fn = (const void *)k_decode<16>; break;
-        case 32: att = sizeof(AttnSmem<32>); fn = (const void *)k_decode<32>; break;
-        case 64: att = sizeof(AttnSmem<64>); fn = (const void *)k_decode<64>; break;
-        case 128: att = sizeof(AttnSmem<128>); fn = (const void *)k_decode<128>; break;
-        default: return cudaSuccess;
+        case 16: att = sizeof(AttnSmem<16>); break;
+        case 32: att = sizeof(AttnSmem<32>); break;
+        case 64: att = sizeof(AttnSmem<64>); break;
+        default: att = sizeof(AttnSmem<128>); break;
     }
     xr = (std::max(xr, att) + 127) / 128 * 128;
     int optin = 0;
     cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
     if (e != cudaSuccess) return e;
-    cudaFuncAttributes fa{};
-    e = cudaFuncGetAttributes(&fa, fn);
+    cudaFuncAttributes fattr{};
+    e = cudaFuncGetAttributes(&fattr, (const void *)fn);
     if (e != cudaSuccess) return e;
-    const long avail = (long)optin - (long)fa.sharedSizeBytes - (long)xr;
-    const long per_slot = (long)MK_WARPS * (MK_SLOT_BYTES + 8);
+    // shared memory: [x / attention region][2 phase descriptors][lite table][split pieces][rings][ring mbarriers]
+    const size_t ph_off = xr, lite_off = ph_off + 2 * sizeof(MkPhase);
+    const size_t part_off = (lite_off + ph.size() * sizeof(MkLite) + 15) / 16 * 16;
+    const size_t ring_off = (part_off + sizeof(MkPart) + 127) / 128 * 128;
+    const long avail = (long)optin - (long)fattr.sharedSizeBytes - (long)ring_off;
+    const long per_slot = (long)MK_WARPS * (MK_SLOT_BYTES + 16);   // buffer + full and empty barriers
     int slots = avail > 0 ? (int)(avail / per_slot) : 0;
     slots = slots > MK_MAX_SLOTS ? MK_MAX_SLOTS : slots;
     if (slots < 2) return cudaSuccess;
-    const size_t smem = xr + (size_t)slots * per_slot;
-    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t bar_off = ring_off + (size_t)MK_WARPS * slots * MK_SLOT_BYTES;
+    const size_t smem = bar_off + (size_t)2 * MK_WARPS * slots * 8;
+    e = cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, GEMV_THREADS, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, (const void *)fn, MK_THREADS, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaSuccess;
+    std::vector<MkLite> lite(ph.size());
+    for (size_t i = 0; i < ph.size(); ++i) {
+        MkLite L{};
+        L.kind = (int8_t)ph[i].kind;
+        L.n_seg = (int8_t)(ph[i].kind == MK_GEMV ? ph[i].a.n_seg : 0);
+        for (int j = 0; j < L.n_seg; ++j) {
+            L.tiles[j] = ph[i].a.seg[j].tiles;
+            L.kt[j] = ph[i].a.seg[j].n_ktiles;
+            L.fmt[j] = (int8_t)ph[i].fmts[j];
+        }
+        for (int j = 0; j <= L.n_seg; ++j) {
+            L.tbase[j] = ph[i].tbase[j];
+            L.rbase[j] = j < L.n_seg ? ph[i].rbase[j] : (j ? ph[i].rbase[j - 1] + ph[i].a.seg[j - 1].n_rtiles : 0);
+        }
+        lite[i] = L;
+    }
     e = cudaMalloc(&s->mk_phases, ph.size() * sizeof(MkPhase));
     if (e != cudaSuccess) return e;
     e = cudaMemcpy(s->mk_phases, ph.data(), ph.size() * sizeof(MkPhase), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return e;
+    e = cudaMalloc(&s->mk_lite, lite.size() * sizeof(MkLite));
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpy(s->mk_lite, lite.data(), lite.size() * sizeof(MkLite), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return e;
     s->mk_n = (int)ph.size();
     s->mk_smem = smem;
     s->mk_slots = slots;
     s->mk_xr = (int)xr;
+    s->mk_ph_off = (int)ph_off;
+    s->mk_lite_off = (int)lite_off;
+    s->mk_part_off = (int)part_off;
+    s->mk_ring_off = (int)ring_off;
+    s->mk_bar_off = (int)bar_off;
     s->mk_grid = m->n_sm;
+    s->mk_fn = (void *)fn;
     s->use_mega = 1;
     return cudaSuccess;
 }
@@ -869,7 +941,7 @@ cudaError_t launch_mega(const v3g_model *m, v3g_state *s, bool want_lm, cudaStre
     const int n = want_lm ? s->mk_n : s->mk_n - 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(s->mk_grid);
-    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.blockDim = dim3(MK_THREADS);
     cfg.dynamicSmemBytes = s->mk_smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -884,14 +956,13 @@ cudaError_t launch_mega(const v3g_model *m, v3g_state *s, bool want_lm, cudaStre
     MkCfg mc;
     mc.slots = s->mk_slots;
     mc.xr_bytes = s->mk_xr;
-    mc.part = s->host.mk_part;
-    mc.cnt = s->host.mk_cnt;
-    switch (m->host.D) {
-        case 16: return cudaLaunchKernelEx(&cfg, k_decode<16>, mdv, sdv, phases, n, scale, mc);
-        case 32: return cudaLaunchKernelEx(&cfg, k_decode<32>, mdv, sdv, phases, n, scale, mc);
-        case 64: return cudaLaunchKernelEx(&cfg, k_decode<64>, mdv, sdv, phases, n, scale, mc);
-        default: return cudaLaunchKernelEx(&cfg, k_decode<128>, mdv, sdv, phases, n, scale, mc);
-    }
+    mc.ph_off = s->mk_ph_off;
+    mc.lite_off = s->mk_lite_off;
+    mc.part_off = s->mk_part_off;
+    mc.ring_off = s->mk_ring_off;
+    mc.bar_off = s->mk_bar_off;
+    mc.lite = static_cast<const MkLite *>(s->mk_lite);
+    return cudaLaunchKernelEx(&cfg, reinterpret_cast<MkKernel>(s->mk_fn), mdv, sdv, phases, n, scale, mc);
 }
 
 // Kernel sequence of one decode step.  Every launch after the first carries programmatic stream serialization:
