@@ -135,6 +135,18 @@ V3G_API int v3g_seq_info(v3g_state *s, uint32_t b, v3g_seq_info_t *info, int64_t
 V3G_API int v3g_dequant(const v3g_model *m, uint32_t tensor_id, float *dev_out, void *stream);
 V3G_API int v3g_gemv(const v3g_model *m, uint32_t tensor_id, const float *dev_x, uint32_t batch, float *dev_y, void *stream);
 
+/* Greedy (first-maximum) token of each of `rows` logit rows (row b at dev_logits + b * ld, `vocab` entries, NaN
+ * never selected), written to dev_tokens[rows] -- the selection v3g_step makes, for callers that hold logits but
+ * may not allocate device memory (their framework's allocator owns the device memory, or cudaMalloc's implicit
+ * device synchronisation is not acceptable in their token loop).  It has no counterpart in the reference.
+ * Allocates nothing: its scratch is a fixed device array of V3G_NOALLOC_MAX_ROWS 8-byte keys that every GPU loading
+ * the library holds until exit; more rows fail with V3G_E_LIMIT.  It runs on the current device; its first call
+ * on a device looks up the array's device address, so make that first call before any stream capture.  All calls
+ * share the array (cleared at the start of each call): calls that overlap on the GPU race. */
+#define V3G_NOALLOC_MAX_ROWS 4096
+V3G_API int v3g_argmax_noalloc(const float *dev_logits, uint32_t rows, uint32_t vocab, uint64_t ld, int32_t *dev_tokens,
+                               void *stream);
+
 V3G_API const char *v3g_error_string(int code);
 V3G_API const char *v3g_last_error(void);   /* detail of the last failure on this thread */
 

@@ -926,3 +926,6 @@ extern "C" const char *v3g_error_string(int code) {
 }
 
 extern "C" const char *v3g_last_error(void) { return g_err.c_str(); }
+
+// failure report for entry points defined in other translation units
+int v3g_fail(int code, const std::string &msg) { return fail(code, msg); }

@@ -52,6 +52,9 @@ struct v3g_state {
     std::string last_error;
 };
 
+// records msg as this thread's v3g_last_error() and returns code
+int v3g_fail(int code, const std::string &msg);
+
 namespace v3g {
 int repack_matrix(MatW &w, const uint8_t *dev_src0, const uint8_t *dev_src1, int fmt, int src_rows, int cols,
                   int rowmap, int head_dim, uint8_t *dst, cudaStream_t st);
