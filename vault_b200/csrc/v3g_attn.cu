@@ -14,7 +14,9 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const ModelDev *mp, c
     griddep_wait();
     griddep_launch();
     const int64_t pos = __ldcg(&sp->step->pos);
-    attn_item<D>(*mp, *sp, layer, scale, blockIdx.x, blockIdx.y, blockIdx.z, pos, sm, blockDim.x);
+    (void)mp;
+    const KeySpan ks = key_span(*sp, blockIdx.z, pos);
+    attn_item<D>(*sp, ks, layer, scale, blockIdx.x, blockIdx.y, blockIdx.z, pos, sm, blockDim.x);
 }
 
 // greedy next token = first index of the largest logit (v3_argmax, runtime/vault3.c:3198-3202; torch.argmax):

@@ -17,8 +17,8 @@ struct KeySpan {   // visible keys of one (sequence, step)
     int n_sk, n_seg, n_prev, n_cur, total, par, bank_par;
 };
 
-__device__ __forceinline__ KeySpan key_span(const ModelDev &m, const StateDev &s, int b, int64_t pos) {
-    const int W = m.W, c = (int)(pos % W);
+__device__ __forceinline__ KeySpan key_span(const StateDev &s, int b, int64_t pos) {
+    const int W = s.W, c = (int)(pos % W);
     const SeqCtl &q = s.seq[b];
     KeySpan k;
     const int n_pin = __ldcg(&q.n_pin), seg_on = __ldcg(&q.seg_on), budget = __ldcg(&q.seg_budget);
@@ -66,13 +66,12 @@ struct AttnSmem {
 // All K and V rows of the chunk are staged in shared memory with cp.async (one round trip), two threads score a
 // key (half a head vector each), one warp per head forms the chunk's softmax pieces, and each thread accumulates
 // (head, dim) outputs.  The CTA writes an unnormalised partial (o, m, l); the last CTA of (b, g) merges the
-// partials in split order into s.attn.  Returns false when the split is empty.
+// partials in split order into s.attn.  ks = key_span(s, b, pos).  Returns false when the split is empty.
 template <int D>
-__device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float scale, int split, int g, int b,
+__device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float scale, int split, int g, int b,
                           int64_t pos, AttnSmem<D> &sm, int nt) {
     constexpr int KP = D + 8, CH = D / 8;
-    const int H = m.H, grp = H / m.G;
-    const KeySpan ks = key_span(m, s, b, pos);
+    const int H = s.H, G = s.G, grp = H / G;
     const int n_splits = (ks.total + ATT_KPC - 1) / ATT_KPC;
     if (split >= n_splits) return false;
     const int j0 = split * ATT_KPC, nk = min(ATT_KPC, ks.total - j0);
@@ -91,7 +90,7 @@ __device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float
         const int hr = idx / D, dd = idx - hr * D;
         const size_t qo = ((size_t)b * H + g * grp + hr) * D + dd;
         sm.q[1][hr][dd] = __ldcg(&s.q_cur[qo]);
-        sm.q[0][hr][dd] = pos >= m.W ? __ldcg(&s.q_far[qo]) : 0.f;
+        sm.q[0][hr][dd] = pos >= s.W ? __ldcg(&s.q_far[qo]) : 0.f;
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     sync_threads(nt);
@@ -169,7 +168,7 @@ __device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float
         sync_threads(nt);
         return true;
     }
-    float *part = s.att_part + ((((size_t)b * m.G + g) * s.max_splits + split) * grp) * (D + 2);
+    float *part = s.att_part + ((((size_t)b * G + g) * s.max_splits + split) * grp) * (D + 2);
     for (int idx = tid; idx < grp * D; idx += nt) {
         const int hr = idx / D, dd = idx - hr * D;
         float o = 0.f;
@@ -183,11 +182,11 @@ __device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float
     }
     __threadfence();
     sync_threads(nt);
-    if (tid == 0) sm.last = atomicAdd(&s.att_cnt[b * m.G + g], 1u) == (uint32_t)(n_splits - 1);
+    if (tid == 0) sm.last = atomicAdd(&s.att_cnt[b * G + g], 1u) == (uint32_t)(n_splits - 1);
     sync_threads(nt);
     if (sm.last) {
         __threadfence();
-        const float *p0 = s.att_part + (((size_t)b * m.G + g) * s.max_splits) * grp * (D + 2);
+        const float *p0 = s.att_part + (((size_t)b * G + g) * s.max_splits) * grp * (D + 2);
         for (int idx = tid; idx < grp * D; idx += nt) {
             const int hr = idx / D, dd = idx - hr * D;
             float M = -INFINITY;
@@ -201,7 +200,7 @@ __device__ bool attn_item(const ModelDev &m, const StateDev &s, int layer, float
             }
             s.attn[((size_t)b * H + g * grp + hr) * D + dd] = O / L;
         }
-        if (tid == 0) s.att_cnt[b * m.G + g] = 0u;
+        if (tid == 0) s.att_cnt[b * G + g] = 0u;
     }
     sync_threads(nt);
     return true;

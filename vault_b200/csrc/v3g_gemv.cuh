@@ -334,16 +334,12 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         }
         convert(act, b, h, n, v, w);
     }
-    // zero the padding columns, row B (read by the lanes of absent batch rows) and the block sums of absent rows /
-    // padding blocks
+    // zero the padding columns and the block sums of padding blocks (tiles may extend past K).  Absent batch rows
+    // (b >= B) are left as they are: their tensor-core columns are computed and never read.
     const int kp = a.kpx, pad = kp - nb * 32;
     for (int idx = tid; idx < a.B * pad; idx += nt) xs[(size_t)(idx / pad) * kp + nb * 32 + idx % pad] = 0;
-    for (int idx = tid; idx < kp / 2; idx += nt) reinterpret_cast<uint32_t *>(xs + (size_t)a.B * kp)[idx] = 0u;
     if (BSUM)
-        for (int idx = tid; idx < a.nblk * GEMV_MB; idx += nt) {
-            const int blk = idx / GEMV_MB, b = idx - blk * GEMV_MB;
-            if (b >= a.B || blk >= nb) bsum[idx] = 0.f;
-        }
+        for (int idx = nb * GEMV_MB + tid; idx < a.nblk * GEMV_MB; idx += nt) bsum[idx] = 0.f;
     sync_threads(nt);
 }
 

@@ -35,11 +35,12 @@ constexpr int MK_WARPS = GEMV_THREADS / 32;            // consumer warps
 constexpr int MK_CT = MK_WARPS * 32;                    // consumer threads (named-barrier count)
 constexpr int MK_THREADS = MK_CT + 32;                  // + the producer warp
 constexpr int MK_MAX_SLOTS = 16;
-constexpr int MK_CHUNK = 4;                             // tiles per chunk (F32: 1)
-constexpr int MK_SLOT_BYTES = MK_CHUNK * 576;           // 4 Q4_0 / Q8_0 / 16-bit tiles or 1 F32 tile
+constexpr int MK_CHUNK = 8;                             // tiles per chunk (F32: 3)
+constexpr int MK_GROUP = 4;                             // tiles computed together (register budget)
+constexpr int MK_SLOT_BYTES = MK_CHUNK * 576;           // 8 Q4_0 / Q8_0 / 16-bit tiles or 3 F32 tiles
 constexpr uint32_t MK_WAIT_LIMIT = 1u << 22;
 
-__host__ __device__ constexpr int mk_cap(int fmt) { return fmt == FMT_F32 ? 1 : MK_CHUNK; }
+__host__ __device__ constexpr int mk_cap(int fmt) { return fmt == FMT_F32 ? MK_SLOT_BYTES / 1536 : MK_CHUNK; }
 
 // full description of one phase (read by the CTA from a shared-memory copy while the phase runs)
 struct alignas(16) MkPhase {
@@ -68,8 +69,18 @@ static_assert(sizeof(MkLite) == 80, "MkLite is one 80-byte record");
 struct MkCfg {
     int slots;            // ring depth per consumer warp
     int xr_bytes;         // activation / attention region at the start of dynamic shared memory
-    int ph_off, lite_off, part_off, ring_off, bar_off;   // shared-memory offsets (bytes); bar_off: full, then empty
+    int ph_off, lite_off, part_off, misc_off, ring_off, bar_off;   // shared-memory offsets (bytes); bar_off: full,
+                                                                    // then empty barriers
     const MkLite *lite;   // global copy of the lite table (n_phases records)
+};
+
+// per-step constants every phase reads, copied to shared memory once at kernel start: the state descriptor, each
+// sequence's visible key span, the RoPE rows of positions c and W + c, and the step position
+struct alignas(16) MkMisc {
+    StateDev sd;
+    KeySpan ks[GEMV_MB];
+    float rope[2][128];
+    int64_t pos;
 };
 
 // shared-memory record of the split row tiles of one phase: per warp, a head piece (row tile begun by an earlier
@@ -207,8 +218,8 @@ __device__ __forceinline__ void mk_emit(const Epi &epi, int B, int si, int r, in
 // ---------------------------------------------------------------------------------------------------------------
 // tile arithmetic on shared-memory chunks
 // ---------------------------------------------------------------------------------------------------------------
-// Activation rows: xq = row min(g, B) of the converted activations + 2t (row B is zero), so absent batch rows
-// contribute nothing without a select.  bq = bsum + 2t.  Both are indexed by the k tile.
+// Activation rows: xq = row g of the converted activations + 2t (row 0 for lanes of absent batch rows g >= B: the
+// tensor-core columns they feed are never read), bq = bsum + 2t.  Both are indexed by the k tile.
 
 // one tile at tb (shared memory) with k tile kt, accumulated into acc (rows g, g+8 x batch 2t, 2t+1)
 template <int FMT>
@@ -269,11 +280,11 @@ __device__ __forceinline__ void mk_tile(const uint8_t *tb, int kt, const uint16_
     }
 }
 
-// a full chunk whose MK_CHUNK tiles lie in one row tile: every shared load first, then the tensor-core chains
+// MK_GROUP consecutive tiles of one row tile: every shared load first, then the tensor-core chains
 template <int FMT>
 __device__ __forceinline__ void mk_chunk_fast(const uint8_t *sb, int kt, const uint16_t *xq, const float *bq, int lane,
                                               float (&acc)[4]) {
-    constexpr int TB = tile_bytes(FMT), TK = tile_k(FMT), NS = TK / 16, N = MK_CHUNK;
+    constexpr int TB = tile_bytes(FMT), TK = tile_k(FMT), NS = TK / 16, N = MK_GROUP;
     const int g = lane >> 2;
     const uint16_t *xk = xq + kt * TK;
     uint4 q[N];
@@ -419,8 +430,12 @@ __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkR
         }
         if (!R.dead) {
             if (n == MK_CHUNK && kt + MK_CHUNK <= KT && (fa ? FA : FB) != FMT_F32) {   // one row, whole chunk
-                if (fa) mk_chunk_fast<FA == FMT_F32 ? FMT_Q8 : FA>(sb, kt, xq, bq, lane, acc);
-                else mk_chunk_fast<FB == FMT_F32 ? FMT_Q8 : FB>(sb, kt, xq, bq, lane, acc);
+                constexpr int TA = tile_bytes(FA == FMT_F32 ? FMT_Q8 : FA), TBb = tile_bytes(FB == FMT_F32 ? FMT_Q8 : FB);
+#pragma unroll
+                for (int g0 = 0; g0 < MK_CHUNK; g0 += MK_GROUP) {
+                    if (fa) mk_chunk_fast<FA == FMT_F32 ? FMT_Q8 : FA>(sb + g0 * TA, kt + g0, xq, bq, lane, acc);
+                    else mk_chunk_fast<FB == FMT_F32 ? FMT_Q8 : FB>(sb + g0 * TBb, kt + g0, xq, bq, lane, acc);
+                }
             } else {
                 for (int i = 0; i < n; ++i) {   // chunk ends a range / segment, or crosses row tiles
                     if (i > 0 && kt == 0) {
@@ -462,13 +477,13 @@ __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkR
 }
 
 template <int FA, int FB>
-__device__ __forceinline__ void mk_consume_epi(const MkPhase &P, const ModelDev *mp, const StateDev *sp, MkRing &R,
+__device__ __forceinline__ void mk_consume_epi(const MkPhase &P, const ModelDev *mp, const MkMisc &ms, MkRing &R,
                                                const MkLite *lite, int n_phases, int p, int cta, int G, int wi,
                                                const uint16_t *xq, const float *bq, const float *s_scale,
                                                MkPart &part, int *status, int lane) {
     switch (P.epi) {
         case MK_EPI_QKV: {
-            EpiQKV e{mp, sp, P.layer, P.bq, P.bk, P.bv};
+            EpiQKV e{mp, &ms.sd, P.layer, P.bq, P.bk, P.bv, ms.rope[0], ms.rope[1], ms.pos};
             mk_consume<FA, FB>(P, e, R, lite, n_phases, p, cta, G, wi, xq, bq, s_scale, part, status, lane);
             break;
         }
@@ -495,7 +510,7 @@ __device__ __forceinline__ void mk_consume_epi(const MkPhase &P, const ModelDev 
 // (empty barrier), until the stream ends; then waits (bounded) until its last copies have landed
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void mk_produce(const MkLite *lite, int n_phases, int c, int G, const MkCfg &cfg,
-                                           uint8_t *smem, int *status) {
+                                           uint8_t *smem, const StateDev *sp) {
     const int lane = threadIdx.x & 31;
     if (lane >= MK_WARPS) return;
     const int S = cfg.slots;
@@ -508,7 +523,7 @@ __device__ __forceinline__ void mk_produce(const MkLite *lite, int n_phases, int
     while (cur.p < n_phases) {
         if (round > 0 && !mbar_test(empty + slot * 8, (round - 1) & 1u)) {   // slot still in use
             if (++idle > MK_WAIT_LIMIT) {
-                atomicOr(status, STATUS_TIMEOUT);
+                atomicOr(&sp->step->status, STATUS_TIMEOUT);
                 break;
             }
             __nanosleep(32);
@@ -546,9 +561,8 @@ __device__ __forceinline__ void mk_fetch_phase(const MkPhase *phases, int p, int
 // of the step; a wait that exceeds its iteration limit records STATUS_TIMEOUT and returns (results then invalid)
 __device__ __forceinline__ void mk_grid_sync(unsigned int *bar, unsigned int target, int *status) {
     sync_threads(MK_CT);
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(bar, 1u);
+    if (threadIdx.x == 0) {   // release-add (the CTA's writes, ordered by the barrier above), then acquire-poll
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
         unsigned int v = 0;
         for (uint32_t spins = 0;; ++spins) {
             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
@@ -558,7 +572,6 @@ __device__ __forceinline__ void mk_grid_sync(unsigned int *bar, unsigned int tar
                 break;
             }
         }
-        __threadfence();
     }
     sync_threads(MK_CT);
 }
@@ -585,12 +598,33 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    const StateDev &st = *sp;
-    int *status = &st.step->status;
     if (warp == MK_WARPS) {   // weights are immutable: the producer streams from the very start
-        mk_produce(lite, n_phases, c, G, cfg, smem, status);
+        mk_produce(lite, n_phases, c, G, cfg, smem, sp);
         return;
     }
+    // per-step constants into shared memory (state descriptor, then position, key spans and RoPE rows)
+    MkMisc &misc = *reinterpret_cast<MkMisc *>(smem + cfg.misc_off);
+    griddep_wait();
+    static_assert(sizeof(StateDev) % 4 == 0, "word copy");
+    for (int i = threadIdx.x; i < (int)(sizeof(StateDev) / 4); i += MK_CT)
+        reinterpret_cast<uint32_t *>(&misc.sd)[i] = __ldcg(reinterpret_cast<const uint32_t *>(sp) + i);
+    const float *rope_tab = mp->rope;
+    const int rope_pos0 = mp->rope_pos0;
+    sync_threads(MK_CT);
+    const StateDev &st = misc.sd;
+    int *status = &st.step->status;
+    const int64_t pos = __ldcg(&st.step->pos);
+    if ((int)threadIdx.x < st.B) misc.ks[threadIdx.x] = key_span(st, threadIdx.x, pos);
+    {
+        const int cpos = (int)(pos % st.W);
+        for (int i = threadIdx.x; i < 2 * D; i += MK_CT) {
+            const int row = i / D;
+            const int64_t rp = (row ? st.W + cpos : cpos) - rope_pos0;
+            misc.rope[row][i - row * D] = __ldg(rope_tab + rp * D + (i - row * D));
+        }
+    }
+    if (threadIdx.x == 0) misc.pos = pos;
+    sync_threads(MK_CT);
     MkRing R;
     R.slots = cfg.slots;
     R.buf = smem + cfg.ring_off + (size_t)warp * cfg.slots * MK_SLOT_BYTES;
@@ -601,9 +635,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
     R.dead = false;
     mk_enter(lite, n_phases, c, G, warp, R.cons, 0);
     MkPart &part = *reinterpret_cast<MkPart *>(smem + cfg.part_off);
-    griddep_wait();
-    const int64_t pos = __ldcg(&st.step->pos);
-    const int n_kv = mp->G, ms = st.max_splits, Bst = st.B;
+    const int n_kv = st.G, ms = st.max_splits, Bst = st.B;
     unsigned int *gbar = st.bar;
     constexpr bool BSUM = fmt_int(FA) || fmt_int(FB);
     float *s_red = reinterpret_cast<float *>(smem);
@@ -615,14 +647,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
             const int n_items = Bst * n_kv * ms;
             for (int i = c; i < n_items; i += G) {
                 const int split = i % ms, g = (i / ms) % n_kv, b = i / (ms * n_kv);
-                attn_item<D>(*mp, st, P.layer, scale, split, g, b, pos, *reinterpret_cast<AttnSmem<D> *>(smem), MK_CT);
+                attn_item<D>(st, misc.ks[b], P.layer, scale, split, g, b, pos, *reinterpret_cast<AttnSmem<D> *>(smem),
+                             MK_CT);
             }
         } else {
             uint16_t *xs = reinterpret_cast<uint16_t *>(bsum + (BSUM ? P.a.nblk * GEMV_MB : 0));
             gemv_prologue<BSUM, 3>(P.a, xs, s_scale, s_red, bsum, MK_CT);
             const int g = lane >> 2, t = lane & 3;
-            const uint16_t *xq = xs + (g < P.a.B ? g : P.a.B) * P.a.kpx + 2 * t;
-            mk_consume_epi<FA, FB>(P, mp, sp, R, lite, n_phases, p, c, G, warp, xq, bsum + 2 * t, s_scale, part,
+            const uint16_t *xq = xs + (g < P.a.B ? g : 0) * P.a.kpx + 2 * t;   // absent rows: columns never read
+            mk_consume_epi<FA, FB>(P, mp, misc, R, lite, n_phases, p, c, G, warp, xq, bsum + 2 * t, s_scale, part,
                                    status, lane);
         }
         if (p + 1 < n_phases) {

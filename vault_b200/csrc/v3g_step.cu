@@ -133,23 +133,27 @@ struct EpiQKV {
     const StateDev *s;
     int layer;
     const float *bq, *bk, *bv;
+    // persistent kernel: the RoPE rows of positions c and W + c and the step position, held in shared memory
+    // (nullptr: read them from the model / state in global memory)
+    const float *rc_s = nullptr, *rf_s = nullptr;
+    int64_t pos_s = 0;
     // lane holds tile rows (g, g+8) = RoPE partners (i, i + D/2) of one head
     __device__ void operator()(int seg, int rt, int g, int b, float y0, float y1) const {
-        const int D = m->D, W = m->W, hd = D / 2;
+        const int D = s->D, W = s->W, hd = D / 2;
         const int head = rt / (D / TILE_ROWS), j = rt % (D / TILE_ROWS), i = 8 * j + g;
         const int r0 = head * D + i, r1 = r0 + hd;
-        const int64_t pos = s->step->pos;
+        const int64_t pos = rc_s ? pos_s : s->step->pos;
         const int c = (int)(pos % W), par = ring_par(pos, W);
-        const float *rc = rope_row(*m, c);
+        const float *rc = rc_s ? rc_s : rope_row(*m, c);
         const float cs = rc[i], sn = rc[hd + i];
         if (seg == 0) {
             const float a = y0 + bq[r0], bb = y1 + bq[r1];
-            float *qc = s->q_cur + ((size_t)b * m->H + head) * D;
+            float *qc = s->q_cur + ((size_t)b * s->H + head) * D;
             qc[i] = a * cs - bb * sn;
             qc[i + hd] = bb * cs + a * sn;
             if (pos >= W) {
-                const float *rf = rope_row(*m, W + c);
-                float *qf = s->q_far + ((size_t)b * m->H + head) * D;
+                const float *rf = rc_s ? rf_s : rope_row(*m, W + c);
+                float *qf = s->q_far + ((size_t)b * s->H + head) * D;
                 qf[i] = a * rf[i] - bb * rf[hd + i];
                 qf[i + hd] = bb * rf[i] + a * rf[hd + i];
             }
@@ -882,7 +886,8 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
     // shared memory: [x / attention region][2 phase descriptors][lite table][split pieces][rings][ring mbarriers]
     const size_t ph_off = xr, lite_off = ph_off + 2 * sizeof(MkPhase);
     const size_t part_off = (lite_off + ph.size() * sizeof(MkLite) + 15) / 16 * 16;
-    const size_t ring_off = (part_off + sizeof(MkPart) + 127) / 128 * 128;
+    const size_t misc_off = (part_off + sizeof(MkPart) + 15) / 16 * 16;
+    const size_t ring_off = (misc_off + sizeof(MkMisc) + 127) / 128 * 128;
     const long avail = (long)optin - (long)fattr.sharedSizeBytes - (long)ring_off;
     const long per_slot = (long)MK_WARPS * (MK_SLOT_BYTES + 16);   // buffer + full and empty barriers
     int slots = avail > 0 ? (int)(avail / per_slot) : 0;
@@ -927,6 +932,7 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
     s->mk_ph_off = (int)ph_off;
     s->mk_lite_off = (int)lite_off;
     s->mk_part_off = (int)part_off;
+    s->mk_misc_off = (int)misc_off;
     s->mk_ring_off = (int)ring_off;
     s->mk_bar_off = (int)bar_off;
     s->mk_grid = m->n_sm;
@@ -959,6 +965,7 @@ cudaError_t launch_mega(const v3g_model *m, v3g_state *s, bool want_lm, cudaStre
     mc.ph_off = s->mk_ph_off;
     mc.lite_off = s->mk_lite_off;
     mc.part_off = s->mk_part_off;
+    mc.misc_off = s->mk_misc_off;
     mc.ring_off = s->mk_ring_off;
     mc.bar_off = s->mk_bar_off;
     mc.lite = static_cast<const MkLite *>(s->mk_lite);
