@@ -30,6 +30,9 @@ sys.path.insert(0, HERE)
 PROMPT, DECODE = 128, 64
 REF_HOST = os.path.join(HERE, "oracle", "_ref", "vault3_host")
 METRIC = "decode tok/s (B=1, Q8_0, 128-token prompt, 64 greedy steps)"
+# DRAM bytes (read + write) of one k_decode launch on config 1, from the ncu capture summarised in
+# profiles/k_decode_q8_0_config1.md
+TRAFFIC = 1647798680
 
 
 def model_path(fmt: str = "q8_0") -> str:
@@ -229,20 +232,27 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_reduce(e2e_dec, op=dist.ReduceOp.MAX)
     e2e_value = world * DECODE * len(e2e) / float(e2e_dec.item())
 
-    # dominant kernel: the decode GEMV, timed alone on the engine stream (lm head, 151936 x 1536 Q8_0)
-    lm_bytes = m.info.lm_head_bytes + 1536 * 4 + 151936 * 4
-    x = torch.randn(1, 1536, device=ids.device)
-    y = torch.empty(1, 151936, device=ids.device)
-    for _ in range(3):
-        _lib.check(L.v3g_gemv(m._h, 1, C.c_void_p(x.data_ptr()), 1, C.c_void_p(y.data_ptr()), sp), "gemv")
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 20
-    g0.record(stream)
-    for _ in range(reps):
-        _lib.check(L.v3g_gemv(m._h, 1, C.c_void_p(x.data_ptr()), 1, C.c_void_p(y.data_ptr()), sp), "gemv")
-    g1.record(stream)
-    torch.cuda.synchronize()
-    gemv_s = g0.elapsed_time(g1) / 1e3 / reps
+    # dominant kernel: the persistent decode kernel (all 28 layers + lm head of one token), timed alone on the
+    # engine stream at the mean decode position of the request (prompt + 32)
+    st.reset()
+    _lib.check(L.v3g_prefill(st._h, C.c_void_p(ids.data_ptr()), PROMPT, PROMPT, None, C.c_void_p(nxt.data_ptr()), sp),
+               "prefill")
+    _lib.check(L.v3g_generate(st._h, C.c_void_p(nxt.data_ptr()), DECODE // 2, C.c_void_p(out.data_ptr()), DECODE, sp),
+               "generate")
+    persistent = L.v3g_decode_pass(st._h, 1, sp) == 0
+    kernel_s = None
+    if persistent:
+        for _ in range(3):
+            _lib.check(L.v3g_decode_pass(st._h, 1, sp), "decode_pass")
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        g0.record(stream)
+        for _ in range(reps):
+            _lib.check(L.v3g_decode_pass(st._h, 1, sp), "decode_pass")
+        g1.record(stream)
+        torch.cuda.synchronize()
+        kernel_s = g0.elapsed_time(g1) / 1e3 / reps
+    st.reset()
 
     if rank != 0:
         return
@@ -253,15 +263,17 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
     n_tok = DECODE * args.steps
     value = world * n_tok / (dec_ms / 1e3)
     step_s = dec_ms / 1e3 / n_tok
-    # KV bytes read per decode step (bf16 K and V of every visible key, all layers): mean context 128 + 32
+    # KV bytes read per decode step (fp16 K and V of every visible key, 2 KV heads x 128, all layers): mean
+    # context 128 + 32 keys
     kv_bytes = 28 * 2 * 2 * 128 * 2 * (PROMPT + DECODE // 2)
     step_bytes = m.info.step_weight_bytes + kv_bytes
-    achieved = lm_bytes / gemv_s / 1e9
+    kernel_bytes = step_bytes   # one launch of the persistent kernel reads every weight once plus the KV rows
+    achieved = kernel_bytes / kernel_s / 1e9 if kernel_s else None
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
-        "dtype": "q8_0 weights; fp16/bf16 mma operands, fp32 accumulate; bf16 KV cache",
+        "dtype": "q8_0 weights; fp16 tensor-core operands, fp32 accumulate; fp16 KV cache",
         "data": "synthetic (random-init N(0,0.02) weights, seeded uniform prompt ids)",
         "config": {"workload": "BASELINE config 1: VAULT v3 1.54B Q8_0, B=1, 128-token prompt + 64 greedy decode steps",
                    "global_batch": world, "seq_len": PROMPT + DECODE, "parallelism": f"sequence replicas x{world}",
@@ -269,19 +281,27 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
         "prefill_tok_s": round(world * PROMPT * args.steps / (pf_ms / 1e3), 2),
         "ms_per_token": round(1e3 * step_s, 4),
         "gpu_launches": None,
-        "roofline": {"kernel": "gemv_kernel (lm head 151936x1536 Q8_0, alone)", "bound": "hbm",
-                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                     "peak_source": peak_kind, "traffic": None,
-                     "algorithmic_bytes_per_launch": int(lm_bytes), "avg_launch_us": round(gemv_s * 1e6, 2)},
+        "roofline": {"kernel": "k_decode (persistent: 28 layers + lm head of one token, timed alone)", "bound": "hbm",
+                     "achieved": round(achieved, 1) if achieved else None, "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4) if achieved else None,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)", "traffic": TRAFFIC,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_decode launch "
+                                       "(profiles/k_decode_q8_0_config1.md)",
+                     "algorithmic_bytes_per_launch": int(kernel_bytes),
+                     "avg_launch_us": round(kernel_s * 1e6, 2) if kernel_s else None},
         "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_bytes / step_s / 1e9, 1),
                           "peak": hbm, "unit": "GB/s", "frac": round(step_bytes / step_s / 1e9 / hbm, 4)},
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * (PROMPT + DECODE),
                 "d2h_bytes_per_step": 4 * (PROMPT + DECODE)},
         "clocks": clk.summary(),
     }
-    # launches per decode token: 1 begin + L x (QKV gemv, attention, O gemv, gate/up gemv, down gemv) + lm gemv
-    # + argmax + advance
-    line["gpu_launches"] = args.steps * ((PROMPT + DECODE) * (2 + 5 * 28) + DECODE + 1) + 2 * args.steps
+    # launches inside the timed region, per request: every token runs k_begin + k_decode (persistent) + k_finish,
+    # plus k_argmax_partial when its next token is needed (the last prompt token and every decode step)
+    if persistent:
+        per_request = (PROMPT + DECODE) * 3 + (DECODE + 1)
+    else:   # per-phase kernels: k_begin, 5 per layer, lm gemv (with lm head) and k_finish
+        per_request = (PROMPT + DECODE) * (2 + 5 * 28) + (DECODE + 1) * 2
+    line["gpu_launches"] = args.steps * per_request
     if world == 1 and os.path.exists(REF_HOST) and not args.no_cpu_baseline:
         try:
             r = run_reference_host(path, os.cpu_count() or 1)

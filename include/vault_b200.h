@@ -134,6 +134,10 @@ V3G_API int v3g_seq_info(v3g_state *s, uint32_t b, v3g_seq_info_t *info, int64_t
 /* Kernel-level entry points (tests and the kernel sweep).  tensor_id uses the VLT3 ids of tools/vlt3.py:34-57. */
 V3G_API int v3g_dequant(const v3g_model *m, uint32_t tensor_id, float *dev_out, void *stream);
 V3G_API int v3g_gemv(const v3g_model *m, uint32_t tensor_id, const float *dev_x, uint32_t batch, float *dev_y, void *stream);
+/* One launch of the persistent decode kernel (every layer of the current position, plus the lm head when want_lm)
+ * on a state whose steps use it, without the step's token bookkeeping: for timing the kernel alone.  It rewrites
+ * the current position's activations and KV rows, so reset the state before decoding again. */
+V3G_API int v3g_decode_pass(v3g_state *s, int want_lm, void *stream);
 
 /* Greedy (first-maximum) token of each of `rows` logit rows (row b at dev_logits + b * ld, `vocab` entries, NaN
  * never selected), written to dev_tokens[rows] -- the selection v3g_step makes, for callers that hold logits but

@@ -884,6 +884,15 @@ static const MatW *find_mat(const v3g_model *m, uint32_t id) {
     return nullptr;
 }
 
+extern "C" int v3g_decode_pass(v3g_state *s, int want_lm, void *stream) {
+    if (!s) return fail(V3G_E_ARG, "null state");
+    if (!s->use_mega) return fail(V3G_E_UNSUPPORTED, "the state does not run the persistent decode kernel");
+    cudaStream_t st = (cudaStream_t)stream;
+    CUDA_TRY(cudaMemsetAsync(s->host.bar, 0, sizeof(unsigned int), st));   // grid-barrier counter, as k_begin does
+    CUDA_TRY(launch_mega(s->m, s, want_lm != 0, st));
+    return V3G_OK;
+}
+
 extern "C" int v3g_dequant(const v3g_model *m, uint32_t tensor_id, float *dev_out, void *stream) {
     if (!m || !dev_out) return fail(V3G_E_ARG, "null argument");
     const MatW *w = find_mat(m, tensor_id);
