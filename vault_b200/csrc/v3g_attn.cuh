@@ -63,9 +63,9 @@ struct AttnSmem {
 };
 
 // One work item = ATT_KPC keys of one (sequence b, KV head g) for its `grp` query heads, run by one CTA.
-// All K and V rows of the chunk are staged in shared memory with cp.async (one round trip), two threads score a
-// key (half a head vector each), one warp per head forms the chunk's softmax pieces, and each thread accumulates
-// (head, dim) outputs.  The CTA writes an unnormalised partial (o, m, l); the last CTA of (b, g) merges the
+// All K and V rows of the chunk are staged in shared memory with cp.async (one round trip), up to four threads
+// score a key (a slice of the head vector each), one warp per head forms the chunk's softmax pieces, and every
+// thread accumulates a column pair of every head over a quarter of the keys.  The CTA writes an unnormalised partial (o, m, l); the last CTA of (b, g) merges the
 // partials in split order into s.attn.  ks = key_span(s, b, pos).  Returns false when the split is empty.
 template <int D>
 __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float scale, int split, int g, int b,
@@ -94,17 +94,19 @@ __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     sync_threads(nt);
-    // scores: threads (2j, 2j+1) take the two halves of key j
-    for (int base = 0; base < 2 * ATT_KPC; base += nt) {
-        const int j = (base + tid) >> 1, half = tid & 1;
+    // scores: QT adjacent threads share key j, each a DQ-wide slice of the head vector; slices meet by shuffles
+    {
+        int QT = nt / ATT_KPC < D / 8 ? nt / ATT_KPC : D / 8;   // 1, 2 or 4 threads per key
+        QT = QT >= 4 ? 4 : (QT >= 2 ? 2 : 1);
+        const int DQ = D / QT;
+        const int j = tid / QT, qi = tid - j * QT;
         float acc[ATT_GRP_MAX];
 #pragma unroll
         for (int hr = 0; hr < ATT_GRP_MAX; ++hr) acc[hr] = 0.f;
-        if (j < nk) {
+        if (j < nk && j < ATT_KPC) {
             const float(*qs)[D] = sm.q[sm.far[j] ? 0 : 1];
-            const kv_t *kr = &sm.k[j * KP + half * (D / 2)];
-#pragma unroll
-            for (int d0 = 0; d0 < D / 2; d0 += 8) {
+            const kv_t *kr = &sm.k[j * KP + qi * DQ];
+            for (int d0 = 0; d0 < DQ; d0 += 8) {
                 const uint4 raw = *reinterpret_cast<const uint4 *>(kr + d0);
                 const __half2 *k2 = reinterpret_cast<const __half2 *>(&raw);
                 float kf[8];
@@ -114,28 +116,29 @@ __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float
                     kf[2 * e] = f.x;
                     kf[2 * e + 1] = f.y;
                 }
-                const int dd = half * (D / 2) + d0;
+                const int dd = qi * DQ + d0;
 #pragma unroll
                 for (int hr = 0; hr < ATT_GRP_MAX; ++hr) {
                     if (hr < grp) {
                         const float4 qa = *reinterpret_cast<const float4 *>(&qs[hr][dd]);
                         const float4 qb = *reinterpret_cast<const float4 *>(&qs[hr][dd + 4]);
-                        acc[hr] = fmaf(qa.x, kf[0], acc[hr]);
-                        acc[hr] = fmaf(qa.y, kf[1], acc[hr]);
-                        acc[hr] = fmaf(qa.z, kf[2], acc[hr]);
-                        acc[hr] = fmaf(qa.w, kf[3], acc[hr]);
-                        acc[hr] = fmaf(qb.x, kf[4], acc[hr]);
-                        acc[hr] = fmaf(qb.y, kf[5], acc[hr]);
-                        acc[hr] = fmaf(qb.z, kf[6], acc[hr]);
-                        acc[hr] = fmaf(qb.w, kf[7], acc[hr]);
+                        float s0 = qa.x * kf[0], s1 = qa.y * kf[1];
+                        s0 = fmaf(qa.z, kf[2], s0);
+                        s1 = fmaf(qa.w, kf[3], s1);
+                        s0 = fmaf(qb.x, kf[4], s0);
+                        s1 = fmaf(qb.y, kf[5], s1);
+                        s0 = fmaf(qb.z, kf[6], s0);
+                        s1 = fmaf(qb.w, kf[7], s1);
+                        acc[hr] += s0 + s1;
                     }
                 }
             }
         }
 #pragma unroll
         for (int hr = 0; hr < ATT_GRP_MAX; ++hr) {
-            const float tot = acc[hr] + __shfl_xor_sync(0xffffffffu, acc[hr], 1);
-            if (hr < grp && half == 0 && j < nk) sm.p[hr][j] = tot * scale;
+            float tot = acc[hr];
+            for (int o = 1; o < QT; o <<= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+            if (hr < grp && qi == 0 && j < nk && j < ATT_KPC) sm.p[hr][j] = tot * scale;
         }
     }
     sync_threads(nt);
@@ -157,13 +160,48 @@ __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float
         }
     }
     sync_threads(nt);
+    // output: thread (column pair c2, key quarter kq) sums its keys for every head; quarters meet in shared memory
+    // (the K rows are no longer needed: their space holds the quarter sums)
+    {
+        constexpr int P2 = D / 2;
+        const int KQ = nt / P2 >= 4 ? 4 : (nt / P2 >= 2 ? 2 : 1);
+        const int c2 = tid % P2, kq = tid / P2;
+        float o[ATT_GRP_MAX][2];
+#pragma unroll
+        for (int hr = 0; hr < ATT_GRP_MAX; ++hr) o[hr][0] = o[hr][1] = 0.f;
+        if (kq < KQ) {
+            for (int jj = kq; jj < nk; jj += KQ) {
+                const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&sm.v[jj * D + 2 * c2]));
+#pragma unroll
+                for (int hr = 0; hr < ATT_GRP_MAX; ++hr) {
+                    if (hr < grp) {
+                        const float pj = sm.p[hr][jj];
+                        o[hr][0] = fmaf(pj, v.x, o[hr][0]);
+                        o[hr][1] = fmaf(pj, v.y, o[hr][1]);
+                    }
+                }
+            }
+        }
+        sync_threads(nt);   // every thread is done with the K rows
+        float *red = reinterpret_cast<float *>(sm.k);   // [KQ][grp][D]
+        if (kq < KQ) {
+#pragma unroll
+            for (int hr = 0; hr < ATT_GRP_MAX; ++hr)
+                if (hr < grp) *reinterpret_cast<float2 *>(&red[(kq * grp + hr) * D + 2 * c2]) = make_float2(o[hr][0], o[hr][1]);
+        }
+        sync_threads(nt);
+        for (int idx = tid; idx < grp * D; idx += nt) {
+            const int hr = idx / D, dd = idx - hr * D;
+            float acc = 0.f;
+            for (int q = 0; q < KQ; ++q) acc += red[(q * grp + hr) * D + dd];
+            sm.q[0][hr][dd] = acc;   // the query rows are no longer needed either: reuse them for the output
+        }
+        sync_threads(nt);
+    }
     if (n_splits == 1) {   // the whole span in one item: normalise and write the head outputs directly
         for (int idx = tid; idx < grp * D; idx += nt) {
             const int hr = idx / D, dd = idx - hr * D;
-            float o = 0.f;
-#pragma unroll 8
-            for (int j = 0; j < nk; ++j) o = fmaf(sm.p[hr][j], kv2f(sm.v[j * D + dd]), o);
-            s.attn[((size_t)b * H + g * grp + hr) * D + dd] = o / sm.l[hr];
+            s.attn[((size_t)b * H + g * grp + hr) * D + dd] = sm.q[0][hr][dd] / sm.l[hr];
         }
         sync_threads(nt);
         return true;
@@ -171,10 +209,7 @@ __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float
     float *part = s.att_part + ((((size_t)b * G + g) * s.max_splits + split) * grp) * (D + 2);
     for (int idx = tid; idx < grp * D; idx += nt) {
         const int hr = idx / D, dd = idx - hr * D;
-        float o = 0.f;
-#pragma unroll 8
-        for (int j = 0; j < nk; ++j) o = fmaf(sm.p[hr][j], kv2f(sm.v[j * D + dd]), o);
-        part[hr * (D + 2) + dd] = o;
+        part[hr * (D + 2) + dd] = sm.q[0][hr][dd];
     }
     if (tid < grp) {
         part[tid * (D + 2) + D] = sm.m[tid];

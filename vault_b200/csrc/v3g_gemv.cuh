@@ -267,11 +267,13 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         }
     }
     sync_threads(nt);
-    if (tid < a.B) {
+    // every thread derives the multiplier of the rows it converts (same arithmetic everywhere: no second sync);
+    // threads b < B also publish the scale the GEMV undoes
+    auto row_mul = [&](int b, float &scale) {
         float S = 0.f, Mx = 0.f;
         for (int w = 0; w < nw; ++w) {
-            S += s_red[tid * 8 + w];
-            Mx = fmaxf(Mx, s_red[64 + tid * 8 + w]);
+            S += s_red[b * 8 + w];
+            Mx = fmaxf(Mx, s_red[64 + b * 8 + w]);
         }
         const float inv = norm ? 1.0f / sqrtf(S / (float)a.K + a.eps) : 1.0f;
         float e = 0.f;
@@ -280,10 +282,14 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
             frexpf(Mx * inv, &ex);
             e = (float)(ex - 14);   // largest |x| scaled into (2^13, 2^14]
         }
-        s_red[128 + tid] = inv * exp2f(-e);   // multiplier applied before rounding to 16 bits
-        s_scale[tid] = exp2f(e);
+        scale = exp2f(e);
+        return inv * exp2f(-e);   // multiplier applied before rounding to 16 bits
+    };
+    if (tid < a.B) {
+        float sc;
+        (void)row_mul(tid, sc);
+        s_scale[tid] = sc;
     }
-    sync_threads(nt);
     auto convert = [&](bool act, int b, int h, int n, const float (&v)[16], const float (&w)[16]) {
         float bs = 0.f;
         if (act) {
@@ -293,7 +299,8 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
                 for (int j = 0; j < 16; ++j)
                     if (j < n) f[j] = v[j];
             }
-            const float mul = s_red[128 + b];
+            float unused;
+            const float mul = row_mul(b, unused);
             uint32_t hw[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {

@@ -39,6 +39,7 @@ constexpr int MK_CHUNK = 8;                             // tiles per chunk (F32:
 constexpr int MK_GROUP = 4;                             // tiles computed together (register budget)
 constexpr int MK_SLOT_BYTES = MK_CHUNK * 576;           // 8 Q4_0 / Q8_0 / 16-bit tiles or 3 F32 tiles
 constexpr uint32_t MK_WAIT_LIMIT = 1u << 22;
+constexpr int MK_OWN_TILES = 4;                         // residual / bias row tiles a CTA keeps in shared memory
 
 __host__ __device__ constexpr int mk_cap(int fmt) { return fmt == FMT_F32 ? MK_SLOT_BYTES / 1536 : MK_CHUNK; }
 
@@ -71,6 +72,7 @@ struct MkCfg {
     int xr_bytes;         // activation / attention region at the start of dynamic shared memory
     int ph_off, lite_off, part_off, misc_off, ring_off, bar_off;   // shared-memory offsets (bytes); bar_off: full,
                                                                     // then empty barriers
+    int x_rtiles, x_ld;   // row tiles of the residual stream (d / 16, rounded up) and its row stride (d)
     const MkLite *lite;   // global copy of the lite table (n_phases records)
 };
 
@@ -81,6 +83,34 @@ struct alignas(16) MkMisc {
     KeySpan ks[GEMV_MB];
     float rope[2][128];
     int64_t pos;
+    // the residual rows x[b, 16 r .. 16 r + 15] of the row tiles r in [own_r0, own_r0 + own_n) that this CTA owns in
+    // the O and down phases (they own the same d-row tiles): kept here so the residual add reads no global memory
+    float xown[MK_OWN_TILES][16][GEMV_MB];
+    int own_r0, own_n;
+    // biases of the CTA's QKV row tiles, refreshed at each QKV phase (16 per row tile, tile-row order)
+    float qkv_bias[MK_OWN_TILES][16];
+    int bias_r0, bias_n;
+};
+
+// residual epilogue of the persistent kernel: x[b, row] += y, from the CTA's shared copy when it owns the row tile
+struct MkEpiResid {
+    float *x;
+    int ld, rows;
+    float (*xown)[16][GEMV_MB];
+    int r0, n;
+    __device__ void operator()(int, int rt, int g, int b, float y0, float y1) const {
+        const int r = TILE_ROWS * rt + g, rl = rt - r0;
+        if (rl >= 0 && rl < n) {
+            const float v0 = xown[rl][g][b] + y0, v1 = xown[rl][g + 8][b] + y1;
+            xown[rl][g][b] = v0;
+            xown[rl][g + 8][b] = v1;
+            if (r < rows) x[(size_t)b * ld + r] = v0;
+            if (r + 8 < rows) x[(size_t)b * ld + r + 8] = v1;
+        } else {   // L1-bypassing read: other SMs updated x in earlier phases
+            if (r < rows) x[(size_t)b * ld + r] = __ldcg(&x[(size_t)b * ld + r]) + y0;
+            if (r + 8 < rows) x[(size_t)b * ld + r + 8] = __ldcg(&x[(size_t)b * ld + r + 8]) + y1;
+        }
+    }
 };
 
 // shared-memory record of the split row tiles of one phase: per warp, a head piece (row tile begun by an earlier
@@ -429,24 +459,34 @@ __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkR
             acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
         }
         if (!R.dead) {
-            if (n == MK_CHUNK && kt + MK_CHUNK <= KT && (fa ? FA : FB) != FMT_F32) {   // one row, whole chunk
-                constexpr int TA = tile_bytes(FA == FMT_F32 ? FMT_Q8 : FA), TBb = tile_bytes(FB == FMT_F32 ? FMT_Q8 : FB);
+            constexpr bool F32A = FA == FMT_F32, F32B = FB == FMT_F32;
+            const int tbytes = fa ? tile_bytes(FA) : tile_bytes(FB);
+            if (n == MK_CHUNK && kt + MK_CHUNK <= KT && !(fa ? F32A : F32B)) {   // whole chunk in one row tile
 #pragma unroll
                 for (int g0 = 0; g0 < MK_CHUNK; g0 += MK_GROUP) {
-                    if (fa) mk_chunk_fast<FA == FMT_F32 ? FMT_Q8 : FA>(sb + g0 * TA, kt + g0, xq, bq, lane, acc);
-                    else mk_chunk_fast<FB == FMT_F32 ? FMT_Q8 : FB>(sb + g0 * TBb, kt + g0, xq, bq, lane, acc);
+                    if (fa) mk_chunk_fast<F32A ? FMT_Q8 : FA>(sb + g0 * tbytes, kt + g0, xq, bq, lane, acc);
+                    else mk_chunk_fast<F32B ? FMT_Q8 : FB>(sb + g0 * tbytes, kt + g0, xq, bq, lane, acc);
                 }
-            } else {
-                for (int i = 0; i < n; ++i) {   // chunk ends a range / segment, or crosses row tiles
-                    if (i > 0 && kt == 0) {
-                        flush();
-                        cur_r = ++r;
-                        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-                    }
-                    if (fa) mk_tile<FA>(sb + i * tile_bytes(FA), kt, xq, bq, lane, acc);
-                    else mk_tile<FB>(sb + i * tile_bytes(FB), kt, xq, bq, lane, acc);
-                    if (++kt == KT) kt = 0;
+                kt += MK_CHUNK;
+                if (kt == KT) kt = 0;
+            } else for (int i = 0; i < n;) {   // groups of MK_GROUP tiles inside one row tile, single tiles otherwise
+                if (i > 0 && kt == 0) {
+                    flush();
+                    cur_r = ++r;
+                    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
                 }
+                if (i + MK_GROUP <= n && kt + MK_GROUP <= KT && !(fa ? F32A : F32B)) {
+                    if (fa) mk_chunk_fast<F32A ? FMT_Q8 : FA>(sb + i * tbytes, kt, xq, bq, lane, acc);
+                    else mk_chunk_fast<F32B ? FMT_Q8 : FB>(sb + i * tbytes, kt, xq, bq, lane, acc);
+                    i += MK_GROUP;
+                    kt += MK_GROUP;
+                } else {
+                    if (fa) mk_tile<FA>(sb + i * tbytes, kt, xq, bq, lane, acc);
+                    else mk_tile<FB>(sb + i * tbytes, kt, xq, bq, lane, acc);
+                    ++i;
+                    ++kt;
+                }
+                if (kt == KT) kt = 0;
             }
             __syncwarp();   // every tile byte of the slot is in registers: release it to the producer
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(R.empty + R.slot * 8) : "memory");
@@ -477,18 +517,20 @@ __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkR
 }
 
 template <int FA, int FB>
-__device__ __forceinline__ void mk_consume_epi(const MkPhase &P, const ModelDev *mp, const MkMisc &ms, MkRing &R,
+__device__ __forceinline__ void mk_consume_epi(const MkPhase &P, const ModelDev *mp, MkMisc &ms, MkRing &R,
                                                const MkLite *lite, int n_phases, int p, int cta, int G, int wi,
                                                const uint16_t *xq, const float *bq, const float *s_scale,
                                                MkPart &part, int *status, int lane) {
     switch (P.epi) {
         case MK_EPI_QKV: {
-            EpiQKV e{mp, &ms.sd, P.layer, P.bq, P.bk, P.bv, ms.rope[0], ms.rope[1], ms.pos};
+            EpiQKV e{mp,       &ms.sd,         P.layer,  P.bq,      P.bk,        P.bv,
+                     ms.rope[0], ms.rope[1], ms.pos, &ms.qkv_bias[0][0], ms.bias_r0, ms.bias_n,
+                     P.rbase[1], P.rbase[2]};
             mk_consume<FA, FB>(P, e, R, lite, n_phases, p, cta, G, wi, xq, bq, s_scale, part, status, lane);
             break;
         }
         case MK_EPI_RESID: {
-            EpiResid e{P.out, P.out_ld, P.out_rows};
+            MkEpiResid e{P.out, P.out_ld, P.out_rows, ms.xown, ms.own_r0, ms.own_n};
             mk_consume<FA, FB>(P, e, R, lite, n_phases, p, cta, G, wi, xq, bq, s_scale, part, status, lane);
             break;
         }
@@ -624,6 +666,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
         }
     }
     if (threadIdx.x == 0) misc.pos = pos;
+    {   // the residual row tiles this CTA owns in the O and down phases
+        const int r0 = (int)((int64_t)c * cfg.x_rtiles / G), r1 = (int)((int64_t)(c + 1) * cfg.x_rtiles / G);
+        const int n = r1 - r0 <= MK_OWN_TILES ? r1 - r0 : 0;
+        if (threadIdx.x == 0) {
+            misc.own_r0 = r0;
+            misc.own_n = n;
+        }
+        for (int i = threadIdx.x; i < n * 16 * GEMV_MB; i += MK_CT) {
+            const int b = i % GEMV_MB, rr = (i / GEMV_MB) % 16, rl = i / (16 * GEMV_MB);
+            const int row = (r0 + rl) * 16 + rr;
+            misc.xown[rl][rr][b] = (b < st.B && row < cfg.x_ld) ? __ldcg(&st.x[(size_t)b * cfg.x_ld + row]) : 0.f;
+        }
+    }
     sync_threads(MK_CT);
     MkRing R;
     R.slots = cfg.slots;
@@ -652,6 +707,22 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
             }
         } else {
             uint16_t *xs = reinterpret_cast<uint16_t *>(bsum + (BSUM ? P.a.nblk * GEMV_MB : 0));
+            if (P.epi == MK_EPI_QKV && threadIdx.x >= MK_CT - 32) {   // the last warp stages this CTA's biases
+                const MkLite &Lq = lite[p];
+                const int NR = Lq.rbase[Lq.n_seg];
+                const int r0 = (int)((int64_t)c * NR / G), r1 = (int)((int64_t)(c + 1) * NR / G);
+                const int n = r1 - r0 <= MK_OWN_TILES ? r1 - r0 : 0, D = st.D;
+                for (int i = threadIdx.x - (MK_CT - 32); i < n * 16; i += 32) {
+                    const int R = r0 + i / 16, tr = i % 16;
+                    const int si = R >= P.rbase[2] ? 2 : (R >= P.rbase[1] ? 1 : 0), rt = R - P.rbase[si];
+                    const int row = (rt / (D / TILE_ROWS)) * D + 8 * (rt % (D / TILE_ROWS)) + (tr & 7) + (tr & 8 ? D / 2 : 0);
+                    misc.qkv_bias[i / 16][tr] = __ldg((si == 0 ? P.bq : (si == 1 ? P.bk : P.bv)) + row);
+                }
+                if (threadIdx.x == MK_CT - 32) {
+                    misc.bias_r0 = r0;
+                    misc.bias_n = n;
+                }
+            }
             gemv_prologue<BSUM, 3>(P.a, xs, s_scale, s_red, bsum, MK_CT);
             const int g = lane >> 2, t = lane & 3;
             const uint16_t *xq = xs + (g < P.a.B ? g : 0) * P.a.kpx + 2 * t;   // absent rows: columns never read

@@ -137,6 +137,10 @@ struct EpiQKV {
     // (nullptr: read them from the model / state in global memory)
     const float *rc_s = nullptr, *rf_s = nullptr;
     int64_t pos_s = 0;
+    // persistent kernel: the biases of the CTA's row tiles [bias_r0, bias_r0 + bias_n) (flat over q, k, v; 16 per
+    // row tile in tile-row order) in shared memory; rb1 / rb2 = flat index of the first k / v row tile
+    const float *bias_s = nullptr;
+    int bias_r0 = 0, bias_n = 0, rb1 = 0, rb2 = 0;
     // lane holds tile rows (g, g+8) = RoPE partners (i, i + D/2) of one head
     __device__ void operator()(int seg, int rt, int g, int b, float y0, float y1) const {
         const int D = s->D, W = s->W, hd = D / 2;
@@ -146,8 +150,12 @@ struct EpiQKV {
         const int c = (int)(pos % W), par = ring_par(pos, W);
         const float *rc = rc_s ? rc_s : rope_row(*m, c);
         const float cs = rc[i], sn = rc[hd + i];
+        const int rl = (seg == 0 ? 0 : (seg == 1 ? rb1 : rb2)) + rt - bias_r0;
+        const bool pre = bias_s && rl >= 0 && rl < bias_n;
+        const float *bsrc = seg == 0 ? bq : (seg == 1 ? bk : bv);
+        const float b0v = pre ? bias_s[rl * 16 + g] : bsrc[r0], b1v = pre ? bias_s[rl * 16 + 8 + g] : bsrc[r1];
         if (seg == 0) {
-            const float a = y0 + bq[r0], bb = y1 + bq[r1];
+            const float a = y0 + b0v, bb = y1 + b1v;
             float *qc = s->q_cur + ((size_t)b * s->H + head) * D;
             qc[i] = a * cs - bb * sn;
             qc[i + hd] = bb * cs + a * sn;
@@ -158,7 +166,7 @@ struct EpiQKV {
                 qf[i + hd] = bb * rf[i] + a * rf[hd + i];
             }
         } else if (seg == 1) {
-            const float a = y0 + bk[r0], bb = y1 + bk[r1];
+            const float a = y0 + b0v, bb = y1 + b1v;
             kv_t *kr = kvp(*s, layer, b, ring_off(*s, par, KIND_KRAW, head, c));
             kv_t *ko = kvp(*s, layer, b, ring_off(*s, par, KIND_KROT, head, c));
             kr[i] = f2kv(a);
@@ -171,7 +179,7 @@ struct EpiQKV {
                 sk[i + hd] = f2kv(bb);
             }
         } else {
-            const float a = y0 + bv[r0], bb = y1 + bv[r1];
+            const float a = y0 + b0v, bb = y1 + b1v;
             kv_t *vv = kvp(*s, layer, b, ring_off(*s, par, KIND_V, head, c));
             vv[i] = f2kv(a);
             vv[i + hd] = f2kv(bb);
@@ -966,6 +974,8 @@ cudaError_t launch_mega(const v3g_model *m, v3g_state *s, bool want_lm, cudaStre
     mc.lite_off = s->mk_lite_off;
     mc.part_off = s->mk_part_off;
     mc.misc_off = s->mk_misc_off;
+    mc.x_rtiles = (m->host.d + TILE_ROWS - 1) / TILE_ROWS;
+    mc.x_ld = m->host.d;
     mc.ring_off = s->mk_ring_off;
     mc.bar_off = s->mk_bar_off;
     mc.lite = static_cast<const MkLite *>(s->mk_lite);
