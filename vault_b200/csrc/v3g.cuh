@@ -184,6 +184,15 @@ __device__ __forceinline__ uint2 ldg_stream8(const void *p) {
 // takes part pass blockDim.x, the persistent decode kernel passes its consumer warps only
 __device__ __forceinline__ void sync_threads(int n) { asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); }
 
+// D (16 x 8, fp32) += A (16 x 16, fp16, row) * B (16 x 8, fp16, col): one warp-wide tensor-core step
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

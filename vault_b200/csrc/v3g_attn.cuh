@@ -53,163 +53,152 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
 
 template <int D>
 struct AttnSmem {
-    kv_t k[ATT_KPC * (D + 8)];   // padded K rows: conflict-free 16-byte reads across rows
-    kv_t v[ATT_KPC * D];
-    float q[2][ATT_GRP_MAX][D];           // [far / cur][head][dim]
-    float p[ATT_GRP_MAX][ATT_KPC];
+    kv_t k[ATT_KPC * (D + 8)];   // K rows, padded so the tensor-core fragment reads hit distinct banks
+    kv_t v[ATT_KPC * (D + 8)];   // V rows, padded likewise; rows past the span are zero
+    __half qa[2][2][ATT_GRP_MAX][D + 8];    // [far / cur query][high / low fp16 part][head][dim]
+    float p[ATT_GRP_MAX][ATT_KPC];          // scaled scores
+    __half pa[2][ATT_GRP_MAX][ATT_KPC + 8]; // [high / low part][head][key]: probabilities exp(s - m)
     float m[ATT_GRP_MAX], l[ATT_GRP_MAX];
-    unsigned char far[ATT_KPC];
     int last;
 };
 
-// One work item = ATT_KPC keys of one (sequence b, KV head g) for its `grp` query heads, run by one CTA.
-// All K and V rows of the chunk are staged in shared memory with cp.async (one round trip), up to four threads
-// score a key (a slice of the head vector each), one warp per head forms the chunk's softmax pieces, and every
-// thread accumulates a column pair of every head over a quarter of the keys.  The CTA writes an unnormalised partial (o, m, l); the last CTA of (b, g) merges the
-// partials in split order into s.attn.  ks = key_span(s, b, pos).  Returns false when the split is empty.
+__device__ __forceinline__ uint32_t ld_h2(const __half *p) { return *reinterpret_cast<const uint32_t *>(p); }
+
+// two 8x8 fp16 matrices from shared memory, transposed: lanes 0-7 give the rows of the first, lanes 8-15 of the
+// second; thread (g, t) receives elements (rows 2t, 2t+1; column g) of each
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t &r0, uint32_t &r1, const void *p) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(a));
+}
+
+// fp32 value as high + low fp16 parts (about 22 significant bits together)
+__device__ __forceinline__ void split_half(float v, __half &hi, __half &lo) {
+    hi = __float2half_rn(v);
+    lo = __float2half_rn(v - __half2float(hi));
+}
+
+// One work item = ATT_KPC keys of one (sequence b, KV head g) for its `grp` query heads, run by one CTA on the
+// tensor cores.  All K and V rows of the chunk are staged in shared memory with cp.async (one round trip).  Scores:
+// for each block of 8 keys, mma steps over the head dimension with A = the group's queries (rows 0-7 their high
+// fp16 parts, rows 8-15 the low parts) and B = the K rows, so each head's dot is the sum of two accumulator rows
+// (about fp32 accuracy with fp16 keys).  Keys of the current chunk are scored with the query at position c, the
+// others with the query at W + c (both kinds only where a key block holds both).  One warp per head forms the
+// softmax pieces (m, l, p), and P V runs the same way: A = probabilities split high / low, B = V read transposed
+// with ldmatrix.  The CTA writes an unnormalised partial (o, m, l); the last CTA of (b, g) merges the partials in
+// split order into s.attn.  ks = key_span(s, b, pos).  Returns false when the split is empty.
 template <int D>
 __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float scale, int split, int g, int b,
                           int64_t pos, AttnSmem<D> &sm, int nt) {
     constexpr int KP = D + 8, CH = D / 8;
+    static_assert(D % 16 == 0 && ATT_KPC % 16 == 0, "mma shapes");
     const int H = s.H, G = s.G, grp = H / G;
     const int n_splits = (ks.total + ATT_KPC - 1) / ATT_KPC;
     if (split >= n_splits) return false;
     const int j0 = split * ATT_KPC, nk = min(ATT_KPC, ks.total - j0);
-    const int tid = threadIdx.x;
-    for (int c = tid; c < nk * CH; c += nt) {
+    const int nfar = ks.n_sk + ks.n_seg + ks.n_prev - j0;   // keys j < nfar are scored with the far query
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarp = nt >> 5;
+    const int gq = lane >> 2, t = lane & 3;
+    for (int c = tid; c < ATT_KPC * CH; c += nt) {
         const int j = c / CH, part = c - j * CH;
-        bool far;
-        const kv_t *kr = kv_row(s, layer, b, g, ks, j0 + j, false, far);
-        const kv_t *vr = kv_row(s, layer, b, g, ks, j0 + j, true, far);
-        cp_async16(&sm.k[j * KP + part * 8], kr + part * 8);
-        cp_async16(&sm.v[j * D + part * 8], vr + part * 8);
-        if (part == 0) sm.far[j] = far ? 1 : 0;
+        if (j < nk) {
+            bool far;
+            cp_async16(&sm.k[j * KP + part * 8], kv_row(s, layer, b, g, ks, j0 + j, false, far) + part * 8);
+            cp_async16(&sm.v[j * KP + part * 8], kv_row(s, layer, b, g, ks, j0 + j, true, far) + part * 8);
+        } else {   // past the span: probability 0 must meet a finite value
+            *reinterpret_cast<uint4 *>(&sm.v[j * KP + part * 8]) = make_uint4(0u, 0u, 0u, 0u);
+        }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    for (int idx = tid; idx < grp * D; idx += nt) {
-        const int hr = idx / D, dd = idx - hr * D;
-        const size_t qo = ((size_t)b * H + g * grp + hr) * D + dd;
-        sm.q[1][hr][dd] = __ldcg(&s.q_cur[qo]);
-        sm.q[0][hr][dd] = pos >= s.W ? __ldcg(&s.q_far[qo]) : 0.f;
+    for (int idx = tid; idx < 2 * ATT_GRP_MAX * D / 4; idx += nt) {   // queries, four dims per item
+        const int w = idx / (ATT_GRP_MAX * D / 4), r = idx - w * (ATT_GRP_MAX * D / 4);
+        const int hr = r / (D / 4), dd = 4 * (r - hr * (D / 4));
+        float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (hr < grp && (w == 1 || pos >= s.W)) {
+            const size_t qo = ((size_t)b * H + g * grp + hr) * D + dd;
+            q = __ldcg(reinterpret_cast<const float4 *>((w ? s.q_cur : s.q_far) + qo));
+        }
+        const float qv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) split_half(qv[e], sm.qa[w][0][hr][dd + e], sm.qa[w][1][hr][dd + e]);
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     sync_threads(nt);
-    // scores: QT adjacent threads share key j, each a DQ-wide slice of the head vector; slices meet by shuffles
-    {
-        int QT = nt / ATT_KPC < D / 8 ? nt / ATT_KPC : D / 8;   // 1, 2 or 4 threads per key
-        QT = QT >= 4 ? 4 : (QT >= 2 ? 2 : 1);
-        const int DQ = D / QT;
-        const int j = tid / QT, qi = tid - j * QT;
-        float acc[ATT_GRP_MAX];
+    // scores of the key blocks kb = warp, warp + nwarp, ...: lane (gq, t) ends with head gq, keys 8 kb + 2t (+1)
+    for (int kb = warp; kb * 8 < nk; kb += nwarp) {
+        const int key0 = kb * 8;
+        const bool any_far = key0 < nfar, any_cur = key0 + 8 > nfar;   // warp-uniform
+        float cf[4] = {0.f, 0.f, 0.f, 0.f}, cc[4] = {0.f, 0.f, 0.f, 0.f};
+        const kv_t *krow = &sm.k[(key0 + gq) * KP + 2 * t];
 #pragma unroll
-        for (int hr = 0; hr < ATT_GRP_MAX; ++hr) acc[hr] = 0.f;
-        if (j < nk && j < ATT_KPC) {
-            const float(*qs)[D] = sm.q[sm.far[j] ? 0 : 1];
-            const kv_t *kr = &sm.k[j * KP + qi * DQ];
-            for (int d0 = 0; d0 < DQ; d0 += 8) {
-                const uint4 raw = *reinterpret_cast<const uint4 *>(kr + d0);
-                const __half2 *k2 = reinterpret_cast<const __half2 *>(&raw);
-                float kf[8];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(k2[e]);
-                    kf[2 * e] = f.x;
-                    kf[2 * e + 1] = f.y;
-                }
-                const int dd = qi * DQ + d0;
-#pragma unroll
-                for (int hr = 0; hr < ATT_GRP_MAX; ++hr) {
-                    if (hr < grp) {
-                        const float4 qa = *reinterpret_cast<const float4 *>(&qs[hr][dd]);
-                        const float4 qb = *reinterpret_cast<const float4 *>(&qs[hr][dd + 4]);
-                        float s0 = qa.x * kf[0], s1 = qa.y * kf[1];
-                        s0 = fmaf(qa.z, kf[2], s0);
-                        s1 = fmaf(qa.w, kf[3], s1);
-                        s0 = fmaf(qb.x, kf[4], s0);
-                        s1 = fmaf(qb.y, kf[5], s1);
-                        s0 = fmaf(qb.z, kf[6], s0);
-                        s1 = fmaf(qb.w, kf[7], s1);
-                        acc[hr] += s0 + s1;
-                    }
-                }
-            }
+        for (int k16 = 0; k16 < D / 16; ++k16) {
+            const uint32_t b0 = ld_h2(krow + 16 * k16), b1 = ld_h2(krow + 16 * k16 + 8);
+            const int qc = 16 * k16 + 2 * t;
+            if (any_far)
+                mma16816(cf, ld_h2(&sm.qa[0][0][gq][qc]), ld_h2(&sm.qa[0][1][gq][qc]), ld_h2(&sm.qa[0][0][gq][qc + 8]),
+                         ld_h2(&sm.qa[0][1][gq][qc + 8]), b0, b1);
+            if (any_cur)
+                mma16816(cc, ld_h2(&sm.qa[1][0][gq][qc]), ld_h2(&sm.qa[1][1][gq][qc]), ld_h2(&sm.qa[1][0][gq][qc + 8]),
+                         ld_h2(&sm.qa[1][1][gq][qc + 8]), b0, b1);
         }
+        if (gq < grp) {
 #pragma unroll
-        for (int hr = 0; hr < ATT_GRP_MAX; ++hr) {
-            float tot = acc[hr];
-            for (int o = 1; o < QT; o <<= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-            if (hr < grp && qi == 0 && j < nk && j < ATT_KPC) sm.p[hr][j] = tot * scale;
+            for (int e = 0; e < 2; ++e) {
+                const int j = key0 + 2 * t + e;
+                const float sc = (j < nfar ? cf[e] + cf[2 + e] : cc[e] + cc[2 + e]) * scale;
+                sm.p[gq][j] = j < nk ? sc : -INFINITY;
+            }
         }
     }
     sync_threads(nt);
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int hr = warp; hr < grp; hr += nt / 32) {
-        float mx = -INFINITY;
-        for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sm.p[hr][j]);
-        mx = warp_max(mx);
-        float l = 0.f;
-        for (int j = lane; j < nk; j += 32) {
-            const float p = expf(sm.p[hr][j] - mx);
-            sm.p[hr][j] = p;
-            l += p;
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            sm.m[hr] = mx;
-            sm.l[hr] = l;
+    // softmax pieces, one warp per head: m = max score, p = exp(s - m) (as fp16 high / low parts), l = sum of p
+    for (int hr = warp; hr < ATT_GRP_MAX; hr += nwarp) {
+        if (hr < grp) {
+            float mx = -INFINITY;
+            for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sm.p[hr][j]);
+            mx = warp_max(mx);
+            float l = 0.f;
+            for (int j = lane; j < ATT_KPC; j += 32) {
+                const float p = j < nk ? expf(sm.p[hr][j] - mx) : 0.f;
+                split_half(p, sm.pa[0][hr][j], sm.pa[1][hr][j]);
+                l += p;
+            }
+            l = warp_sum(l);
+            if (lane == 0) {
+                sm.m[hr] = mx;
+                sm.l[hr] = l;
+            }
+        } else {
+            for (int j = lane; j < ATT_KPC; j += 32) sm.pa[0][hr][j] = sm.pa[1][hr][j] = __float2half_rn(0.f);
         }
     }
     sync_threads(nt);
-    // output: thread (column pair c2, key quarter kq) sums its keys for every head; quarters meet in shared memory
-    // (the K rows are no longer needed: their space holds the quarter sums)
-    {
-        constexpr int P2 = D / 2;
-        const int KQ = nt / P2 >= 4 ? 4 : (nt / P2 >= 2 ? 2 : 1);
-        const int c2 = tid % P2, kq = tid / P2;
-        float o[ATT_GRP_MAX][2];
-#pragma unroll
-        for (int hr = 0; hr < ATT_GRP_MAX; ++hr) o[hr][0] = o[hr][1] = 0.f;
-        if (kq < KQ) {
-            for (int jj = kq; jj < nk; jj += KQ) {
-                const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&sm.v[jj * D + 2 * c2]));
-#pragma unroll
-                for (int hr = 0; hr < ATT_GRP_MAX; ++hr) {
-                    if (hr < grp) {
-                        const float pj = sm.p[hr][jj];
-                        o[hr][0] = fmaf(pj, v.x, o[hr][0]);
-                        o[hr][1] = fmaf(pj, v.y, o[hr][1]);
-                    }
-                }
+    // P V for the 8-column blocks nb = warp, warp + nwarp, ...: lane (gq, t) ends with head gq, columns 8 nb + 2t (+1)
+    const int nk16 = (nk + 15) / 16;
+    float *part = n_splits == 1 ? nullptr : s.att_part + ((((size_t)b * G + g) * s.max_splits + split) * grp) * (D + 2);
+    for (int nb = warp; nb < D / 8; nb += nwarp) {
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int k16 = 0; k16 < nk16; ++k16) {
+            uint32_t b0, b1;
+            ldsm_x2_trans(b0, b1, &sm.v[(16 * k16 + (lane & 15)) * KP + 8 * nb]);
+            const int pc = 16 * k16 + 2 * t;
+            mma16816(c, ld_h2(&sm.pa[0][gq][pc]), ld_h2(&sm.pa[1][gq][pc]), ld_h2(&sm.pa[0][gq][pc + 8]),
+                     ld_h2(&sm.pa[1][gq][pc + 8]), b0, b1);
+        }
+        if (gq < grp) {
+            const int dd = 8 * nb + 2 * t;
+            const float o0 = c[0] + c[2], o1 = c[1] + c[3];
+            if (!part) {   // the whole span in one item: normalise and write the head outputs directly
+                const float inv = 1.f / sm.l[gq];
+                *reinterpret_cast<float2 *>(&s.attn[((size_t)b * H + g * grp + gq) * D + dd]) = make_float2(o0 * inv, o1 * inv);
+            } else {
+                part[gq * (D + 2) + dd] = o0;
+                part[gq * (D + 2) + dd + 1] = o1;
             }
         }
-        sync_threads(nt);   // every thread is done with the K rows
-        float *red = reinterpret_cast<float *>(sm.k);   // [KQ][grp][D]
-        if (kq < KQ) {
-#pragma unroll
-            for (int hr = 0; hr < ATT_GRP_MAX; ++hr)
-                if (hr < grp) *reinterpret_cast<float2 *>(&red[(kq * grp + hr) * D + 2 * c2]) = make_float2(o[hr][0], o[hr][1]);
-        }
-        sync_threads(nt);
-        for (int idx = tid; idx < grp * D; idx += nt) {
-            const int hr = idx / D, dd = idx - hr * D;
-            float acc = 0.f;
-            for (int q = 0; q < KQ; ++q) acc += red[(q * grp + hr) * D + dd];
-            sm.q[0][hr][dd] = acc;   // the query rows are no longer needed either: reuse them for the output
-        }
-        sync_threads(nt);
     }
-    if (n_splits == 1) {   // the whole span in one item: normalise and write the head outputs directly
-        for (int idx = tid; idx < grp * D; idx += nt) {
-            const int hr = idx / D, dd = idx - hr * D;
-            s.attn[((size_t)b * H + g * grp + hr) * D + dd] = sm.q[0][hr][dd] / sm.l[hr];
-        }
+    if (!part) {
         sync_threads(nt);
         return true;
-    }
-    float *part = s.att_part + ((((size_t)b * G + g) * s.max_splits + split) * grp) * (D + 2);
-    for (int idx = tid; idx < grp * D; idx += nt) {
-        const int hr = idx / D, dd = idx - hr * D;
-        part[hr * (D + 2) + dd] = sm.q[0][hr][dd];
     }
     if (tid < grp) {
         part[tid * (D + 2) + D] = sm.m[tid];

@@ -48,13 +48,6 @@ struct GemvArgs {
 __host__ __device__ constexpr bool fmt_int(int fmt) { return fmt == FMT_Q8 || fmt == FMT_Q4; }
 __host__ __device__ constexpr float fmt_offset(int fmt) { return fmt == FMT_Q8 ? 1152.f : 1032.f; }
 
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 __device__ __forceinline__ float2 h2f2(uint32_t h) {
     __half2 v = *reinterpret_cast<__half2 *>(&h);
     return __half22float2(v);
@@ -198,19 +191,42 @@ __device__ __forceinline__ void load16(const float *p, bool vec, int n, float (&
     }
 }
 
+// 16 norm weights through a generic pointer: the vector in global memory, or a shared-memory copy of it that the
+// caller staged
+__device__ __forceinline__ void load16_norm(const float *p, bool vec, int n, float (&w)[16]) {
+    if (vec) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 q = reinterpret_cast<const float4 *>(p)[j];
+            w[4 * j] = q.x;
+            w[4 * j + 1] = q.y;
+            w[4 * j + 2] = q.z;
+            w[4 * j + 3] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) w[j] = j < n ? p[j] : 0.f;
+    }
+}
+
+// 2^e for an integer e in [-126, 127], built from its exponent bits (exact)
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
+
 // Convert the pass's activation rows once per CTA into shared memory: RMSNorm (optional), fp16 with a per-row
 // power-of-two scale (largest |x| scaled into (2^13, 2^14]); s_scale[b] receives the scale to undo and, with
 // BSUM, bsum[blk * 8 + b] the fp32 sum of converted 32-wide block blk of row b.  Work items are half blocks (16
 // values; the two halves of a block sit in adjacent lanes): one stats pass and one convert pass.  A thread keeps
 // its first items in registers between the passes -- CACHE of them without RMSNorm, one item and its norm weights
-// (in the last cache slot) with it -- so such rows cost one round trip to L2.
+// (in the last cache slot) with it -- so such rows cost one round trip to L2.  nw_s: optional shared-memory copy
+// of the norm weights (a.norm_w).
 template <bool BSUM, int CACHE = 0>
 __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_scale, float *s_red, float *bsum,
-                                     int nt) {
+                                     int nt, const float *nw_s = nullptr) {
     const int tid = threadIdx.x, nw = nt / 32;
     const bool norm = a.prologue == PRO_RMSNORM;
     const bool vec = (a.K & 31) == 0 && (a.x_ld & 3) == 0;
     const int nb = (a.K + 31) >> 5, nh = 2 * nb, items = a.B * nh;
+    const float *nwp = nw_s ? nw_s : a.norm_w;
     float ss[GEMV_MB], mx[GEMV_MB];
 #pragma unroll
     for (int b = 0; b < GEMV_MB; ++b) {
@@ -241,7 +257,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         if (k < ncache && it < items) {
             const int b = it / nh, h = it - b * nh, n = a.K - h * 16;
             load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, vc[k]);
-            if (k == 0 && norm) load16<false>(a.norm_w + h * 16, vec, n, wc);
+            if (k == 0 && norm) load16_norm(nwp + h * 16, vec, n, wc);
         }
     }
 #pragma unroll
@@ -253,7 +269,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         const int b = it / nh, h = it - b * nh, n = a.K - h * 16;
         float v[16], w[16];
         load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, v);
-        if (norm) load16<false>(a.norm_w + h * 16, vec, n, w);
+        if (norm) load16_norm(nwp + h * 16, vec, n, w);
         stats(b, v, w);
     }
 #pragma unroll
@@ -276,14 +292,13 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
             Mx = fmaxf(Mx, s_red[64 + b * 8 + w]);
         }
         const float inv = norm ? 1.0f / sqrtf(S / (float)a.K + a.eps) : 1.0f;
-        float e = 0.f;
-        if (Mx * inv > 0.f) {
-            int ex;
-            frexpf(Mx * inv, &ex);
-            e = (float)(ex - 14);   // largest |x| scaled into (2^13, 2^14]
-        }
-        scale = exp2f(e);
-        return inv * exp2f(-e);   // multiplier applied before rounding to 16 bits
+        // largest |x| scaled into (2^13, 2^14]: e = frexp exponent - 14, read from the exponent bits (the row
+        // maximum is a finite non-negative float; a zero or subnormal maximum keeps e = 0)
+        const int be = (__float_as_int(Mx * inv) >> 23) & 0xff;
+        int e = be > 0 ? be - 140 : 0;
+        e = e < -126 ? -126 : (e > 126 ? 126 : e);
+        scale = pow2i(e);
+        return inv * pow2i(-e);   // multiplier applied before rounding to 16 bits
     };
     if (tid < a.B) {
         float sc;
@@ -337,7 +352,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         float v[16], w[16];
         if (act) {
             load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, v);
-            if (norm) load16<false>(a.norm_w + h * 16, vec, n, w);
+            if (norm) load16_norm(nwp + h * 16, vec, n, w);
         }
         convert(act, b, h, n, v, w);
     }
@@ -426,7 +441,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
 
 inline size_t gemv_smem_bytes(const GemvArgs &a, bool bsum) {
     return (136 + GEMV_MB + 8 * 32 * 4 + (bsum ? a.nblk * GEMV_MB : 0)) * sizeof(float) +
-           (size_t)(a.B + 1) * a.kpx * sizeof(uint16_t);
+           (size_t)a.B * a.kpx * sizeof(uint16_t);
 }
 
 // Host helper: choose the k split so the launch covers the GPU, fill the launch parameters.

@@ -47,7 +47,8 @@ struct v3g_state {
     void *mk_lite = nullptr;         // device MkLite[mk_n] (chunk-stream table)
     void *mk_fn = nullptr;           // kernel instantiation for this model's head size and tile formats
     int mk_n = 0, mk_grid = 0, mk_slots = 0, mk_xr = 0;
-    int mk_ph_off = 0, mk_lite_off = 0, mk_part_off = 0, mk_misc_off = 0, mk_ring_off = 0, mk_bar_off = 0;
+    int mk_ph_off = 0, mk_lite_off = 0, mk_part_off = 0, mk_misc_off = 0, mk_nw_off = 0, mk_ring_off = 0,
+        mk_bar_off = 0;
     size_t mk_smem = 0;
     std::string last_error;
 };

@@ -53,6 +53,11 @@ struct alignas(16) MkPhase {
     const float *bq, *bk, *bv;
     float *out;
     int out_ld, out_rows;
+    // norm weights of the NEXT phase (nullptr when it has no RMSNorm or they cannot be staged): this phase copies
+    // them into shared memory while it runs, so the next prologue does not wait on them
+    const float *next_norm;
+    int next_k;
+    int norm_staged;      // the previous phase staged this phase's norm weights
 };
 
 // chunk-stream view of one phase; the whole table lives in shared memory for the kernel's lifetime
@@ -70,8 +75,8 @@ static_assert(sizeof(MkLite) == 80, "MkLite is one 80-byte record");
 struct MkCfg {
     int slots;            // ring depth per consumer warp
     int xr_bytes;         // activation / attention region at the start of dynamic shared memory
-    int ph_off, lite_off, part_off, misc_off, ring_off, bar_off;   // shared-memory offsets (bytes); bar_off: full,
-                                                                    // then empty barriers
+    int ph_off, lite_off, part_off, misc_off, nw_off, ring_off, bar_off;   // shared-memory offsets (bytes); bar_off:
+                                                                            // full, then empty barriers
     int x_rtiles, x_ld;   // row tiles of the residual stream (d / 16, rounded up) and its row stride (d)
     const MkLite *lite;   // global copy of the lite table (n_phases records)
 };
@@ -175,12 +180,21 @@ __device__ __forceinline__ int mk_row_tile(const MkLite &L, int R) {
     return L.tbase[si] + (R - L.rbase[si]) * L.kt[si];
 }
 
-// tile range [t0, t1) of consumer warp wi of CTA c (of G) in phase L
+// tile range [t0, t1) of consumer warp wi of CTA c (of G) in phase L.  A CTA range of fewer than two chunks per
+// warp is cut at whole chunks (some warps then get none): a full chunk runs the fast path and costs little more
+// than a partial one, and fewer pieces meet in the combine.
 __device__ __forceinline__ void mk_range(const MkLite &L, int c, int G, int wi, int &t0, int &t1) {
     const int NR = L.rbase[L.n_seg];
     const int lo = mk_row_tile(L, (int)((int64_t)c * NR / G)), hi = mk_row_tile(L, (int)((int64_t)(c + 1) * NR / G));
-    t0 = lo + (int)((int64_t)wi * (hi - lo) / MK_WARPS);
-    t1 = lo + (int)((int64_t)(wi + 1) * (hi - lo) / MK_WARPS);
+    const int n = hi - lo;
+    if (n < 2 * MK_CHUNK * MK_WARPS) {
+        const int nc = (n + MK_CHUNK - 1) / MK_CHUNK;
+        t0 = lo + min(n, wi * nc / MK_WARPS * MK_CHUNK);
+        t1 = lo + min(n, (wi + 1) * nc / MK_WARPS * MK_CHUNK);
+    } else {
+        t0 = lo + (int)((int64_t)wi * n / MK_WARPS);
+        t1 = lo + (int)((int64_t)(wi + 1) * n / MK_WARPS);
+    }
 }
 
 __device__ __forceinline__ void mk_seg(const MkLite &L, MkCur &c) {
@@ -737,7 +751,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
                     misc.bias_n = n;
                 }
             }
-            gemv_prologue<BSUM, 3>(P.a, xs, s_scale, s_red, bsum, MK_CT);
+            float *nw_s = reinterpret_cast<float *>(smem + cfg.nw_off);
+            gemv_prologue<BSUM, 3>(P.a, xs, s_scale, s_red, bsum, MK_CT, P.norm_staged ? nw_s : nullptr);
+            if (P.next_norm) {   // stage the next phase's norm weights while this one streams (landed by the barrier)
+                for (int i = threadIdx.x; i < P.next_k / 4; i += MK_CT) cp_async16(nw_s + 4 * i, P.next_norm + 4 * i);
+                asm volatile("cp.async.commit_group;" ::: "memory");
+            }
             const int g = lane >> 2, t = lane & 3;
             const uint16_t *xq = xs + (g < P.a.B ? g : 0) * P.a.kpx + 2 * t;   // absent rows: columns never read
             mk_consume_epi<FA, FB>(P, mp, misc, R, lite, n_phases, p, c, G, warp, xq, bsum + 2 * t, s_scale, part,

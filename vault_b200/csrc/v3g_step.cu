@@ -859,6 +859,16 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
     const MatW *lm[1] = {&md.embed};
     add_gemv(lm, 1, sd.x, md.d, md.d, PRO_RMSNORM, md.norm, MK_EPI_STORE, -1, sd.logits, md.vocab, md.vocab);
     if (!ok) return cudaSuccess;
+    // a phase followed by an RMSNorm phase stages that phase's norm weights in shared memory (16-byte pieces)
+    for (size_t i = 0; i + 1 < ph.size(); ++i) {
+        const MkPhase &nx = ph[i + 1];
+        if (ph[i].kind == MK_GEMV && nx.kind == MK_GEMV && nx.a.prologue == PRO_RMSNORM && nx.a.K == md.d &&
+            md.d % 4 == 0 && reinterpret_cast<uintptr_t>(nx.a.norm_w) % 16 == 0) {
+            ph[i].next_norm = nx.a.norm_w;
+            ph[i].next_k = nx.a.K;
+            ph[i + 1].norm_staged = 1;
+        }
+    }
     // the kernel's format pair: every segment of every GEMV phase must be FA or FB
     bool has[16] = {};
     for (const MkPhase &q : ph)
@@ -891,11 +901,13 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
     cudaFuncAttributes fattr{};
     e = cudaFuncGetAttributes(&fattr, (const void *)fn);
     if (e != cudaSuccess) return e;
-    // shared memory: [x / attention region][2 phase descriptors][lite table][split pieces][rings][ring mbarriers]
+    // shared memory: [x / attention region][2 phase descriptors][lite table][split pieces][per-step constants]
+    // [staged norm weights][rings][ring mbarriers]
     const size_t ph_off = xr, lite_off = ph_off + 2 * sizeof(MkPhase);
     const size_t part_off = (lite_off + ph.size() * sizeof(MkLite) + 15) / 16 * 16;
     const size_t misc_off = (part_off + sizeof(MkPart) + 15) / 16 * 16;
-    const size_t ring_off = (misc_off + sizeof(MkMisc) + 127) / 128 * 128;
+    const size_t nw_off = (misc_off + sizeof(MkMisc) + 15) / 16 * 16;
+    const size_t ring_off = (nw_off + (size_t)md.d * sizeof(float) + 127) / 128 * 128;
     const long avail = (long)optin - (long)fattr.sharedSizeBytes - (long)ring_off;
     const long per_slot = (long)MK_WARPS * (MK_SLOT_BYTES + 16);   // buffer + full and empty barriers
     int slots = avail > 0 ? (int)(avail / per_slot) : 0;
@@ -941,6 +953,7 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
     s->mk_lite_off = (int)lite_off;
     s->mk_part_off = (int)part_off;
     s->mk_misc_off = (int)misc_off;
+    s->mk_nw_off = (int)nw_off;
     s->mk_ring_off = (int)ring_off;
     s->mk_bar_off = (int)bar_off;
     s->mk_grid = m->n_sm;
@@ -974,6 +987,7 @@ cudaError_t launch_mega(const v3g_model *m, v3g_state *s, bool want_lm, cudaStre
     mc.lite_off = s->mk_lite_off;
     mc.part_off = s->mk_part_off;
     mc.misc_off = s->mk_misc_off;
+    mc.nw_off = s->mk_nw_off;
     mc.x_rtiles = (m->host.d + TILE_ROWS - 1) / TILE_ROWS;
     mc.x_ld = m->host.d;
     mc.ring_off = s->mk_ring_off;
