@@ -31,7 +31,7 @@ struct GemvArgs {
     int seg_base;     // segment index reported to the epilogue for seg[0]
     int total_rtiles;
     int K;            // logical K
-    int kpx;          // smem row pitch of the converted activations (elements) = padded K + 8
+    int kpx;          // padded K + 8 (kept for the host plan; the converted activations use nblk 32-blocks)
     int nblk;         // 32-wide blocks of the padded K (block sums)
     int B;            // batch rows in this pass (<= GEMV_MB)
     int b0;           // first batch row of this pass
@@ -79,32 +79,39 @@ __device__ __forceinline__ void load_tile(TileRegs &r, const uint8_t *tb, int la
     }
 }
 
-// activation fragment of k step starting at kk for this lane (zero when its batch row g >= B)
-__device__ __forceinline__ void bfrag(const uint16_t *xr, int kk, int t, uint32_t &b0, uint32_t &b1) {
-    if (xr) {
-        b0 = *reinterpret_cast<const uint32_t *>(xr + kk + 2 * t);
-        b1 = *reinterpret_cast<const uint32_t *>(xr + kk + 2 * t + 8);
-    } else {
-        b0 = 0u;
-        b1 = 0u;
+// Converted activations in shared memory are fragment-major: for each 32-wide k block, each batch row b and each
+// lane quad position t one 16-byte record {x[2t..], x[2t+8..], x[2t+16..], x[2t+24..]} (fp16 pairs), i.e. the
+// tensor-core B fragments of the block's two k16 steps for lane (g = b, t), record index (blk * B + b) * 4 + t.  A
+// lane reads a Q8 tile's activations with one 16-byte load (64 bytes per quad: one wavefront, no bank conflicts for
+// any batch size).  XFrag addresses one lane's records: base = record of block 0, stride = records per block (4 B).
+struct XFrag {
+    const uint4 *base;   // nullptr: batch row absent (fragments read as zero)
+    int stride;
+    __device__ __forceinline__ uint4 blk(int i) const { return base ? base[i * stride] : make_uint4(0u, 0u, 0u, 0u); }
+    // fragments (b0, b1) of absolute k16 step j
+    __device__ __forceinline__ void step(int j, uint32_t &b0, uint32_t &b1) const {
+        if (base) {
+            const uint2 v = reinterpret_cast<const uint2 *>(base + (j >> 1) * stride)[j & 1];
+            b0 = v.x;
+            b1 = v.y;
+        } else {
+            b0 = 0u;
+            b1 = 0u;
+        }
     }
-}
+};
 
 template <int FMT>
-__device__ __forceinline__ void compute_tile(const TileRegs &r, int kt, const uint16_t *xr, const float *bsum, int t,
+__device__ __forceinline__ void compute_tile(const TileRegs &r, int kt, const XFrag &xf, const float *bsum, int t,
                                              float (&acc)[4]) {
-    constexpr int TK = tile_k(FMT);
-    const int kb = kt * TK;
     const uint32_t w[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
     if constexpr (FMT == FMT_Q8) {
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-            uint32_t b0, b1;
-            bfrag(xr, kb + 16 * s, t, b0, b1);
-            mma16816(d, q8_pair(w[2 * s], 0x4140u), q8_pair(w[2 * s], 0x4342u), q8_pair(w[2 * s + 1], 0x4140u),
-                     q8_pair(w[2 * s + 1], 0x4342u), b0, b1);
-        }
+        const uint4 xv = xf.blk(kt);
+        mma16816(d, q8_pair(w[0], 0x4140u), q8_pair(w[0], 0x4342u), q8_pair(w[1], 0x4140u), q8_pair(w[1], 0x4342u),
+                 xv.x, xv.y);
+        mma16816(d, q8_pair(w[2], 0x4140u), q8_pair(w[2], 0x4342u), q8_pair(w[3], 0x4140u), q8_pair(w[3], 0x4342u),
+                 xv.z, xv.w);
         const float2 S = *reinterpret_cast<const float2 *>(bsum + kt * GEMV_MB + 2 * t);   // batch 2t, 2t+1
         const float2 ds = h2f2(r.s.x);                                                   // rows g, g+8
         acc[0] = fmaf(ds.x, fmaf(-1152.f, S.x, d[0]), acc[0]);
@@ -116,13 +123,11 @@ __device__ __forceinline__ void compute_tile(const TileRegs &r, int kt, const ui
 #pragma unroll
         for (int blk = 0; blk < 2; ++blk) {
             float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int ss = 0; ss < 2; ++ss) {
-                const int s = 2 * blk + ss;
-                uint32_t b0, b1;
-                bfrag(xr, kb + 16 * s, t, b0, b1);
-                mma16816(d, q4_pair<0>(w[s]), q4_pair<4>(w[s]), q4_pair<8>(w[s]), q4_pair<12>(w[s]), b0, b1);
-            }
+            const uint4 xv = xf.blk(2 * kt + blk);
+            mma16816(d, q4_pair<0>(w[2 * blk]), q4_pair<4>(w[2 * blk]), q4_pair<8>(w[2 * blk]), q4_pair<12>(w[2 * blk]),
+                     xv.x, xv.y);
+            mma16816(d, q4_pair<0>(w[2 * blk + 1]), q4_pair<4>(w[2 * blk + 1]), q4_pair<8>(w[2 * blk + 1]),
+                     q4_pair<12>(w[2 * blk + 1]), xv.z, xv.w);
             const float2 S = *reinterpret_cast<const float2 *>(bsum + (2 * kt + blk) * GEMV_MB + 2 * t);
             const float2 ds = h2f2(sc[blk]);
             acc[0] = fmaf(ds.x, fmaf(-1032.f, S.x, d[0]), acc[0]);
@@ -132,7 +137,7 @@ __device__ __forceinline__ void compute_tile(const TileRegs &r, int kt, const ui
         }
     } else if constexpr (FMT == FMT_F32) {   // planes accumulate apart, then hi + 2^-11 mid + 2^-22 lo
         uint32_t b0, b1;
-        bfrag(xr, kb, t, b0, b1);
+        xf.step(kt, b0, b1);
         float dm[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
         mma16816(acc, w[0], w[1], w[2], w[3], b0, b1);
         mma16816(dm, r.m.x, r.m.y, r.m.z, r.m.w, b0, b1);
@@ -141,7 +146,7 @@ __device__ __forceinline__ void compute_tile(const TileRegs &r, int kt, const ui
         for (int i = 0; i < 4; ++i) acc[i] = fmaf(dm[i], F32_MID, fmaf(dl[i], F32_LO, acc[i]));
     } else {
         uint32_t b0, b1;
-        bfrag(xr, kb, t, b0, b1);
+        xf.step(kt, b0, b1);
         mma16816(acc, w[0], w[1], w[2], w[3], b0, b1);
     }
 }
@@ -156,7 +161,7 @@ __device__ __forceinline__ void prefetch_tiles(TileRegs (&pre)[GEMV_U], const ui
 // stream nkt tiles starting at tp (the first GEMV_U already in `pre`), double-buffered
 template <int FMT>
 __device__ __forceinline__ void stream_tiles(TileRegs (&pre)[GEMV_U], const uint8_t *tp, int kt0, int nkt,
-                                             const uint16_t *xr, const float *bsum, int lane, float (&acc)[4]) {
+                                             const XFrag &xf, const float *bsum, int lane, float (&acc)[4]) {
     constexpr int TB = tile_bytes(FMT);
     const int t = lane & 3;
     for (int i = 0; i < nkt; i += GEMV_U) {
@@ -166,7 +171,7 @@ __device__ __forceinline__ void stream_tiles(TileRegs (&pre)[GEMV_U], const uint
             if (i + GEMV_U + u < nkt) load_tile<FMT>(nxt[u], tp + (size_t)(i + GEMV_U + u) * TB, lane);
 #pragma unroll
         for (int u = 0; u < GEMV_U; ++u)
-            if (i + u < nkt) compute_tile<FMT>(pre[u], kt0 + i + u, xr, bsum, t, acc);
+            if (i + u < nkt) compute_tile<FMT>(pre[u], kt0 + i + u, xf, bsum, t, acc);
 #pragma unroll
         for (int u = 0; u < GEMV_U; ++u) pre[u] = nxt[u];
     }
@@ -227,6 +232,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
     const bool vec = (a.K & 31) == 0 && (a.x_ld & 3) == 0;
     const int nb = (a.K + 31) >> 5, nh = 2 * nb, items = a.B * nh;
     const float *nwp = nw_s ? nw_s : a.norm_w;
+    const float inv_k = 1.0f / (float)a.K;
     float ss[GEMV_MB], mx[GEMV_MB];
 #pragma unroll
     for (int b = 0; b < GEMV_MB; ++b) {
@@ -274,8 +280,13 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
     }
 #pragma unroll
     for (int b = 0; b < GEMV_MB; ++b) {
-        if (b < a.B) {
-            const float S = warp_sum(ss[b]), M = warp_max(mx[b]);
+        if (b < a.B) {   // warp partials: the sum and max shuffle chains interleave
+            float S = ss[b], M = mx[b];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                S += __shfl_xor_sync(0xffffffffu, S, o);
+                M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            }
             if ((tid & 31) == 0) {
                 s_red[b * 8 + (tid >> 5)] = S;
                 s_red[64 + b * 8 + (tid >> 5)] = M;
@@ -284,14 +295,17 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
     }
     sync_threads(nt);
     // every thread derives the multiplier of the rows it converts (same arithmetic everywhere: no second sync);
-    // threads b < B also publish the scale the GEMV undoes
+    // threads b < B also publish the scale the GEMV undoes.  Warp partials are summed in warp order.
     auto row_mul = [&](int b, float &scale) {
         float S = 0.f, Mx = 0.f;
-        for (int w = 0; w < nw; ++w) {
-            S += s_red[b * 8 + w];
-            Mx = fmaxf(Mx, s_red[64 + b * 8 + w]);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {   // nt <= 256: at most 8 warp partials, all loads in flight
+            if (w < nw) {
+                S += s_red[b * 8 + w];
+                Mx = fmaxf(Mx, s_red[64 + b * 8 + w]);
+            }
         }
-        const float inv = norm ? 1.0f / sqrtf(S / (float)a.K + a.eps) : 1.0f;
+        const float inv = norm ? rsqrtf(S * inv_k + a.eps) : 1.0f;
         // largest |x| scaled into (2^13, 2^14]: e = frexp exponent - 14, read from the exponent bits (the row
         // maximum is a finite non-negative float; a zero or subnormal maximum keeps e = 0)
         const int be = (__float_as_int(Mx * inv) >> 23) & 0xff;
@@ -300,9 +314,12 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         scale = pow2i(e);
         return inv * pow2i(-e);   // multiplier applied before rounding to 16 bits
     };
+    int cb = -1;          // row whose multiplier cmul holds (threads convert few distinct rows: compute each once)
+    float cmul = 0.f;
     if (tid < a.B) {
         float sc;
-        (void)row_mul(tid, sc);
+        cmul = row_mul(tid, sc);
+        cb = tid;
         s_scale[tid] = sc;
     }
     auto convert = [&](bool act, int b, int h, int n, const float (&v)[16], const float (&w)[16]) {
@@ -314,8 +331,12 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
                 for (int j = 0; j < 16; ++j)
                     if (j < n) f[j] = v[j];
             }
-            float unused;
-            const float mul = row_mul(b, unused);
+            if (b != cb) {
+                float unused;
+                cmul = row_mul(b, unused);
+                cb = b;
+            }
+            const float mul = cmul;
             uint32_t hw[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -326,9 +347,11 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
                 bs += back.x + back.y;
                 hw[j] = *reinterpret_cast<const uint32_t *>(&hv);
             }
-            uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)b * a.kpx + h * 16);
-            dst[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            dst[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            // fragment-major records of block h / 2, row b: lane quad t takes pairs t (b0) and t + 4 (b1) of
+            // this half block, at the record's k16 step h & 1
+            uint2 *dst = reinterpret_cast<uint2 *>(reinterpret_cast<uint4 *>(xs) + ((size_t)(h >> 1) * a.B + b) * 4) + (h & 1);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[2 * q] = make_uint2(hw[q], hw[q + 4]);
         }
         if (BSUM) {   // the two halves of a block sit in adjacent lanes (warp-uniform call)
             bs += __shfl_xor_sync(0xffffffffu, bs, 1);
@@ -356,10 +379,10 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         }
         convert(act, b, h, n, v, w);
     }
-    // zero the padding columns and the block sums of padding blocks (tiles may extend past K).  Absent batch rows
-    // (b >= B) are left as they are: their tensor-core columns are computed and never read.
-    const int kp = a.kpx, pad = kp - nb * 32;
-    for (int idx = tid; idx < a.B * pad; idx += nt) xs[(size_t)(idx / pad) * kp + nb * 32 + idx % pad] = 0;
+    // zero the records and block sums of padding blocks (tiles may extend past K).  Absent batch rows (b >= B) have
+    // no records: their lanes read row 0, whose tensor-core columns are computed and never read.
+    for (int idx = nb * a.B * 4 + tid; idx < a.nblk * a.B * 4; idx += nt)
+        reinterpret_cast<uint4 *>(xs)[idx] = make_uint4(0u, 0u, 0u, 0u);
     if (BSUM)
         for (int idx = nb * GEMV_MB + tid; idx < a.nblk * GEMV_MB; idx += nt) bsum[idx] = 0.f;
     sync_threads(nt);
@@ -406,9 +429,9 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     if (active) {
         const int g = lane >> 2;
-        const uint16_t *xr = g < a.B ? xs + g * a.kpx : nullptr;
-        if (si == 0) stream_tiles<FA>(pre, tp, k0, nkt, xr, bsum, lane, acc);
-        else stream_tiles<FB>(pre, tp, k0, nkt, xr, bsum, lane, acc);
+        const XFrag xf{g < a.B ? reinterpret_cast<const uint4 *>(xs) + g * 4 + (lane & 3) : nullptr, 4 * a.B};
+        if (si == 0) stream_tiles<FA>(pre, tp, k0, nkt, xf, bsum, lane, acc);
+        else stream_tiles<FB>(pre, tp, k0, nkt, xf, bsum, lane, acc);
     }
     if (a.wk > 1) {
         *reinterpret_cast<float4 *>(&s_part[(warp * 32 + lane) * 4]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
@@ -441,7 +464,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
 
 inline size_t gemv_smem_bytes(const GemvArgs &a, bool bsum) {
     return (136 + GEMV_MB + 8 * 32 * 4 + (bsum ? a.nblk * GEMV_MB : 0)) * sizeof(float) +
-           (size_t)a.B * a.kpx * sizeof(uint16_t);
+           (size_t)a.B * a.nblk * 64;
 }
 
 // Host helper: choose the k split so the launch covers the GPU, fill the launch parameters.

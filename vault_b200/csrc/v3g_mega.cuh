@@ -64,7 +64,10 @@ struct alignas(16) MkPhase {
 struct MkLite {
     const uint8_t *tiles[3];
     int tbase[4];
-    int rbase[4];         // flat row-tile index where segment s starts; rbase[n_seg] = row tiles of the phase
+    union {
+        int rbase[4];     // host table: flat row-tile index where segment s starts; rbase[n_seg] = row tiles
+        int own[4];       // a CTA's shared copy, from kernel start: [own[0], own[1]) = the CTA's flat tile range
+    };
     int kt[3];            // k tiles per row tile of segment s
     int8_t kind, n_seg;
     int8_t fmt[3];
@@ -130,12 +133,22 @@ struct MkPart {
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-// expect `bytes` on bar and copy them global -> shared (no multicast: a plain CTA-local bulk copy)
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+// L2 policy for streamed weights: evict first, so the weight stream (read once per step) does not push the
+// activations, KV rows and counters that the phases hand each other out of L2
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// expect `bytes` on bar and copy them global -> shared (no multicast: a plain CTA-local bulk copy) under L2 policy pol
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar, uint64_t pol) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+        : "memory");
 }
 
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
@@ -180,20 +193,27 @@ __device__ __forceinline__ int mk_row_tile(const MkLite &L, int R) {
     return L.tbase[si] + (R - L.rbase[si]) * L.kt[si];
 }
 
-// tile range [t0, t1) of consumer warp wi of CTA c (of G) in phase L.  A CTA range of fewer than two chunks per
-// warp is cut at whole chunks (some warps then get none): a full chunk runs the fast path and costs little more
-// than a partial one, and fewer pieces meet in the combine.
-__device__ __forceinline__ void mk_range(const MkLite &L, int c, int G, int wi, int &t0, int &t1) {
+// CTA c (of G) owns the whole row tiles [c NR / G, (c+1) NR / G) of phase L: its flat tile range, computed once
+// per phase at kernel start (it replaces rbase in the CTA's shared copy of the table)
+__device__ __forceinline__ void mk_own_range(MkLite &L, int c, int G) {
     const int NR = L.rbase[L.n_seg];
     const int lo = mk_row_tile(L, (int)((int64_t)c * NR / G)), hi = mk_row_tile(L, (int)((int64_t)(c + 1) * NR / G));
-    const int n = hi - lo;
+    L.own[0] = lo;
+    L.own[1] = hi;
+}
+
+// tile range [t0, t1) of consumer warp wi in phase L (L.own = the CTA's range).  A CTA range of fewer than two
+// chunks per warp is cut at whole chunks (some warps then get none): a full chunk runs the fast path and costs
+// little more than a partial one, and fewer pieces meet in the combine.
+__device__ __forceinline__ void mk_range(const MkLite &L, int wi, int &t0, int &t1) {
+    const int lo = L.own[0], n = L.own[1] - lo;
     if (n < 2 * MK_CHUNK * MK_WARPS) {
         const int nc = (n + MK_CHUNK - 1) / MK_CHUNK;
         t0 = lo + min(n, wi * nc / MK_WARPS * MK_CHUNK);
         t1 = lo + min(n, (wi + 1) * nc / MK_WARPS * MK_CHUNK);
     } else {
-        t0 = lo + (int)((int64_t)wi * n / MK_WARPS);
-        t1 = lo + (int)((int64_t)(wi + 1) * n / MK_WARPS);
+        t0 = lo + wi * n / MK_WARPS;
+        t1 = lo + (wi + 1) * n / MK_WARPS;
     }
 }
 
@@ -207,12 +227,12 @@ __device__ __forceinline__ void mk_seg(const MkLite &L, MkCur &c) {
     c.tiles = L.tiles[c.si];
 }
 
-__device__ __forceinline__ void mk_enter(const MkLite *lite, int n_phases, int cta, int G, int wi, MkCur &c, int p) {
+__device__ __forceinline__ void mk_enter(const MkLite *lite, int n_phases, int wi, MkCur &c, int p) {
     for (; p < n_phases; ++p) {
         const MkLite &L = lite[p];
         if (L.kind != MK_GEMV) continue;
         int t0, t1;
-        mk_range(L, cta, G, wi, t0, t1);
+        mk_range(L, wi, t0, t1);
         if (t0 >= t1) continue;
         c.p = p;
         c.t = t0;
@@ -231,10 +251,10 @@ __device__ __forceinline__ int mk_chunk_n(const MkCur &c) {
 }
 
 // move the cursor past the n tiles of its current chunk
-__device__ __forceinline__ void mk_advance(const MkLite *lite, int n_phases, int cta, int G, int wi, MkCur &c, int n) {
+__device__ __forceinline__ void mk_advance(const MkLite *lite, int n_phases, int wi, MkCur &c, int n) {
     c.t += n;
     if (c.t >= c.t1) {
-        mk_enter(lite, n_phases, cta, G, wi, c, c.p + 1);
+        mk_enter(lite, n_phases, wi, c, c.p + 1);
     } else if (c.t >= c.send) {
         ++c.si;
         mk_seg(lite[c.p], c);
@@ -262,26 +282,24 @@ __device__ __forceinline__ void mk_emit(const Epi &epi, int B, int si, int r, in
 // ---------------------------------------------------------------------------------------------------------------
 // tile arithmetic on shared-memory chunks
 // ---------------------------------------------------------------------------------------------------------------
-// Activation rows: xq = row g of the converted activations + 2t (row 0 for lanes of absent batch rows g >= B: the
-// tensor-core columns they feed are never read), bq = bsum + 2t.  Both are indexed by the k tile.
+// Activations: xq = this lane's fragment records (row g of the converted activations, row 0 for lanes of absent
+// batch rows g >= B: the tensor-core columns they feed are never read, quad position t), xbs = records per 32-wide
+// k block (4 B); bq = bsum + 2t.  See XFrag for the record layout.
 
 // one tile at tb (shared memory) with k tile kt, accumulated into acc (rows g, g+8 x batch 2t, 2t+1)
 template <int FMT>
-__device__ __forceinline__ void mk_tile(const uint8_t *tb, int kt, const uint16_t *xq, const float *bq, int lane,
-                                        float (&acc)[4]) {
-    constexpr int TK = tile_k(FMT);
+__device__ __forceinline__ void mk_tile(const uint8_t *tb, int kt, const uint4 *xq, int xbs, const float *bq,
+                                        int lane, float (&acc)[4]) {
     const int g = lane >> 2;
     const uint4 q = *reinterpret_cast<const uint4 *>(tb + lane * 16);
-    const uint16_t *xk = xq + kt * TK;
     if constexpr (FMT == FMT_Q8) {
         const uint32_t sc = *reinterpret_cast<const uint32_t *>(tb + 512 + g * 4);
+        const uint4 xv = xq[kt * xbs];
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int s = 0; s < 2; ++s)
-            mma16816(d, q8_pair(w[2 * s], 0x4140u), q8_pair(w[2 * s], 0x4342u), q8_pair(w[2 * s + 1], 0x4140u),
-                     q8_pair(w[2 * s + 1], 0x4342u), *reinterpret_cast<const uint32_t *>(xk + 16 * s),
-                     *reinterpret_cast<const uint32_t *>(xk + 16 * s + 8));
+        mma16816(d, q8_pair(q.x, 0x4140u), q8_pair(q.x, 0x4342u), q8_pair(q.y, 0x4140u), q8_pair(q.y, 0x4342u), xv.x,
+                 xv.y);
+        mma16816(d, q8_pair(q.z, 0x4140u), q8_pair(q.z, 0x4342u), q8_pair(q.w, 0x4140u), q8_pair(q.w, 0x4342u), xv.z,
+                 xv.w);
         const float2 S = *reinterpret_cast<const float2 *>(bq + kt * GEMV_MB);
         const float2 ds = h2f2(sc);
         acc[0] = fmaf(ds.x, fmaf(-1152.f, S.x, d[0]), acc[0]);
@@ -293,14 +311,12 @@ __device__ __forceinline__ void mk_tile(const uint8_t *tb, int kt, const uint16_
         const uint32_t w[4] = {q.x, q.y, q.z, q.w}, scw[2] = {sc.x, sc.y};
 #pragma unroll
         for (int blk = 0; blk < 2; ++blk) {
+            const uint4 xv = xq[(2 * kt + blk) * xbs];
             float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int ss = 0; ss < 2; ++ss) {
-                const int s = 2 * blk + ss;
-                mma16816(d, q4_pair<0>(w[s]), q4_pair<4>(w[s]), q4_pair<8>(w[s]), q4_pair<12>(w[s]),
-                         *reinterpret_cast<const uint32_t *>(xk + 16 * s),
-                         *reinterpret_cast<const uint32_t *>(xk + 16 * s + 8));
-            }
+            mma16816(d, q4_pair<0>(w[2 * blk]), q4_pair<4>(w[2 * blk]), q4_pair<8>(w[2 * blk]), q4_pair<12>(w[2 * blk]),
+                     xv.x, xv.y);
+            mma16816(d, q4_pair<0>(w[2 * blk + 1]), q4_pair<4>(w[2 * blk + 1]), q4_pair<8>(w[2 * blk + 1]),
+                     q4_pair<12>(w[2 * blk + 1]), xv.z, xv.w);
             const float2 S = *reinterpret_cast<const float2 *>(bq + (2 * kt + blk) * GEMV_MB);
             const float2 ds = h2f2(scw[blk]);
             acc[0] = fmaf(ds.x, fmaf(-1032.f, S.x, d[0]), acc[0]);
@@ -308,41 +324,48 @@ __device__ __forceinline__ void mk_tile(const uint8_t *tb, int kt, const uint16_
             acc[2] = fmaf(ds.y, fmaf(-1032.f, S.x, d[2]), acc[2]);
             acc[3] = fmaf(ds.y, fmaf(-1032.f, S.y, d[3]), acc[3]);
         }
-    } else if constexpr (FMT == FMT_F32) {   // planes accumulate apart, then hi + 2^-11 mid + 2^-22 lo
-        const uint4 m = *reinterpret_cast<const uint4 *>(tb + 512 + lane * 16);
-        const uint4 l = *reinterpret_cast<const uint4 *>(tb + 1024 + lane * 16);
-        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(xk), b1 = *reinterpret_cast<const uint32_t *>(xk + 8);
-        float dm[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
-        mma16816(acc, q.x, q.y, q.z, q.w, b0, b1);
-        mma16816(dm, m.x, m.y, m.z, m.w, b0, b1);
-        mma16816(dl, l.x, l.y, l.z, l.w, b0, b1);
+    } else {   // 16-wide k tiles: one k16 step, half of a block record
+        const uint2 xv = reinterpret_cast<const uint2 *>(xq + (kt >> 1) * xbs)[kt & 1];
+        if constexpr (FMT == FMT_F32) {   // planes accumulate apart, then hi + 2^-11 mid + 2^-22 lo
+            const uint4 m = *reinterpret_cast<const uint4 *>(tb + 512 + lane * 16);
+            const uint4 l = *reinterpret_cast<const uint4 *>(tb + 1024 + lane * 16);
+            float dm[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
+            mma16816(acc, q.x, q.y, q.z, q.w, xv.x, xv.y);
+            mma16816(dm, m.x, m.y, m.z, m.w, xv.x, xv.y);
+            mma16816(dl, l.x, l.y, l.z, l.w, xv.x, xv.y);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[i] = fmaf(dm[i], F32_MID, fmaf(dl[i], F32_LO, acc[i]));
-    } else {   // fp16 tiles (F16 files, BF16 weights stored as scaled fp16)
-        mma16816(acc, q.x, q.y, q.z, q.w, *reinterpret_cast<const uint32_t *>(xk),
-                 *reinterpret_cast<const uint32_t *>(xk + 8));
+            for (int i = 0; i < 4; ++i) acc[i] = fmaf(dm[i], F32_MID, fmaf(dl[i], F32_LO, acc[i]));
+        } else {   // fp16 tiles (F16 files, BF16 weights stored as scaled fp16)
+            mma16816(acc, q.x, q.y, q.z, q.w, xv.x, xv.y);
+        }
     }
 }
 
 // MK_GROUP consecutive tiles of one row tile: every shared load first, then the tensor-core chains
 template <int FMT>
-__device__ __forceinline__ void mk_chunk_fast(const uint8_t *sb, int kt, const uint16_t *xq, const float *bq, int lane,
-                                              float (&acc)[4]) {
-    constexpr int TB = tile_bytes(FMT), TK = tile_k(FMT), NS = TK / 16, N = MK_GROUP;
+__device__ __forceinline__ void mk_chunk_fast(const uint8_t *sb, int kt, const uint4 *xq, int xbs, const float *bq,
+                                              int lane, float (&acc)[4]) {
+    constexpr int TB = tile_bytes(FMT), N = MK_GROUP;
     const int g = lane >> 2;
-    const uint16_t *xk = xq + kt * TK;
     uint4 q[N];
     uint2 sc[N];
-    uint32_t b0[N][NS], b1[N][NS];
+    uint32_t b0[N][2], b1[N][2];   // Q4 reads two records per tile below; Q8 / 16-bit tiles fill these
 #pragma unroll
     for (int i = 0; i < N; ++i) {
         q[i] = *reinterpret_cast<const uint4 *>(sb + i * TB + lane * 16);
-        if constexpr (FMT == FMT_Q8) sc[i].x = *reinterpret_cast<const uint32_t *>(sb + i * TB + 512 + g * 4);
-        if constexpr (FMT == FMT_Q4) sc[i] = *reinterpret_cast<const uint2 *>(sb + i * TB + 512 + g * 8);
-#pragma unroll
-        for (int s = 0; s < NS; ++s) {
-            b0[i][s] = *reinterpret_cast<const uint32_t *>(xk + i * TK + 16 * s);
-            b1[i][s] = *reinterpret_cast<const uint32_t *>(xk + i * TK + 16 * s + 8);
+        if constexpr (FMT == FMT_Q8) {
+            sc[i].x = *reinterpret_cast<const uint32_t *>(sb + i * TB + 512 + g * 4);
+            const uint4 xv = xq[(kt + i) * xbs];
+            b0[i][0] = xv.x;
+            b1[i][0] = xv.y;
+            b0[i][1] = xv.z;
+            b1[i][1] = xv.w;
+        } else if constexpr (FMT == FMT_Q4) {
+            sc[i] = *reinterpret_cast<const uint2 *>(sb + i * TB + 512 + g * 8);
+        } else {
+            const uint2 xv = reinterpret_cast<const uint2 *>(xq + ((kt + i) >> 1) * xbs)[(kt + i) & 1];
+            b0[i][0] = xv.x;
+            b1[i][0] = xv.y;
         }
     }
     if constexpr (FMT == FMT_Q8) {
@@ -372,13 +395,12 @@ __device__ __forceinline__ void mk_chunk_fast(const uint8_t *sb, int kt, const u
             const uint32_t w[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
 #pragma unroll
             for (int blk = 0; blk < 2; ++blk) {
+                const uint4 xv = xq[(2 * (kt + i) + blk) * xbs];
                 d[i][blk][0] = d[i][blk][1] = d[i][blk][2] = d[i][blk][3] = 0.f;
-#pragma unroll
-                for (int ss = 0; ss < 2; ++ss) {
-                    const int s = 2 * blk + ss;
-                    mma16816(d[i][blk], q4_pair<0>(w[s]), q4_pair<4>(w[s]), q4_pair<8>(w[s]), q4_pair<12>(w[s]),
-                             b0[i][s], b1[i][s]);
-                }
+                mma16816(d[i][blk], q4_pair<0>(w[2 * blk]), q4_pair<4>(w[2 * blk]), q4_pair<8>(w[2 * blk]),
+                         q4_pair<12>(w[2 * blk]), xv.x, xv.y);
+                mma16816(d[i][blk], q4_pair<0>(w[2 * blk + 1]), q4_pair<4>(w[2 * blk + 1]), q4_pair<8>(w[2 * blk + 1]),
+                         q4_pair<12>(w[2 * blk + 1]), xv.z, xv.w);
             }
         }
 #pragma unroll
@@ -428,16 +450,16 @@ struct MkRing {
 // them); warps without tiles in the phase only take part in the combine.
 template <int FA, int FB, class Epi>
 __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkRing &R, const MkLite *lite,
-                                           int n_phases, int p, int cta, int G, int wi, const uint16_t *xq,
+                                           int n_phases, int p, int cta, int G, int wi, const uint4 *xq,
                                            const float *bq, const float *s_scale, MkPart &part, int *status,
                                            int lane) {
-    const int t = lane & 3, B = P.a.B;
+    const int t = lane & 3, B = P.a.B, xbs = 4 * B;
     const float sc0 = 2 * t < B ? s_scale[2 * t] : 0.f, sc1 = 2 * t + 1 < B ? s_scale[2 * t + 1] : 0.f;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     int cur_si = -1, cur_r = -1;
     int tail_si = -1, tail_r = -1;   // split row tile begun in this warp, finished after the phase
     int t0w = 0, t1w = 0;
-    mk_range(lite[p], cta, G, wi, t0w, t1w);
+    mk_range(lite[p], wi, t0w, t1w);
     if (lane == 0) part.head_row[wi] = t0w < t1w ? -1 : -2;
     auto flush = [&]() {   // the finished piece of row tile (cur_si, cur_r)
         const float ws = P.a.seg[cur_si].wscale, s0 = sc0 * ws, s1 = sc1 * ws;
@@ -478,8 +500,8 @@ __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkR
             if (n == MK_CHUNK && kt + MK_CHUNK <= KT && !(fa ? F32A : F32B)) {   // whole chunk in one row tile
 #pragma unroll
                 for (int g0 = 0; g0 < MK_CHUNK; g0 += MK_GROUP) {
-                    if (fa) mk_chunk_fast<F32A ? FMT_Q8 : FA>(sb + g0 * tbytes, kt + g0, xq, bq, lane, acc);
-                    else mk_chunk_fast<F32B ? FMT_Q8 : FB>(sb + g0 * tbytes, kt + g0, xq, bq, lane, acc);
+                    if (fa) mk_chunk_fast<F32A ? FMT_Q8 : FA>(sb + g0 * tbytes, kt + g0, xq, xbs, bq, lane, acc);
+                    else mk_chunk_fast<F32B ? FMT_Q8 : FB>(sb + g0 * tbytes, kt + g0, xq, xbs, bq, lane, acc);
                 }
                 kt += MK_CHUNK;
                 if (kt == KT) kt = 0;
@@ -490,13 +512,13 @@ __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkR
                     acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
                 }
                 if (i + MK_GROUP <= n && kt + MK_GROUP <= KT && !(fa ? F32A : F32B)) {
-                    if (fa) mk_chunk_fast<F32A ? FMT_Q8 : FA>(sb + i * tbytes, kt, xq, bq, lane, acc);
-                    else mk_chunk_fast<F32B ? FMT_Q8 : FB>(sb + i * tbytes, kt, xq, bq, lane, acc);
+                    if (fa) mk_chunk_fast<F32A ? FMT_Q8 : FA>(sb + i * tbytes, kt, xq, xbs, bq, lane, acc);
+                    else mk_chunk_fast<F32B ? FMT_Q8 : FB>(sb + i * tbytes, kt, xq, xbs, bq, lane, acc);
                     i += MK_GROUP;
                     kt += MK_GROUP;
                 } else {
-                    if (fa) mk_tile<FA>(sb + i * tbytes, kt, xq, bq, lane, acc);
-                    else mk_tile<FB>(sb + i * tbytes, kt, xq, bq, lane, acc);
+                    if (fa) mk_tile<FA>(sb + i * tbytes, kt, xq, xbs, bq, lane, acc);
+                    else mk_tile<FB>(sb + i * tbytes, kt, xq, xbs, bq, lane, acc);
                     ++i;
                     ++kt;
                 }
@@ -509,7 +531,7 @@ __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkR
             R.slot = 0;
             R.phase ^= 1u;
         }
-        mk_advance(lite, n_phases, cta, G, wi, R.cons, n);
+        mk_advance(lite, n_phases, wi, R.cons, n);
     }
     if (cur_r >= 0) flush();
     sync_threads(MK_CT);   // every piece of every split row tile is in shared memory
@@ -569,7 +591,7 @@ struct MkEpiAny {
 template <int FA, int FB>
 __device__ __forceinline__ void mk_consume_epi(const MkPhase &P, const ModelDev *mp, MkMisc &ms, MkRing &R,
                                                const MkLite *lite, int n_phases, int p, int cta, int G, int wi,
-                                               const uint16_t *xq, const float *bq, const float *s_scale,
+                                               const uint4 *xq, const float *bq, const float *s_scale,
                                                MkPart &part, int *status, int lane) {
     const MkEpiAny e{&P, mp, &ms};
     mk_consume<FA, FB>(P, e, R, lite, n_phases, p, cta, G, wi, xq, bq, s_scale, part, status, lane);
@@ -588,8 +610,9 @@ __device__ __forceinline__ void mk_produce(const MkLite *lite, int n_phases, int
     const uint32_t full = smem_u32(smem + cfg.bar_off) + (uint32_t)(lane * S * 8);
     const uint32_t empty = full + (uint32_t)(MK_WARPS * S * 8);
     MkCur cur;
-    mk_enter(lite, n_phases, c, G, lane, cur, 0);
+    mk_enter(lite, n_phases, lane, cur, 0);
     uint32_t slot = 0, round = 0, idle = 0;
+    const uint64_t pol = l2_evict_first();
     while (cur.p < n_phases) {
         if (round > 0 && !mbar_test(empty + slot * 8, (round - 1) & 1u)) {   // slot still in use
             if (++idle > MK_WAIT_LIMIT) {
@@ -602,8 +625,8 @@ __device__ __forceinline__ void mk_produce(const MkLite *lite, int n_phases, int
         idle = 0;
         const int n = mk_chunk_n(cur);
         const int tb = tile_bytes(cur.fmt);
-        bulk_load(buf + slot * MK_SLOT_BYTES, cur.tiles + (size_t)cur.tl * tb, (uint32_t)(n * tb), full + slot * 8);
-        mk_advance(lite, n_phases, c, G, lane, cur, n);
+        bulk_load(buf + slot * MK_SLOT_BYTES, cur.tiles + (size_t)cur.tl * tb, (uint32_t)(n * tb), full + slot * 8, pol);
+        mk_advance(lite, n_phases, lane, cur, n);
         if (++slot == (uint32_t)S) {
             slot = 0;
             ++round;
@@ -668,6 +691,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
+    for (int p = threadIdx.x; p < n_phases; p += blockDim.x)   // this CTA's tile range of every GEMV phase
+        if (lite[p].kind == MK_GEMV) mk_own_range(lite[p], c, G);
+    __syncthreads();
     if (warp == MK_WARPS) {   // weights are immutable: the producer streams from the very start
         mk_produce(lite, n_phases, c, G, cfg, smem, sp);
         return;
@@ -716,7 +742,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
     R.slot = 0;
     R.phase = 0;
     R.dead = false;
-    mk_enter(lite, n_phases, c, G, warp, R.cons, 0);
+    mk_enter(lite, n_phases, warp, R.cons, 0);
     MkPart &part = *reinterpret_cast<MkPart *>(smem + cfg.part_off);
     const int n_kv = st.G, ms = st.max_splits, Bst = st.B;
     unsigned int *gbar = st.bar;
@@ -736,8 +762,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
         } else {
             uint16_t *xs = reinterpret_cast<uint16_t *>(bsum + (BSUM ? P.a.nblk * GEMV_MB : 0));
             if (P.epi == MK_EPI_QKV && threadIdx.x >= MK_CT - 32) {   // the last warp stages this CTA's biases
-                const MkLite &Lq = lite[p];
-                const int NR = Lq.rbase[Lq.n_seg];
+                const int NR = P.a.total_rtiles;
                 const int r0 = (int)((int64_t)c * NR / G), r1 = (int)((int64_t)(c + 1) * NR / G);
                 const int n = r1 - r0 <= MK_OWN_TILES ? r1 - r0 : 0;
                 for (int i = threadIdx.x - (MK_CT - 32); i < n * 16; i += 32) {
@@ -758,7 +783,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
                 asm volatile("cp.async.commit_group;" ::: "memory");
             }
             const int g = lane >> 2, t = lane & 3;
-            const uint16_t *xq = xs + (g < P.a.B ? g : 0) * P.a.kpx + 2 * t;   // absent rows: columns never read
+            const uint4 *xq = reinterpret_cast<const uint4 *>(xs) + (g < P.a.B ? g : 0) * 4 + t;   // absent rows: row 0
             mk_consume_epi<FA, FB>(P, mp, misc, R, lite, n_phases, p, c, G, warp, xq, bsum + 2 * t, s_scale, part,
                                    status, lane);
         }
