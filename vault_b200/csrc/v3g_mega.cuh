@@ -179,6 +179,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 // ---------------------------------------------------------------------------------------------------------------
 struct MkCur {
     int p, si;            // phase (n_phases when exhausted) and segment of the next chunk
+    int pend;             // 1: the range in phase p - 1 ended; the next range is searched from phase p (mk_grid_sync)
     int t, t1, send;      // next flat tile, end of this warp's range in phase p, end of the run in segment si
     int tl;               // tile index of t inside segment si
     int r, kt, KT;        // row tile / k tile of tl, k tiles per row tile
@@ -228,6 +229,7 @@ __device__ __forceinline__ void mk_seg(const MkLite &L, MkCur &c) {
 }
 
 __device__ __forceinline__ void mk_enter(const MkLite *lite, int n_phases, int wi, MkCur &c, int p) {
+    c.pend = 0;
     for (; p < n_phases; ++p) {
         const MkLite &L = lite[p];
         if (L.kind != MK_GEMV) continue;
@@ -250,11 +252,19 @@ __device__ __forceinline__ int mk_chunk_n(const MkCur &c) {
     return c.send - c.t < cap ? c.send - c.t : cap;
 }
 
-// move the cursor past the n tiles of its current chunk
+// move the cursor past the n tiles of its current chunk.  LAZY: at the end of the range only mark the cursor
+// pending (phase p + 1, searched later) -- the consumer warps look up their next range while they wait at the grid
+// barrier instead of before the phase's closing combine
+template <bool LAZY>
 __device__ __forceinline__ void mk_advance(const MkLite *lite, int n_phases, int wi, MkCur &c, int n) {
     c.t += n;
     if (c.t >= c.t1) {
-        mk_enter(lite, n_phases, wi, c, c.p + 1);
+        if (LAZY) {
+            ++c.p;
+            c.pend = 1;
+        } else {
+            mk_enter(lite, n_phases, wi, c, c.p + 1);
+        }
     } else if (c.t >= c.send) {
         ++c.si;
         mk_seg(lite[c.p], c);
@@ -531,7 +541,7 @@ __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkR
             R.slot = 0;
             R.phase ^= 1u;
         }
-        mk_advance(lite, n_phases, wi, R.cons, n);
+        mk_advance<true>(lite, n_phases, wi, R.cons, n);
     }
     if (cur_r >= 0) flush();
     sync_threads(MK_CT);   // every piece of every split row tile is in shared memory
@@ -626,7 +636,7 @@ __device__ __forceinline__ void mk_produce(const MkLite *lite, int n_phases, int
         const int n = mk_chunk_n(cur);
         const int tb = tile_bytes(cur.fmt);
         bulk_load(buf + slot * MK_SLOT_BYTES, cur.tiles + (size_t)cur.tl * tb, (uint32_t)(n * tb), full + slot * 8, pol);
-        mk_advance(lite, n_phases, lane, cur, n);
+        mk_advance<false>(lite, n_phases, lane, cur, n);
         if (++slot == (uint32_t)S) {
             slot = 0;
             ++round;
@@ -651,11 +661,15 @@ __device__ __forceinline__ void mk_fetch_phase(const MkPhase *phases, int p, int
 }
 
 // bounded grid barrier over the consumer warps: every CTA arrives once per phase on a counter zeroed at the start
-// of the step; a wait that exceeds its iteration limit records STATUS_TIMEOUT and returns (results then invalid)
-__device__ __forceinline__ void mk_grid_sync(unsigned int *bar, unsigned int target, int *status) {
+// of the step; a wait that exceeds its iteration limit records STATUS_TIMEOUT and returns (results then invalid).
+// Between the CTA's arrival and the wait each consumer warp moves a pending chunk cursor to its next range.
+__device__ __forceinline__ void mk_grid_sync(unsigned int *bar, unsigned int target, int *status, const MkLite *lite,
+                                             int n_phases, int wi, MkCur &cur) {
     sync_threads(MK_CT);
-    if (threadIdx.x == 0) {   // release-add (the CTA's writes, ordered by the barrier above), then acquire-poll
+    if (threadIdx.x == 0)   // release-add (the CTA's writes, ordered by the barrier above)
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+    if (cur.pend) mk_enter(lite, n_phases, wi, cur, cur.p);
+    if (threadIdx.x == 0) {   // acquire-poll
         unsigned int v = 0;
         for (uint32_t spins = 0;; ++spins) {
             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
@@ -789,7 +803,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
         }
         if (p + 1 < n_phases) {
             asm volatile("cp.async.wait_all;" ::: "memory");   // descriptor p + 1 is in place after the barrier
-            mk_grid_sync(gbar, (unsigned int)(p + 1) * (unsigned int)G, status);
+            mk_grid_sync(gbar, (unsigned int)(p + 1) * (unsigned int)G, status, lite, n_phases, warp, R.cons);
             mk_fetch_phase(phases, p + 2, n_phases, ph_s + (p & 1));   // slot of phase p, now unused
         }
     }
