@@ -177,14 +177,17 @@ __device__ __forceinline__ void stream_tiles(TileRegs (&pre)[GEMV_U], const uint
     }
 }
 
-// 16 consecutive fp32 values of a row; four 16-byte loads in flight when the row is made of whole 16-byte-aligned
-// 32-blocks, else guarded scalar loads (zero past n).  L2 loads for activations (written by other SMs).
+// 2^e for an integer e in [-126, 127], built from its exponent bits (exact)
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
+
+// 8 consecutive fp32 values of a row: two 16-byte loads when the row is made of whole 16-byte-aligned 32-blocks,
+// else guarded scalar loads (zero past n).  L2: L1-bypassing loads (activations written by other SMs).
 template <bool L2>
-__device__ __forceinline__ void load16(const float *p, bool vec, int n, float (&v)[16]) {
+__device__ __forceinline__ void load8(const float *p, bool vec, int n, float (&v)[8]) {
     if (vec) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float4 q = L2 ? __ldcg(reinterpret_cast<const float4 *>(p) + j) : __ldg(reinterpret_cast<const float4 *>(p) + j);
+        for (int j = 0; j < 2; ++j) {
+            const float4 q = L2 ? __ldcg(reinterpret_cast<const float4 *>(p) + j) : reinterpret_cast<const float4 *>(p)[j];
             v[4 * j] = q.x;
             v[4 * j + 1] = q.y;
             v[4 * j + 2] = q.z;
@@ -192,45 +195,24 @@ __device__ __forceinline__ void load16(const float *p, bool vec, int n, float (&
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = j < n ? (L2 ? __ldcg(p + j) : __ldg(p + j)) : 0.f;
+        for (int j = 0; j < 8; ++j) v[j] = j < n ? (L2 ? __ldcg(p + j) : p[j]) : 0.f;
     }
 }
-
-// 16 norm weights through a generic pointer: the vector in global memory, or a shared-memory copy of it that the
-// caller staged
-__device__ __forceinline__ void load16_norm(const float *p, bool vec, int n, float (&w)[16]) {
-    if (vec) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float4 q = reinterpret_cast<const float4 *>(p)[j];
-            w[4 * j] = q.x;
-            w[4 * j + 1] = q.y;
-            w[4 * j + 2] = q.z;
-            w[4 * j + 3] = q.w;
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) w[j] = j < n ? p[j] : 0.f;
-    }
-}
-
-// 2^e for an integer e in [-126, 127], built from its exponent bits (exact)
-__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
 
 // Convert the pass's activation rows once per CTA into shared memory: RMSNorm (optional), fp16 with a per-row
 // power-of-two scale (largest |x| scaled into (2^13, 2^14]); s_scale[b] receives the scale to undo and, with
-// BSUM, bsum[blk * 8 + b] the fp32 sum of converted 32-wide block blk of row b.  Work items are half blocks (16
-// values; the two halves of a block sit in adjacent lanes): one stats pass and one convert pass.  A thread keeps
-// its first items in registers between the passes -- CACHE of them without RMSNorm, one item and its norm weights
-// (in the last cache slot) with it -- so such rows cost one round trip to L2.  nw_s: optional shared-memory copy
-// of the norm weights (a.norm_w).
+// BSUM, bsum[blk * 8 + b] the fp32 sum of converted 32-wide block blk of row b.  Work items are quarter blocks
+// (8 values; the four quarters of a block sit in adjacent lanes), so a 1536-wide row keeps 192 threads busy: one
+// stats pass and one convert pass.  A thread keeps its first items in registers between the passes -- CACHE of
+// them without RMSNorm, one item and its norm weights (in the last cache slot) with it -- so such rows cost one
+// round trip to L2.  nw_s: optional shared-memory copy of the norm weights (a.norm_w).
 template <bool BSUM, int CACHE = 0>
 __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_scale, float *s_red, float *bsum,
                                      int nt, const float *nw_s = nullptr) {
     const int tid = threadIdx.x, nw = nt / 32;
     const bool norm = a.prologue == PRO_RMSNORM;
     const bool vec = (a.K & 31) == 0 && (a.x_ld & 3) == 0;
-    const int nb = (a.K + 31) >> 5, nh = 2 * nb, items = a.B * nh;
+    const int nb = (a.K + 31) >> 5, nq = 4 * nb, items = a.B * nq;
     const float *nwp = nw_s ? nw_s : a.norm_w;
     const float inv_k = 1.0f / (float)a.K;
     float ss[GEMV_MB], mx[GEMV_MB];
@@ -240,16 +222,19 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         mx[b] = 0.f;
     }
     constexpr int NC = CACHE > 1 ? CACHE : 2;
-    float vc[NC][16];
-    float (&wc)[16] = vc[NC - 1];               // norm weights of the first item (RMSNorm)
+    float vc[NC][8];
+    float (&wc)[8] = vc[NC - 1];                // norm weights of the first item (RMSNorm)
     const int ncache = CACHE == 0 ? 0 : (norm ? 1 : CACHE);
-    auto stats = [&](int b, const float (&v)[16], const float (&w)[16]) {
-        float s2 = 0.f, m = 0.f;
+    auto stats = [&](int b, const float (&v)[8], const float (&w)[8]) {
+        float s2a = 0.f, s2b = 0.f, ma = 0.f, mb = 0.f;   // two chains each
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            s2 = fmaf(v[j], v[j], s2);
-            m = fmaxf(m, fabsf(norm ? v[j] * w[j] : v[j]));
+        for (int j = 0; j < 8; j += 2) {
+            s2a = fmaf(v[j], v[j], s2a);
+            s2b = fmaf(v[j + 1], v[j + 1], s2b);
+            ma = fmaxf(ma, fabsf(norm ? v[j] * w[j] : v[j]));
+            mb = fmaxf(mb, fabsf(norm ? v[j + 1] * w[j + 1] : v[j + 1]));
         }
+        const float s2 = s2a + s2b, m = fmaxf(ma, mb);
 #pragma unroll
         for (int bb = 0; bb < GEMV_MB; ++bb)
             if (bb == b) {
@@ -261,21 +246,21 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
     for (int k = 0; k < CACHE; ++k) {   // cached items: loads of all of them in flight together
         const int it = tid + k * nt;
         if (k < ncache && it < items) {
-            const int b = it / nh, h = it - b * nh, n = a.K - h * 16;
-            load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, vc[k]);
-            if (k == 0 && norm) load16_norm(nwp + h * 16, vec, n, wc);
+            const int b = it / nq, u = it - b * nq, n = a.K - u * 8;
+            load8<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + u * 8, vec, n, vc[k]);
+            if (k == 0 && norm) load8<false>(nwp + u * 8, vec, n, wc);
         }
     }
 #pragma unroll
     for (int k = 0; k < CACHE; ++k) {
         const int it = tid + k * nt;
-        if (k < ncache && it < items) stats(it / nh, vc[k], wc);
+        if (k < ncache && it < items) stats(it / nq, vc[k], wc);
     }
     for (int it = tid + ncache * nt; it < items; it += nt) {
-        const int b = it / nh, h = it - b * nh, n = a.K - h * 16;
-        float v[16], w[16];
-        load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, v);
-        if (norm) load16_norm(nwp + h * 16, vec, n, w);
+        const int b = it / nq, u = it - b * nq, n = a.K - u * 8;
+        float v[8], w[8];
+        load8<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + u * 8, vec, n, v);
+        if (norm) load8<false>(nwp + u * 8, vec, n, w);
         stats(b, v, w);
     }
 #pragma unroll
@@ -322,13 +307,14 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         cb = tid;
         s_scale[tid] = sc;
     }
-    auto convert = [&](bool act, int b, int h, int n, const float (&v)[16], const float (&w)[16]) {
+    uint32_t *xw = reinterpret_cast<uint32_t *>(xs);
+    auto convert = [&](bool act, int b, int u, int n, const float (&v)[8], const float (&w)[8]) {
         float bs = 0.f;
         if (act) {
             if (a.feat && blockIdx.x == 0) {
-                float *f = a.feat + (size_t)(a.b0 + b) * a.feat_ld + h * 16;
+                float *f = a.feat + (size_t)(a.b0 + b) * a.feat_ld + u * 8;
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
+                for (int j = 0; j < 8; ++j)
                     if (j < n) f[j] = v[j];
             }
             if (b != cb) {
@@ -337,25 +323,25 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
                 cb = b;
             }
             const float mul = cmul;
-            uint32_t hw[8];
+            // quarter u of block u / 4 holds the fp16 pairs t = 0..3 of word (u & 3) in the records (block, b, t)
+            uint32_t *dst = xw + ((size_t)(u >> 2) * a.B + b) * 16 + (u & 3);
+            float bs2 = 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float x0 = (norm ? v[2 * j] * w[2 * j] : v[2 * j]) * mul;
-                const float x1 = (norm ? v[2 * j + 1] * w[2 * j + 1] : v[2 * j + 1]) * mul;
+            for (int t = 0; t < 4; ++t) {
+                const float x0 = (norm ? v[2 * t] * w[2 * t] : v[2 * t]) * mul;
+                const float x1 = (norm ? v[2 * t + 1] * w[2 * t + 1] : v[2 * t + 1]) * mul;
                 const __half2 hv = __floats2half2_rn(x0, x1);
                 const float2 back = __half22float2(hv);
-                bs += back.x + back.y;
-                hw[j] = *reinterpret_cast<const uint32_t *>(&hv);
+                if (t & 1) bs2 += back.x + back.y;
+                else bs += back.x + back.y;
+                dst[4 * t] = *reinterpret_cast<const uint32_t *>(&hv);
             }
-            // fragment-major records of block h / 2, row b: lane quad t takes pairs t (b0) and t + 4 (b1) of
-            // this half block, at the record's k16 step h & 1
-            uint2 *dst = reinterpret_cast<uint2 *>(reinterpret_cast<uint4 *>(xs) + ((size_t)(h >> 1) * a.B + b) * 4) + (h & 1);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) dst[2 * q] = make_uint2(hw[q], hw[q + 4]);
+            bs += bs2;
         }
-        if (BSUM) {   // the two halves of a block sit in adjacent lanes (warp-uniform call)
+        if (BSUM) {   // the four quarters of a block sit in adjacent lanes (warp-uniform call)
             bs += __shfl_xor_sync(0xffffffffu, bs, 1);
-            if (act && (h & 1) == 0) bsum[(h >> 1) * GEMV_MB + b] = bs;
+            bs += __shfl_xor_sync(0xffffffffu, bs, 2);
+            if (act && (u & 3) == 0) bsum[(u >> 2) * GEMV_MB + b] = bs;
         }
     };
     int base = 0;
@@ -364,20 +350,20 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         if (k >= ncache || base >= items) break;
         const int it = base + tid;
         const bool act = it < items;
-        const int b = act ? it / nh : 0, h = act ? it - b * nh : 0, n = a.K - h * 16;
-        convert(act, b, h, n, vc[k], wc);
+        const int b = act ? it / nq : 0, u = act ? it - b * nq : 0, n = a.K - u * 8;
+        convert(act, b, u, n, vc[k], wc);
         base += nt;
     }
     for (; base < items; base += nt) {   // warp-uniform trip count
         const int it = base + tid;
         const bool act = it < items;
-        const int b = act ? it / nh : 0, h = act ? it - b * nh : 0, n = a.K - h * 16;
-        float v[16], w[16];
+        const int b = act ? it / nq : 0, u = act ? it - b * nq : 0, n = a.K - u * 8;
+        float v[8], w[8];
         if (act) {
-            load16<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + h * 16, vec, n, v);
-            if (norm) load16_norm(nwp + h * 16, vec, n, w);
+            load8<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + u * 8, vec, n, v);
+            if (norm) load8<false>(nwp + u * 8, vec, n, w);
         }
-        convert(act, b, h, n, v, w);
+        convert(act, b, u, n, v, w);
     }
     // zero the records and block sums of padding blocks (tiles may extend past K).  Absent batch rows (b >= B) have
     // no records: their lanes read row 0, whose tensor-core columns are computed and never read.

@@ -791,7 +791,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
                 }
             }
             float *nw_s = reinterpret_cast<float *>(smem + cfg.nw_off);
-            gemv_prologue<BSUM, 3>(P.a, xs, s_scale, s_red, bsum, MK_CT, P.norm_staged ? nw_s : nullptr);
+            // a CTA without row tiles in this phase converts nothing (CTA 0 still captures scorer features)
+            if (lite[p].own[1] > lite[p].own[0] || (P.a.feat && c == 0))
+                gemv_prologue<BSUM, 5>(P.a, xs, s_scale, s_red, bsum, MK_CT, P.norm_staged ? nw_s : nullptr);
             if (P.next_norm) {   // stage the next phase's norm weights while this one streams (landed by the barrier)
                 for (int i = threadIdx.x; i < P.next_k / 4; i += MK_CT) cp_async16(nw_s + 4 * i, P.next_norm + 4 * i);
                 asm volatile("cp.async.commit_group;" ::: "memory");
