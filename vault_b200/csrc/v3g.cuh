@@ -60,6 +60,8 @@ constexpr int MAX_SEG_BUDGET = 16384;
 constexpr int GEMV_MB = 8;             // batch rows per GEMV pass (mma rows 0..7)
 constexpr int GEMV_THREADS = 256;
 constexpr int ATT_KEYS_PER_CTA = 64;   // split-KV chunk
+constexpr int ATT_MERGE_MAX = 4;        // persistent kernel: up to this many splits are merged by their reader
+__host__ __device__ constexpr int att_part_stride(int D) { return D + 4; }   // partial row: o[D], m, l, 2 pad
 constexpr int ATT_THREADS = 128;
 constexpr int GEMV_MAX_SMEM = 220 * 1024;   // launch-time cap (below the 227 KB opt-in minus static smem)
 
@@ -138,7 +140,7 @@ struct StateDev {
     float *attn;                 // [B][H*D]
     float *hbuf;                 // [B][F]
     float *q_cur, *q_far;        // [B][H][D]
-    float *att_part;             // [B][G][max_splits][grp][D + 2]
+    float *att_part;             // [B][G][max_splits][grp][att_part_stride(D)]
     uint32_t *att_cnt;           // [B][G]
     float *logits;               // [B][V]
     unsigned long long *amax;    // [B]

@@ -575,7 +575,7 @@ Layout make_layout(const ModelDev &md, int B, int seg_cap) {
     L.off_h = take((uint64_t)B * md.F * 4);
     L.off_qc = take((uint64_t)B * md.H * md.D * 4);
     L.off_qf = take((uint64_t)B * md.H * md.D * 4);
-    L.off_part = take((uint64_t)B * md.G * L.max_splits * grp * (md.D + 2) * 4);
+    L.off_part = take((uint64_t)B * md.G * L.max_splits * grp * att_part_stride(md.D) * 4);
     L.off_cnt = take((uint64_t)B * md.G * 4);
     L.off_logits = take((uint64_t)B * md.vocab * 4);
     L.off_amax = take((uint64_t)B * 8);

@@ -77,6 +77,46 @@ __device__ __forceinline__ void split_half(float v, __half &hi, __half &lo) {
     lo = __float2half_rn(v - __half2float(hi));
 }
 
+// 8 consecutive attention outputs e0 .. e0 + 7 of sequence b (inside one head: e0 = head * D + dd, dd a multiple
+// of 8), merged from the n_splits (2 .. ATT_MERGE_MAX) unnormalised partials of the head's KV group in split
+// order, with the arithmetic of attn_item's last-CTA merge (same results, bit for bit).  Out of line: inlined into
+// the unrolled prologue, the partials of several items crowd its registers.
+template <int D>
+__device__ __noinline__ void attn_merged8(const StateDev &s, int b, int e0, int n_splits, float (&v)[8]) {
+    constexpr int PS = att_part_stride(D);
+    const int grp = s.H / s.G, head = e0 / D, dd = e0 - head * D, g = head / grp, hr = head - g * grp;
+    const float *p0 = s.att_part + ((((size_t)b * s.G + g) * s.max_splits) * grp + hr) * PS;
+    float4 o[ATT_MERGE_MAX][2];
+    float2 ml[ATT_MERGE_MAX];
+#pragma unroll
+    for (int sp = 0; sp < ATT_MERGE_MAX; ++sp) {   // every load in flight at once
+        if (sp < n_splits) {
+            const float *pp = p0 + (size_t)sp * grp * PS;
+            o[sp][0] = __ldcg(reinterpret_cast<const float4 *>(pp + dd));
+            o[sp][1] = __ldcg(reinterpret_cast<const float4 *>(pp + dd + 4));
+            ml[sp] = __ldcg(reinterpret_cast<const float2 *>(pp + D));
+        }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int sp = 0; sp < ATT_MERGE_MAX; ++sp)
+        if (sp < n_splits) M = fmaxf(M, ml[sp].x);
+    float L = 0.f, O[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int sp = 0; sp < ATT_MERGE_MAX; ++sp) {
+        if (sp < n_splits) {
+            const float w = expf(ml[sp].x - M);
+            L = fmaf(ml[sp].y, w, L);
+            const float ov[8] = {o[sp][0].x, o[sp][0].y, o[sp][0].z, o[sp][0].w,
+                                 o[sp][1].x, o[sp][1].y, o[sp][1].z, o[sp][1].w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) O[j] = fmaf(ov[j], w, O[j]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = O[j] / L;
+}
+
 // One work item = ATT_KPC keys of one (sequence b, KV head g) for its `grp` query heads, run by one CTA on the
 // tensor cores.  All K and V rows of the chunk are staged in shared memory with cp.async (one round trip).  Scores:
 // for each block of 8 keys, mma steps over the head dimension with A = the group's queries (rows 0-7 their high
@@ -85,11 +125,13 @@ __device__ __forceinline__ void split_half(float v, __half &hi, __half &lo) {
 // others with the query at W + c (both kinds only where a key block holds both).  One warp per head forms the
 // softmax pieces (m, l, p), and P V runs the same way: A = probabilities split high / low, B = V read transposed
 // with ldmatrix.  The CTA writes an unnormalised partial (o, m, l); the last CTA of (b, g) merges the partials in
-// split order into s.attn.  ks = key_span(s, b, pos).  Returns false when the split is empty.
+// split order into s.attn.  With defer_merge (the persistent kernel) a span of at most ATT_MERGE_MAX splits is
+// left as partials, which the next phase's activation prologue merges the same way (attn_merged8).
+// ks = key_span(s, b, pos).  Returns false when the split is empty.
 template <int D>
 __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float scale, int split, int g, int b,
-                          int64_t pos, AttnSmem<D> &sm, int nt) {
-    constexpr int KP = D + 8, CH = D / 8;
+                          int64_t pos, AttnSmem<D> &sm, int nt, bool defer_merge = false) {
+    constexpr int KP = D + 8, CH = D / 8, PS = att_part_stride(D);
     static_assert(D % 16 == 0 && ATT_KPC % 16 == 0, "mma shapes");
     const int H = s.H, G = s.G, grp = H / G;
     const int n_splits = (ks.total + ATT_KPC - 1) / ATT_KPC;
@@ -174,7 +216,7 @@ __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float
     sync_threads(nt);
     // P V for the 8-column blocks nb = warp, warp + nwarp, ...: lane (gq, t) ends with head gq, columns 8 nb + 2t (+1)
     const int nk16 = (nk + 15) / 16;
-    float *part = n_splits == 1 ? nullptr : s.att_part + ((((size_t)b * G + g) * s.max_splits + split) * grp) * (D + 2);
+    float *part = n_splits == 1 ? nullptr : s.att_part + ((((size_t)b * G + g) * s.max_splits + split) * grp) * PS;
     for (int nb = warp; nb < D / 8; nb += nwarp) {
         float c[4] = {0.f, 0.f, 0.f, 0.f};
         for (int k16 = 0; k16 < nk16; ++k16) {
@@ -191,8 +233,7 @@ __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float
                 const float inv = 1.f / sm.l[gq];
                 *reinterpret_cast<float2 *>(&s.attn[((size_t)b * H + g * grp + gq) * D + dd]) = make_float2(o0 * inv, o1 * inv);
             } else {
-                part[gq * (D + 2) + dd] = o0;
-                part[gq * (D + 2) + dd + 1] = o1;
+                *reinterpret_cast<float2 *>(&part[gq * PS + dd]) = make_float2(o0, o1);
             }
         }
     }
@@ -200,9 +241,10 @@ __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float
         sync_threads(nt);
         return true;
     }
-    if (tid < grp) {
-        part[tid * (D + 2) + D] = sm.m[tid];
-        part[tid * (D + 2) + D + 1] = sm.l[tid];
+    if (tid < grp) *reinterpret_cast<float2 *>(&part[tid * PS + D]) = make_float2(sm.m[tid], sm.l[tid]);
+    if (defer_merge && n_splits <= ATT_MERGE_MAX) {   // the reader merges (its phase starts after a grid barrier)
+        sync_threads(nt);
+        return true;
     }
     __threadfence();
     sync_threads(nt);
@@ -210,14 +252,14 @@ __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float
     sync_threads(nt);
     if (sm.last) {
         __threadfence();
-        const float *p0 = s.att_part + (((size_t)b * G + g) * s.max_splits) * grp * (D + 2);
+        const float *p0 = s.att_part + (((size_t)b * G + g) * s.max_splits) * grp * PS;
         for (int idx = tid; idx < grp * D; idx += nt) {
             const int hr = idx / D, dd = idx - hr * D;
             float M = -INFINITY;
-            for (int sp2 = 0; sp2 < n_splits; ++sp2) M = fmaxf(M, __ldcg(&p0[((size_t)sp2 * grp + hr) * (D + 2) + D]));
+            for (int sp2 = 0; sp2 < n_splits; ++sp2) M = fmaxf(M, __ldcg(&p0[((size_t)sp2 * grp + hr) * PS + D]));
             float L = 0.f, O = 0.f;
             for (int sp2 = 0; sp2 < n_splits; ++sp2) {
-                const float *pp = p0 + ((size_t)sp2 * grp + hr) * (D + 2);
+                const float *pp = p0 + ((size_t)sp2 * grp + hr) * PS;
                 const float w = expf(__ldcg(&pp[D]) - M);
                 L = fmaf(__ldcg(&pp[D + 1]), w, L);
                 O = fmaf(__ldcg(&pp[dd]), w, O);

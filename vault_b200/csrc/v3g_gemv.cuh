@@ -199,16 +199,24 @@ __device__ __forceinline__ void load8(const float *p, bool vec, int n, float (&v
     }
 }
 
+// default activation loader of gemv_prologue: 8 values of row b at quarter block u, read from a.x
+struct XPlain {
+    __device__ __forceinline__ void operator()(const GemvArgs &a, int b, int u, bool vec, int n, float (&v)[8]) const {
+        load8<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + u * 8, vec, n, v);
+    }
+};
+
 // Convert the pass's activation rows once per CTA into shared memory: RMSNorm (optional), fp16 with a per-row
 // power-of-two scale (largest |x| scaled into (2^13, 2^14]); s_scale[b] receives the scale to undo and, with
 // BSUM, bsum[blk * 8 + b] the fp32 sum of converted 32-wide block blk of row b.  Work items are quarter blocks
 // (8 values; the four quarters of a block sit in adjacent lanes), so a 1536-wide row keeps 192 threads busy: one
 // stats pass and one convert pass.  A thread keeps its first items in registers between the passes -- CACHE of
 // them without RMSNorm, one item and its norm weights (in the last cache slot) with it -- so such rows cost one
-// round trip to L2.  nw_s: optional shared-memory copy of the norm weights (a.norm_w).
-template <bool BSUM, int CACHE = 0>
+// round trip to L2.  nw_s: optional shared-memory copy of the norm weights (a.norm_w); xl: the loader of the
+// activation values (XPlain reads a.x).
+template <bool BSUM, int CACHE = 0, class XL = XPlain>
 __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_scale, float *s_red, float *bsum,
-                                     int nt, const float *nw_s = nullptr) {
+                                     int nt, const float *nw_s = nullptr, const XL &xl = XL()) {
     const int tid = threadIdx.x, nw = nt / 32;
     const bool norm = a.prologue == PRO_RMSNORM;
     const bool vec = (a.K & 31) == 0 && (a.x_ld & 3) == 0;
@@ -247,7 +255,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         const int it = tid + k * nt;
         if (k < ncache && it < items) {
             const int b = it / nq, u = it - b * nq, n = a.K - u * 8;
-            load8<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + u * 8, vec, n, vc[k]);
+            xl(a, b, u, vec, n, vc[k]);
             if (k == 0 && norm) load8<false>(nwp + u * 8, vec, n, wc);
         }
     }
@@ -259,7 +267,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
     for (int it = tid + ncache * nt; it < items; it += nt) {
         const int b = it / nq, u = it - b * nq, n = a.K - u * 8;
         float v[8], w[8];
-        load8<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + u * 8, vec, n, v);
+        xl(a, b, u, vec, n, v);
         if (norm) load8<false>(nwp + u * 8, vec, n, w);
         stats(b, v, w);
     }
@@ -360,7 +368,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
         const int b = act ? it / nq : 0, u = act ? it - b * nq : 0, n = a.K - u * 8;
         float v[8], w[8];
         if (act) {
-            load8<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + u * 8, vec, n, v);
+            xl(a, b, u, vec, n, v);
             if (norm) load8<false>(nwp + u * 8, vec, n, w);
         }
         convert(act, b, u, n, v, w);

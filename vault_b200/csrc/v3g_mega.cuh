@@ -58,6 +58,7 @@ struct alignas(16) MkPhase {
     const float *next_norm;
     int next_k;
     int norm_staged;      // the previous phase staged this phase's norm weights
+    int attn_in;          // the input is the attention output: merge split partials while loading (MkXLoad)
 };
 
 // chunk-stream view of one phase; the whole table lives in shared memory for the kernel's lifetime
@@ -98,6 +99,20 @@ struct alignas(16) MkMisc {
     // biases of the CTA's QKV row tiles, refreshed at each QKV phase (16 per row tile, tile-row order)
     float qkv_bias[MK_OWN_TILES][16];
     int bias_r0, bias_n;
+};
+
+// activation loader of the persistent kernel's prologues: for the phase after attention, a sequence whose keys
+// fell into 2 .. ATT_MERGE_MAX splits has only partials, merged here; everything else reads a.x
+template <int D>
+struct MkXLoad {
+    const StateDev *s;
+    const KeySpan *ks;
+    int attn_in;
+    __device__ __forceinline__ void operator()(const GemvArgs &a, int b, int u, bool vec, int n, float (&v)[8]) const {
+        const int ns = (ks[b].total + ATT_KPC - 1) / ATT_KPC;
+        if (attn_in && ns >= 2 && ns <= ATT_MERGE_MAX) attn_merged8<D>(*s, b, u * 8, ns, v);
+        else load8<true>(a.x + (size_t)(a.b0 + b) * a.x_ld + u * 8, vec, n, v);
+    }
 };
 
 // residual epilogue of the persistent kernel: x[b, row] += y, from the CTA's shared copy when it owns the row tile
@@ -771,7 +786,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
             for (int i = c; i < n_items; i += G) {
                 const int split = i % ms, g = (i / ms) % n_kv, b = i / (ms * n_kv);
                 attn_item<D>(st, misc.ks[b], P.layer, scale, split, g, b, pos, *reinterpret_cast<AttnSmem<D> *>(smem),
-                             MK_CT);
+                             MK_CT, true);
             }
         } else {
             uint16_t *xs = reinterpret_cast<uint16_t *>(bsum + (BSUM ? P.a.nblk * GEMV_MB : 0));
@@ -793,7 +808,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
             float *nw_s = reinterpret_cast<float *>(smem + cfg.nw_off);
             // a CTA without row tiles in this phase converts nothing (CTA 0 still captures scorer features)
             if (lite[p].own[1] > lite[p].own[0] || (P.a.feat && c == 0))
-                gemv_prologue<BSUM, 5>(P.a, xs, s_scale, s_red, bsum, MK_CT, P.norm_staged ? nw_s : nullptr);
+                gemv_prologue<BSUM, 5>(P.a, xs, s_scale, s_red, bsum, MK_CT, P.norm_staged ? nw_s : nullptr,
+                                       MkXLoad<D>{&misc.sd, misc.ks, P.attn_in});
             if (P.next_norm) {   // stage the next phase's norm weights while this one streams (landed by the barrier)
                 for (int i = threadIdx.x; i < P.next_k / 4; i += MK_CT) cp_async16(nw_s + 4 * i, P.next_norm + 4 * i);
                 asm volatile("cp.async.commit_group;" ::: "memory");

@@ -850,7 +850,8 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
         at.layer = l;
         ph.push_back(at);
         const MatW *o[1] = {&L.o};
-        add_gemv(o, 1, sd.attn, md.H * md.D, md.H * md.D, PRO_PLAIN, nullptr, MK_EPI_RESID, l, sd.x, md.d, md.d);
+        add_gemv(o, 1, sd.attn, md.H * md.D, md.H * md.D, PRO_PLAIN, nullptr, MK_EPI_RESID, l, sd.x, md.d, md.d)
+            .attn_in = 1;
         const MatW *gu[1] = {&L.gu};
         add_gemv(gu, 1, sd.x, md.d, md.d, PRO_RMSNORM, L.ln2, MK_EPI_GATEUP, l, sd.hbuf, md.F, md.F);
         const MatW *dn[1] = {&L.down};
