@@ -57,6 +57,22 @@ def ensure_model(path: str, fmt: str, rank: int, barrier: bool = True) -> None:
         dist.barrier()
 
 
+def rank_max(values, device) -> list:
+    """Element-wise maximum of per-rank values over every rank: the slowest rank sets each reported time.  Works on
+    any process group (NCCL with CUDA tensors on the GPU box, gloo with CPU tensors in the tests)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    if dist.is_initialized():
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def aggregate_rate(world: int, units_per_rank: float, seconds: float) -> float:
+    """Whole-job rate: every one of `world` ranks processed `units_per_rank` units in at most `seconds`."""
+    return world * units_per_rank / seconds
+
+
 def prompt_ids(seed: int):
     import numpy as np
     return np.random.default_rng(seed).integers(0, 151643, size=PROMPT).astype("int64")
@@ -199,10 +215,7 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
     total_ms = start.elapsed_time(end)
     pf_ms = sum(e[0].elapsed_time(e[1]) for e in evs)
     dec_ms = sum(e[1].elapsed_time(e[2]) for e in evs)
-    times = torch.tensor([total_ms, pf_ms, dec_ms], dtype=torch.float64, device=ids.device)
-    if dist.is_initialized():
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    total_ms, pf_ms, dec_ms = times.tolist()
+    total_ms, pf_ms, dec_ms = rank_max([total_ms, pf_ms, dec_ms], ids.device)
     st.check()
 
     # e2e: the same request through the C ABI with host buffers (one v3g_step_host call per token)
@@ -227,10 +240,8 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
 
     e2e_request()
     e2e = [e2e_request() for _ in range(max(1, min(args.steps, 5)))]
-    e2e_dec = torch.tensor([sum(d for _, d in e2e)], dtype=torch.float64, device=ids.device)
-    if dist.is_initialized():
-        dist.all_reduce(e2e_dec, op=dist.ReduceOp.MAX)
-    e2e_value = world * DECODE * len(e2e) / float(e2e_dec.item())
+    e2e_dec = rank_max([sum(d for _, d in e2e)], ids.device)[0]
+    e2e_value = aggregate_rate(world, DECODE * len(e2e), e2e_dec)
 
     # dominant kernel: the persistent decode kernel (all 28 layers + lm head of one token), timed alone on the
     # engine stream at the mean decode position of the request (prompt + 32)
@@ -261,7 +272,7 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
     hbm = peaks.get("hbm_gbs", 6650.0)
     peak_kind = "measured" if "hbm_gbs" in peaks else "fallback"
     n_tok = DECODE * args.steps
-    value = world * n_tok / (dec_ms / 1e3)
+    value = aggregate_rate(world, n_tok, dec_ms / 1e3)
     step_s = dec_ms / 1e3 / n_tok
     # KV bytes read per decode step (fp16 K and V of every visible key, 2 KV heads x 128, all layers): mean
     # context 128 + 32 keys
@@ -278,7 +289,7 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
         "config": {"workload": "BASELINE config 1: VAULT v3 1.54B Q8_0, B=1, 128-token prompt + 64 greedy decode steps",
                    "global_batch": world, "seq_len": PROMPT + DECODE, "parallelism": f"sequence replicas x{world}",
                    "l2": "weights (1.64 GB) larger than L2 (126 MB); no flush needed"},
-        "prefill_tok_s": round(world * PROMPT * args.steps / (pf_ms / 1e3), 2),
+        "prefill_tok_s": round(aggregate_rate(world, PROMPT * args.steps, pf_ms / 1e3), 2),
         "ms_per_token": round(1e3 * step_s, 4),
         "gpu_launches": None,
         "roofline": {"kernel": "k_decode (persistent: 28 layers + lm head of one token, timed alone)", "bound": "hbm",

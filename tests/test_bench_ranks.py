@@ -1,0 +1,52 @@
+"""bench.py's multi-GPU host logic on two CPU ranks (gloo): the path shards by sequence, so ranks share nothing
+but the timing rule -- every rank times its own requests, the slowest rank's time is reported, and the whole-job
+rate counts every rank's tokens.  The GPU work of each rank is the single-GPU path covered by the gpu tests."""
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(HERE))
+
+import bench  # noqa: E402
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_two_gloo_ranks_report_the_slowest_time_and_serve_their_own_requests(tmp_path):
+    port = str(_free_port())
+    outs = [str(tmp_path / f"rank{r}.json") for r in range(2)]
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "ranks_worker.py"), str(r), "2", port, outs[r]])
+             for r in range(2)]
+    try:
+        for p in procs:
+            assert p.wait(timeout=180) == 0
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+    res = [json.load(open(o)) for o in outs]
+    expected = [110.0, 40.0, 60.5]   # element-wise max of the two ranks' (total, prefill, decode) times
+    for r in res:
+        assert r["got"] == expected
+    assert res[0]["ids"] != res[1]["ids"]   # each rank streams its own prompt
+    for r in range(2):
+        assert res[r]["ids"] == bench.prompt_ids(1000 + r)[:16].tolist()
+    assert res[1]["reference_arm"] == "returned"   # the reference arm runs on rank 0 alone
+
+
+def test_whole_job_rate_counts_every_rank():
+    assert bench.aggregate_rate(1, 640, 0.5) == pytest.approx(1280.0)
+    assert bench.aggregate_rate(8, 640, 0.5) == pytest.approx(8 * 1280.0)
+
+
+def test_rank_max_without_a_process_group_is_the_identity():
+    assert bench.rank_max([3.0, 1.5], "cpu") == [3.0, 1.5]
