@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
     }
     griddep_wait();
     griddep_launch();
-    gemv_prologue<BSUM>(a, xs, s_scale, s_red, bsum, blockDim.x);
+    gemv_prologue<BSUM, 5>(a, xs, s_scale, s_red, bsum, blockDim.x);
 
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     if (active) {
