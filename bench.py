@@ -32,7 +32,7 @@ REF_HOST = os.path.join(HERE, "oracle", "_ref", "vault3_host")
 METRIC = "decode tok/s (B=1, Q8_0, 128-token prompt, 64 greedy steps)"
 # DRAM bytes (read + write) of one k_decode launch on config 1, from the ncu capture summarised in
 # profiles/k_decode_q8_0_config1.md
-TRAFFIC = 1648604928
+TRAFFIC = 1650602240
 
 
 def model_path(fmt: str = "q8_0") -> str:
