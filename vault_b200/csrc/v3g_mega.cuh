@@ -99,6 +99,9 @@ struct alignas(16) MkMisc {
     // biases of the CTA's QKV row tiles, refreshed at each QKV phase (16 per row tile, tile-row order)
     float qkv_bias[MK_OWN_TILES][16];
     int bias_r0, bias_n;
+    // 1 from the CTA's arrival at a grid barrier until the next phase's activation prologue is done: the producer
+    // issues no copies meanwhile, so the ring's refill does not queue in front of the prologue's loads
+    volatile int quiet;
 };
 
 // activation loader of the persistent kernel's prologues: for the phase after attention, a sequence whose keys
@@ -630,6 +633,8 @@ __device__ __forceinline__ void mk_produce(const MkLite *lite, int n_phases, int
                                            uint8_t *smem, const StateDev *sp) {
     const int lane = threadIdx.x & 31;
     if (lane >= MK_WARPS) return;
+    const volatile int *quiet = &reinterpret_cast<MkMisc *>(smem + cfg.misc_off)->quiet;
+    uint32_t hush = 0;
     const int S = cfg.slots;
     const uint32_t buf = smem_u32(smem + cfg.ring_off + (size_t)lane * S * MK_SLOT_BYTES);
     const uint32_t full = smem_u32(smem + cfg.bar_off) + (uint32_t)(lane * S * 8);
@@ -648,6 +653,12 @@ __device__ __forceinline__ void mk_produce(const MkLite *lite, int n_phases, int
             continue;
         }
         idle = 0;
+        if (*quiet && hush < MK_WAIT_LIMIT) {   // hold the copy while the consumers load activations (bounded)
+            ++hush;
+            __nanosleep(64);
+            continue;
+        }
+        hush = 0;
         const int n = mk_chunk_n(cur);
         const int tb = tile_bytes(cur.fmt);
         bulk_load(buf + slot * MK_SLOT_BYTES, cur.tiles + (size_t)cur.tl * tb, (uint32_t)(n * tb), full + slot * 8, pol);
@@ -722,6 +733,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
     __syncthreads();
     for (int p = threadIdx.x; p < n_phases; p += blockDim.x)   // this CTA's tile range of every GEMV phase
         if (lite[p].kind == MK_GEMV) mk_own_range(lite[p], c, G);
+    if (threadIdx.x == 0) reinterpret_cast<MkMisc *>(smem + cfg.misc_off)->quiet = 0;
     __syncthreads();
     if (warp == MK_WARPS) {   // weights are immutable: the producer streams from the very start
         mk_produce(lite, n_phases, c, G, cfg, smem, sp);
@@ -810,6 +822,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
             if (lite[p].own[1] > lite[p].own[0] || (P.a.feat && c == 0))
                 gemv_prologue<BSUM, 5>(P.a, xs, s_scale, s_red, bsum, MK_CT, P.norm_staged ? nw_s : nullptr,
                                        MkXLoad<D>{&misc.sd, misc.ks, P.attn_in});
+            if (threadIdx.x == 0) misc.quiet = 0;   // activations are in place: the ring may refill
             if (P.next_norm) {   // stage the next phase's norm weights while this one streams (landed by the barrier)
                 for (int i = threadIdx.x; i < P.next_k / 4; i += MK_CT) cp_async16(nw_s + 4 * i, P.next_norm + 4 * i);
                 asm volatile("cp.async.commit_group;" ::: "memory");
@@ -821,6 +834,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
         }
         if (p + 1 < n_phases) {
             asm volatile("cp.async.wait_all;" ::: "memory");   // descriptor p + 1 is in place after the barrier
+            if (threadIdx.x == 0 && lite[p + 1].kind == MK_GEMV) misc.quiet = 1;
             mk_grid_sync(gbar, (unsigned int)(p + 1) * (unsigned int)G, status, lite, n_phases, warp, R.cons);
             mk_fetch_phase(phases, p + 2, n_phases, ph_s + (p & 1));   // slot of phase p, now unused
         }
