@@ -2,6 +2,7 @@
 
 One bench "step" is one config-1 request: reset the fixed state, stream the 128-token random prompt, then decode
 64 tokens greedily (batch 1, Q8_0 weights of the 1.54B architecture, random-init N(0, 0.02), W = 1024, no sinks).
+`--config 2` runs BASELINE config 2 instead: Hybrid Q4_0 weights, a 2,560-token prompt and 256 decode steps.
 The headline value is decode tokens/s (summed over ranks for --gpus N: every rank serves its own requests; the
 path shards by sequence, so there is no collective on the data path -> "scaling": "weak").
 
@@ -27,12 +28,32 @@ import time
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
-PROMPT, DECODE = 128, 64
 REF_HOST = os.path.join(HERE, "oracle", "_ref", "vault3_host")
-METRIC = "decode tok/s (B=1, Q8_0, 128-token prompt, 64 greedy steps)"
-# DRAM bytes (read + write) of one k_decode launch on config 1, from the ncu capture summarised in
-# profiles/k_decode_q8_0_config1.md
-TRAFFIC = 1650602240
+# BASELINE configs this bench runs (--config; 1 is the headline).  traffic: DRAM bytes (read + write) of one k_decode
+# launch from the ncu capture summarised in `profile` (None: not captured for that config).
+CONFIGS = {
+    1: dict(fmt="q8_0", prompt=128, decode=64,
+            metric="decode tok/s (B=1, Q8_0, 128-token prompt, 64 greedy steps)",
+            workload="BASELINE config 1: VAULT v3 1.54B Q8_0, B=1, 128-token prompt + 64 greedy decode steps",
+            traffic=1650602240, profile="profiles/k_decode_q8_0_config1.md"),
+    2: dict(fmt="q4_0", prompt=2560, decode=256,
+            metric="decode tok/s (B=1, Hybrid Q4_0, 2,560-token prompt, 256 greedy steps)",
+            workload="BASELINE config 2: VAULT v3 1.54B Hybrid Q4_0, B=1, 2,560-token prompt + 256 greedy decode steps "
+                     "(the W=1024 window rolls over twice)",
+            traffic=None, profile=None),
+}
+CONFIG = 1
+FMT = CONFIGS[1]["fmt"]
+PROMPT, DECODE = CONFIGS[1]["prompt"], CONFIGS[1]["decode"]
+METRIC = CONFIGS[1]["metric"]
+TRAFFIC = CONFIGS[1]["traffic"]
+
+
+def select_config(n: int) -> None:
+    """Point the module-level workload constants at BASELINE config n."""
+    global CONFIG, FMT, PROMPT, DECODE, METRIC, TRAFFIC
+    c = CONFIGS[n]
+    CONFIG, FMT, PROMPT, DECODE, METRIC, TRAFFIC = n, c["fmt"], c["prompt"], c["decode"], c["metric"], c["traffic"]
 
 
 def model_path(fmt: str = "q8_0") -> str:
@@ -136,8 +157,8 @@ def run_reference_host(path: str, threads: int, timeout: int = 600):
 def reference_arm(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    path = model_path()
-    ensure_model(path, "q8_0", 0, barrier=False)
+    path = model_path(FMT)
+    ensure_model(path, FMT, 0, barrier=False)
     threads = os.cpu_count() or 1
     if not os.path.exists(REF_HOST):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/vault3_host not built (needs the reference "
@@ -153,13 +174,14 @@ def reference_arm(args, rank: int, world: int) -> None:
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * wall / args.steps, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 weights, fp32 compute",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": f"{FMT} weights, fp32 compute",
         "data": "synthetic (random-init N(0,0.02) weights, seeded uniform prompt ids; vault3_host --bench ids)",
-        "config": {"workload": "BASELINE config 1: VAULT v3 1.54B Q8_0, B=1, 128-token prompt + 64 decode steps",
-                   "global_batch": 1, "seq_len": PROMPT + DECODE, "parallelism": "cpu threads"},
+        "config": {"workload": CONFIGS[CONFIG]["workload"], "global_batch": 1, "seq_len": PROMPT + DECODE,
+                   "parallelism": "cpu threads"},
         "prefill_tok_s": round(sum(r["prefill_tokens"] for r in runs) / sum(r["prefill_s"] for r in runs), 3),
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": runs[0]["threads"], "kind": "reference",
-                         "sample": f"{args.steps} x (128-token token-by-token prefill + 64 decode), vault3_host --bench"},
+                         "sample": f"{args.steps} x ({PROMPT}-token token-by-token prefill + {DECODE} decode), "
+                                   "vault3_host --bench"},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 
@@ -172,8 +194,8 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
     from vault_b200.model import VAULTv3ForCausalLM
 
     torch.cuda.set_device(local_rank)
-    path = model_path()
-    ensure_model(path, "q8_0", rank)
+    path = model_path(FMT)
+    ensure_model(path, FMT, rank)
     m = VAULTv3ForCausalLM(path, device=local_rank, verify_crc=False)
     L = _lib.lib()
     stream = torch.cuda.current_stream()
@@ -250,6 +272,11 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
                "prefill")
     _lib.check(L.v3g_generate(st._h, C.c_void_p(nxt.data_ptr()), DECODE // 2, C.c_void_p(out.data_ptr()), DECODE, sp),
                "generate")
+    # visible keys at this position (the KV rows one decode step reads): sinks and bank from 2W on, then the
+    # previous and the current window chunk
+    si = st.info()
+    W, pos = m.cfg.window, PROMPT + DECODE // 2
+    keys = ((si.n_pin + si.mem_cnt) if pos >= 2 * W else 0) + (W if pos >= W else 0) + pos % W + 1
     persistent = L.v3g_decode_pass(st._h, 1, sp) == 0
     kernel_s = None
     if persistent:
@@ -274,9 +301,9 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
     n_tok = DECODE * args.steps
     value = aggregate_rate(world, n_tok, dec_ms / 1e3)
     step_s = dec_ms / 1e3 / n_tok
-    # KV bytes read per decode step (fp16 K and V of every visible key, 2 KV heads x 128, all layers): mean
-    # context 128 + 32 keys
-    kv_bytes = 28 * 2 * 2 * 128 * 2 * (PROMPT + DECODE // 2)
+    # KV bytes read per decode step (fp16 K and V of every visible key, 2 KV heads x 128, all layers) at the
+    # request's mid-decode position
+    kv_bytes = 28 * 2 * 2 * 128 * 2 * keys
     step_bytes = m.info.step_weight_bytes + kv_bytes
     kernel_bytes = step_bytes   # one launch of the persistent kernel reads every weight once plus the KV rows
     achieved = kernel_bytes / kernel_s / 1e9 if kernel_s else None
@@ -284,10 +311,9 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
-        "dtype": "q8_0 weights; fp16 tensor-core operands, fp32 accumulate; fp16 KV cache",
+        "dtype": f"{FMT} weights; fp16 tensor-core operands, fp32 accumulate; fp16 KV cache",
         "data": "synthetic (random-init N(0,0.02) weights, seeded uniform prompt ids)",
-        "config": {"workload": "BASELINE config 1: VAULT v3 1.54B Q8_0, B=1, 128-token prompt + 64 greedy decode steps",
-                   "global_batch": world, "seq_len": PROMPT + DECODE, "parallelism": f"sequence replicas x{world}",
+        "config": {"workload": CONFIGS[CONFIG]["workload"], "global_batch": world, "seq_len": PROMPT + DECODE, "parallelism": f"sequence replicas x{world}",
                    "l2": "weights (1.64 GB) larger than L2 (126 MB); no flush needed"},
         "prefill_tok_s": round(aggregate_rate(world, PROMPT * args.steps, pf_ms / 1e3), 2),
         "ms_per_token": round(1e3 * step_s, 4),
@@ -296,8 +322,8 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
                      "achieved": round(achieved, 1) if achieved else None, "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4) if achieved else None,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)", "traffic": TRAFFIC,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_decode launch "
-                                       "(profiles/k_decode_q8_0_config1.md)",
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_decode launch "
+                                        f"({CONFIGS[CONFIG]['profile']})") if TRAFFIC else "not captured for this config",
                      "algorithmic_bytes_per_launch": int(kernel_bytes),
                      "avg_launch_us": round(kernel_s * 1e6, 2) if kernel_s else None},
         "step_roofline": {"bytes_per_step": int(step_bytes), "achieved": round(step_bytes / step_s / 1e9, 1),
@@ -318,7 +344,8 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
             r = run_reference_host(path, os.cpu_count() or 1)
             line["cpu_baseline"] = {"value": r["decode_tok_s"], "unit": "tok/s", "cores": r["threads"],
                                     "kind": "reference",
-                                    "sample": "1 x (128-token prefill + 64 decode) with runtime/vault3_host --bench"}
+                                    "sample": f"1 x ({PROMPT}-token prefill + {DECODE} decode) with runtime/vault3_host "
+                                              "--bench"}
         except Exception as e:  # noqa: BLE001
             line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "reference",
                                     "sample": f"failed: {e}"[:200]}
@@ -332,7 +359,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
     args = ap.parse_args()
+    select_config(args.config)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
