@@ -377,7 +377,7 @@ __device__ __forceinline__ void mk_chunk_fast(const uint8_t *sb, int kt, const u
     const int g = lane >> 2;
     uint4 q[N];
     uint2 sc[N];
-    uint32_t b0[N][2], b1[N][2];   // Q4 reads two records per tile below; Q8 / 16-bit tiles fill these
+    uint32_t b0[N][4], b1[N][4];   // B fragments of each tile's k16 steps (Q4: 4, Q8: 2, 16-bit: 1)
 #pragma unroll
     for (int i = 0; i < N; ++i) {
         q[i] = *reinterpret_cast<const uint4 *>(sb + i * TB + lane * 16);
@@ -390,6 +390,14 @@ __device__ __forceinline__ void mk_chunk_fast(const uint8_t *sb, int kt, const u
             b1[i][1] = xv.w;
         } else if constexpr (FMT == FMT_Q4) {
             sc[i] = *reinterpret_cast<const uint2 *>(sb + i * TB + 512 + g * 8);
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                const uint4 xv = xq[(2 * (kt + i) + blk) * xbs];
+                b0[i][2 * blk] = xv.x;
+                b1[i][2 * blk] = xv.y;
+                b0[i][2 * blk + 1] = xv.z;
+                b1[i][2 * blk + 1] = xv.w;
+            }
         } else {
             const uint2 xv = reinterpret_cast<const uint2 *>(xq + ((kt + i) >> 1) * xbs)[(kt + i) & 1];
             b0[i][0] = xv.x;
@@ -423,12 +431,11 @@ __device__ __forceinline__ void mk_chunk_fast(const uint8_t *sb, int kt, const u
             const uint32_t w[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
 #pragma unroll
             for (int blk = 0; blk < 2; ++blk) {
-                const uint4 xv = xq[(2 * (kt + i) + blk) * xbs];
                 d[i][blk][0] = d[i][blk][1] = d[i][blk][2] = d[i][blk][3] = 0.f;
                 mma16816(d[i][blk], q4_pair<0>(w[2 * blk]), q4_pair<4>(w[2 * blk]), q4_pair<8>(w[2 * blk]),
-                         q4_pair<12>(w[2 * blk]), xv.x, xv.y);
+                         q4_pair<12>(w[2 * blk]), b0[i][2 * blk], b1[i][2 * blk]);
                 mma16816(d[i][blk], q4_pair<0>(w[2 * blk + 1]), q4_pair<4>(w[2 * blk + 1]), q4_pair<8>(w[2 * blk + 1]),
-                         q4_pair<12>(w[2 * blk + 1]), xv.z, xv.w);
+                         q4_pair<12>(w[2 * blk + 1]), b0[i][2 * blk + 1], b1[i][2 * blk + 1]);
             }
         }
 #pragma unroll
