@@ -57,25 +57,17 @@ def select_config(n: int) -> None:
 
 
 def model_path(fmt: str = "q8_0") -> str:
-    d = os.environ.get("VAULT_B200_BENCH_DIR", "/tmp/vault_b200_bench")
-    os.makedirs(d, exist_ok=True)
-    return os.path.join(d, f"vault_v3_1p5b_{fmt}_seed0.vlt3")
-
-
-def ensure_model(path: str, fmt: str, rank: int, barrier: bool = True) -> None:
-    import torch
-    import torch.distributed as dist
     from vault_b200 import synth
-    done = path + ".done"
-    if rank == 0 and not os.path.exists(done):
-        cfg = synth.full_config(n_sink=0)
-        t0 = time.time()
-        synth.write_synthetic_vlt3_fast(path, cfg, fmt, seed=0, device="cuda" if torch.cuda.is_available() else "cpu")
-        open(done, "w").close()
-        print(f"[bench] wrote {path} ({os.path.getsize(path) / 1e9:.2f} GB) in {time.time() - t0:.1f}s",
-              file=sys.stderr)
+    return synth.full_model_file(fmt, seed=0, n_sink=0)
+
+
+def ensure_model(fmt: str, rank: int, barrier: bool = True) -> str:
+    """Rank 0 writes the cached synthetic model file (once per box); the other ranks wait at the barrier."""
+    import torch.distributed as dist
+    path = model_path(fmt) if rank == 0 else None
     if barrier and dist.is_initialized():
         dist.barrier()
+    return path or model_path(fmt)
 
 
 def rank_max(values, device) -> list:
@@ -157,8 +149,7 @@ def run_reference_host(path: str, threads: int, timeout: int = 600):
 def reference_arm(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    path = model_path(FMT)
-    ensure_model(path, FMT, 0, barrier=False)
+    path = ensure_model(FMT, 0, barrier=False)
     threads = os.cpu_count() or 1
     if not os.path.exists(REF_HOST):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/vault3_host not built (needs the reference "
@@ -194,8 +185,7 @@ def engine_arm(args, rank: int, world: int, local_rank: int) -> None:
     from vault_b200.model import VAULTv3ForCausalLM
 
     torch.cuda.set_device(local_rank)
-    path = model_path(FMT)
-    ensure_model(path, FMT, rank)
+    path = ensure_model(FMT, rank)
     m = VAULTv3ForCausalLM(path, device=local_rank, verify_crc=False)
     L = _lib.lib()
     stream = torch.cuda.current_stream()

@@ -87,6 +87,10 @@ typedef struct {
  * max_sink: cap of the ChatML auto-pinned prefix (the Python reference's VAULTv3Config.max_sink, default 512;
  * 0 selects 512).  The loader allocates the model's device memory itself (freed by v3g_free). */
 V3G_API int v3g_load(v3g_model **out, const uint8_t *buf, uint64_t size, int verify_crc, int device, uint32_t max_sink);
+/* Validate a VLT3 buffer on the host only (no device call): the checks and status codes v3g_load applies before it
+ * uploads anything.  The Python reader (vault_b200.vlt3.read_vlt3, the counterpart of tools/vlt3.py:453-545
+ * read_vlt3) validates through it, so both loaders accept and reject the same files. */
+V3G_API int v3g_validate(const uint8_t *buf, uint64_t size, int verify_crc);
 V3G_API int v3g_model_get_info(const v3g_model *m, v3g_model_info *out);
 V3G_API void v3g_free(v3g_model *m);
 
@@ -140,7 +144,7 @@ V3G_API int v3g_gemv(const v3g_model *m, uint32_t tensor_id, const float *dev_x,
 V3G_API int v3g_decode_pass(v3g_state *s, int want_lm, void *stream);
 
 /* Greedy (first-maximum) token of each of `rows` logit rows (row b at dev_logits + b * ld, `vocab` entries, NaN
- * never selected), written to dev_tokens[rows] -- the selection v3g_step makes, for callers that hold logits but
+ * never selected, -0.0 equal to +0.0, token 0 for a row that is all NaN), written to dev_tokens[rows] -- the selection v3g_step makes, for callers that hold logits but
  * may not allocate device memory (their framework's allocator owns the device memory, or cudaMalloc's implicit
  * device synchronisation is not acceptable in their token loop).  It has no counterpart in the reference.
  * Allocates nothing: its scratch is a fixed device array of V3G_NOALLOC_MAX_ROWS 8-byte keys that every GPU loading

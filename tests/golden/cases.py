@@ -48,6 +48,9 @@ CASES["chat_spoof_q8_0"] = dict(cfg=_CHAT, fmt="q8_0", seed=18, L=140, stream="s
 CASES["b2_swa_q8_0"] = dict(cfg=_B2, fmt="q8_0", seed=0, L=53, B=2, stream="random", std=0.2, gain=(0.85, 1.15))
 for _fmt in ("q8_0", "q4_0", "bf16"):
     CASES[f"mini_gqa_{_fmt}"] = dict(cfg=_MINI, fmt=_fmt, seed=5, L=100, stream="chat", std=0.02)
+# eight layers: Hybrid Q4_0 keeps q/o of layers 0, 1, 6, 7 in Q8_0 (the n_layers >= 8 branch of tools/vlt3.py:312-330)
+CASES["deep_hybrid_q4_0"] = dict(cfg=dict(_TINY, n_layers=8, seg_layers=(2, 5)), fmt="q4_0", seed=11, L=80,
+                                 stream="random", std=0.08, gain=(0.9, 1.1), ln_bias_std=0.02)
 
 
 def case_config(spec: dict) -> VAULTv3Config:

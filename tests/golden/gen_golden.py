@@ -11,7 +11,7 @@ For each case it
   3. stores the ids and fp32 logits in <case>.npz.
 It also stores Q8_0/Q4_0 block-codec vectors produced by the reference quantizers/dequantizers.
 
-Usage:  python tests/golden/gen_golden.py [--ref /path/to/reference]
+Usage:  python tests/golden/gen_golden.py --ref <reference checkout>   (or VAULT_REFERENCE=<dir>)
 """
 
 from __future__ import annotations
@@ -36,8 +36,12 @@ from vault_b200 import vlt3 as my_vlt3  # noqa: E402
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", nargs="*", default=None, help="regenerate these cases only (others keep their files)")
+    ap.add_argument("--ref", default=os.environ.get("VAULT_REFERENCE"),
+                    help="root of the reference checkout (default: $VAULT_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("pass --ref or set VAULT_REFERENCE")
     sys.path.insert(0, args.ref)
     sys.path.insert(0, os.path.join(args.ref, "tools"))
     import torch
@@ -45,9 +49,15 @@ def main() -> None:
     import vlt3 as ref_vlt3  # noqa: E402
 
     torch.set_num_threads(8)
+    man_path = os.path.join(HERE, "manifest.json")
     manifest = {}
+    if args.only and os.path.exists(man_path):
+        with open(man_path) as f:
+            manifest = json.load(f)
     with tempfile.TemporaryDirectory() as td:
         for name, spec in CASES.items():
+            if args.only and name not in args.only:
+                continue
             cfg = case_config(spec)
             tokdir = os.path.join(td, f"tok_{cfg.vocab_size}")
             synth.make_tokenizer_dir(tokdir, cfg.vocab_size, synth.SMALL_EXTRA_TOKENS)
@@ -103,6 +113,10 @@ def main() -> None:
                   f"mem={len(out['final_mem_pos'])} fwd-vs-step={fwd_err:.2e}")
 
     # block-codec vectors from the reference quantizers / dequantizers
+    if args.only:
+        with open(man_path, "w") as f:
+            json.dump(manifest, f, indent=1, sort_keys=True)
+        return
     rng = np.random.default_rng(1234)
     w = (rng.standard_normal(32 * 96).astype(np.float32) * 0.05)
     w[:32] = 0.0                                   # all-zero block (d = 0 path)

@@ -82,3 +82,17 @@ def test_block_codecs_bit_exact(golden_dir):
         orc = vo.dequant(g[key].tobytes(), dt, w.size)
         assert mine.view(np.uint32).tobytes() == ref.view(np.uint32).tobytes()
         assert orc.view(np.uint32).tobytes() == ref.view(np.uint32).tobytes()
+
+
+def test_hybrid_policy_keeps_boundary_layers_q8(case_files):
+    """Hybrid Q4_0 on an 8-layer model: q/o of layers 0, 1, L-2, L-1 and every k/v stay Q8_0, the rest Q4_0
+    (tools/vlt3.py:312-330); the file is byte-identical to the reference writer's (manifest sha256)."""
+    vf = vlt3.read_vlt3(case_files("deep_hybrid_q4_0"))
+    L = vf.header["n_layers"]
+    assert L == 8
+    for li in range(L):
+        for kind, want in (("q_proj", vlt3.Q8_0 if li in (0, 1, L - 2, L - 1) else vlt3.Q4_0),
+                           ("o_proj", vlt3.Q8_0 if li in (0, 1, L - 2, L - 1) else vlt3.Q4_0),
+                           ("k_proj", vlt3.Q8_0), ("v_proj", vlt3.Q8_0)):
+            assert vf.entry(f"layers.{li}.self_attn.{kind}.weight")["dtype"] == want, (li, kind)
+        assert vf.entry(f"layers.{li}.mlp.down_proj.weight")["dtype"] == vlt3.Q4_0

@@ -76,3 +76,22 @@ def test_argmax_noalloc_rejects_too_many_rows():
     rc = L.v3g_argmax_noalloc(C.c_void_p(logits.data_ptr()), rows, 8, 8, C.c_void_p(out.data_ptr()), _stream())
     assert rc == -10, rc   # V3G_E_LIMIT
     assert "V3G_NOALLOC_MAX_ROWS" in L.v3g_last_error().decode()
+
+
+def test_argmax_noalloc_selection_rules():
+    """The key rules on synthetic rows: NaN is never selected (an all-NaN row gives token 0), a NaN before the
+    maximum does not hide it, and -0.0 ties with +0.0 so the first of them wins (runtime/vault3.c:3198-3202)."""
+    from vault_b200 import _lib
+    L = _lib.lib()
+    torch.cuda.set_device(0)
+    nan = float("nan")
+    rows = torch.tensor([
+        [nan, nan, nan, nan, nan, nan],
+        [nan, 1.0, 3.0, nan, 2.0, 3.0],
+        [-1.0, -0.0, 0.0, -2.0, 0.0, -0.5],
+        [-3.0, -1.0, -1.0, -2.0, -4.0, -1.5],
+    ], dtype=torch.float32, device="cuda:0")
+    for _ in range(2):   # two calls in a row: the shared keys are cleared each time
+        got = _noalloc(L, rows)
+        torch.cuda.synchronize()
+        assert got.cpu().tolist() == [0, 2, 1, 1]

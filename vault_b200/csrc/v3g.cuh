@@ -206,9 +206,12 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// order-preserving float -> uint32 (larger float -> larger key); NaN-free inputs assumed
+// order-preserving float -> uint32 (larger float -> larger key); -0.0 maps to the key of +0.0, so the two compare
+// equal and the first-index tie rule of v3_argmax (runtime/vault3.c:3198-3202) holds for them too.  NaN-free
+// inputs assumed (callers skip NaN).
 __device__ __forceinline__ uint32_t float_key(float f) {
     uint32_t u = __float_as_uint(f);
+    if (u == 0x80000000u) u = 0u;
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 

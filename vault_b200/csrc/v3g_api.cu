@@ -262,6 +262,13 @@ int break_tier(const uint8_t *b, uint32_t n) {
 }  // namespace
 
 // ------------------------------------------------------------------------------------------ model load
+extern "C" int v3g_validate(const uint8_t *buf, uint64_t size, int verify_crc) {
+    Parsed *P = new Parsed();   // large (per-layer tensor table): keep it off the caller's stack
+    const int rc = parse_vlt3(buf, size, verify_crc, *P);
+    delete P;
+    return rc;
+}
+
 extern "C" int v3g_load(v3g_model **out, const uint8_t *buf, uint64_t size, int verify_crc, int device,
                         uint32_t max_sink) {
     if (!out) return fail(V3G_E_ARG, "null output pointer");

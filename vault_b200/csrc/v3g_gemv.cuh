@@ -46,6 +46,32 @@ struct GemvArgs {
 };
 
 __host__ __device__ constexpr bool fmt_int(int fmt) { return fmt == FMT_Q8 || fmt == FMT_Q4; }
+
+// Activation precision.  A batch of B <= 4 rows leaves tensor-core columns free, so every activation row enters as
+// two fp16 parts -- high part x_h = fp16(x), low part x_l = fp16(x - x_h), about 22 significant bits together --
+// in columns b (high) and P + b (low), P = 1, 2 or 4; the two columns are added after the tensor core.  Larger
+// batches keep one fp16 part per row (11 bits).  gemv_lo(B) = P (0: no low parts), gemv_xrows(B) = record rows.
+__host__ __device__ constexpr int gemv_lo(int B) { return B == 1 ? 1 : (B == 2 ? 2 : (B <= 4 ? 4 : 0)); }
+__host__ __device__ constexpr int gemv_xrows(int B) { return gemv_lo(B) ? 2 * gemv_lo(B) : B; }
+// record row read by the lanes of tensor-core column g: its own row when it holds data, else row 0 (the columns of
+// absent rows are computed and never read)
+__device__ __forceinline__ int gemv_rec_row(int B, int g) {
+    const int P = gemv_lo(B);
+    if (P) return (g < 2 * P && (g & (P - 1)) < B) ? g : 0;
+    return g < B ? g : 0;
+}
+// add the low-part columns into the high-part columns of a lane's accumulators (rows g, g+8 x columns 2t, 2t+1);
+// every lane of the warp must call it together
+__device__ __forceinline__ void gemv_fold_lo(int B, float (&acc)[4]) {
+    const int P = gemv_lo(B);
+    if (P == 1) {
+        acc[0] += acc[1];
+        acc[2] += acc[3];
+    } else if (P) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], P >> 1);
+    }
+}
 __host__ __device__ constexpr float fmt_offset(int fmt) { return fmt == FMT_Q8 ? 1152.f : 1032.f; }
 
 __device__ __forceinline__ float2 h2f2(uint32_t h) {
@@ -221,6 +247,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
     const bool norm = a.prologue == PRO_RMSNORM;
     const bool vec = (a.K & 31) == 0 && (a.x_ld & 3) == 0;
     const int nb = (a.K + 31) >> 5, nq = 4 * nb, items = a.B * nq;
+    const int xr = gemv_xrows(a.B), lo = gemv_lo(a.B);
     const float *nwp = nw_s ? nw_s : a.norm_w;
     const float inv_k = 1.0f / (float)a.K;
     float ss[GEMV_MB], mx[GEMV_MB];
@@ -317,7 +344,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
     }
     uint32_t *xw = reinterpret_cast<uint32_t *>(xs);
     auto convert = [&](bool act, int b, int u, int n, const float (&v)[8], const float (&w)[8]) {
-        float bs = 0.f;
+        float bs = 0.f, bsl = 0.f;
         if (act) {
             if (a.feat && blockIdx.x == 0) {
                 float *f = a.feat + (size_t)(a.b0 + b) * a.feat_ld + u * 8;
@@ -331,8 +358,9 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
                 cb = b;
             }
             const float mul = cmul;
-            // quarter u of block u / 4 holds the fp16 pairs t = 0..3 of word (u & 3) in the records (block, b, t)
-            uint32_t *dst = xw + ((size_t)(u >> 2) * a.B + b) * 16 + (u & 3);
+            // quarter u of block u / 4 holds the fp16 pairs t = 0..3 of word (u & 3) in the records (block, row, t);
+            // the low parts of row b go to record row lo + b
+            uint32_t *dst = xw + ((size_t)(u >> 2) * xr + b) * 16 + (u & 3);
             float bs2 = 0.f;
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
@@ -343,6 +371,12 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
                 if (t & 1) bs2 += back.x + back.y;
                 else bs += back.x + back.y;
                 dst[4 * t] = *reinterpret_cast<const uint32_t *>(&hv);
+                if (lo) {
+                    const __half2 lv = __floats2half2_rn(x0 - back.x, x1 - back.y);
+                    const float2 lb = __half22float2(lv);
+                    bsl += lb.x + lb.y;
+                    dst[lo * 16 + 4 * t] = *reinterpret_cast<const uint32_t *>(&lv);
+                }
             }
             bs += bs2;
         }
@@ -350,6 +384,11 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
             bs += __shfl_xor_sync(0xffffffffu, bs, 1);
             bs += __shfl_xor_sync(0xffffffffu, bs, 2);
             if (act && (u & 3) == 0) bsum[(u >> 2) * GEMV_MB + b] = bs;
+            if (lo) {
+                bsl += __shfl_xor_sync(0xffffffffu, bsl, 1);
+                bsl += __shfl_xor_sync(0xffffffffu, bsl, 2);
+                if (act && (u & 3) == 0) bsum[(u >> 2) * GEMV_MB + lo + b] = bsl;
+            }
         }
     };
     int base = 0;
@@ -375,7 +414,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
     }
     // zero the records and block sums of padding blocks (tiles may extend past K).  Absent batch rows (b >= B) have
     // no records: their lanes read row 0, whose tensor-core columns are computed and never read.
-    for (int idx = nb * a.B * 4 + tid; idx < a.nblk * a.B * 4; idx += nt)
+    for (int idx = nb * xr * 4 + tid; idx < a.nblk * xr * 4; idx += nt)
         reinterpret_cast<uint4 *>(xs)[idx] = make_uint4(0u, 0u, 0u, 0u);
     if (BSUM)
         for (int idx = nb * GEMV_MB + tid; idx < a.nblk * GEMV_MB; idx += nt) bsum[idx] = 0.f;
@@ -423,7 +462,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     if (active) {
         const int g = lane >> 2;
-        const XFrag xf{g < a.B ? reinterpret_cast<const uint4 *>(xs) + g * 4 + (lane & 3) : nullptr, 4 * a.B};
+        const XFrag xf{reinterpret_cast<const uint4 *>(xs) + gemv_rec_row(a.B, g) * 4 + (lane & 3), 4 * gemv_xrows(a.B)};
         if (si == 0) stream_tiles<FA>(pre, tp, k0, nkt, xf, bsum, lane, acc);
         else stream_tiles<FB>(pre, tp, k0, nkt, xf, bsum, lane, acc);
     }
@@ -442,6 +481,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
         }
     }
     if (active && kw == 0) {
+        gemv_fold_lo(a.B, acc);
         const int g = lane >> 2, t = lane & 3;
         const int sg = si + a.seg_base;
         const float ws = a.seg[si].wscale;
@@ -458,7 +498,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
 
 inline size_t gemv_smem_bytes(const GemvArgs &a, bool bsum) {
     return (136 + GEMV_MB + 8 * 32 * 4 + (bsum ? a.nblk * GEMV_MB : 0)) * sizeof(float) +
-           (size_t)a.B * a.nblk * 64;
+           (size_t)gemv_xrows(a.B) * a.nblk * 64;
 }
 
 // Host helper: choose the k split so the launch covers the GPU, fill the launch parameters.

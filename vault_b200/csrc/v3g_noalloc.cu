@@ -27,15 +27,17 @@ __global__ void k_noalloc_clear(unsigned long long *keys, int rows) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x) keys[i] = 0ull;
 }
 
-// row blockIdx.y, vocab slice blockIdx.x: the same selection rule as the step's argmax (NaN never wins)
+// row blockIdx.y, vocab slice blockIdx.x: the same selection rule as the step's argmax (NaN never wins; -0.0 and
+// +0.0 tie, the first index wins; a row without a non-NaN value keeps key 0 and yields token 0)
 __global__ void __launch_bounds__(256) k_noalloc_argmax(const float *logits, int vocab, size_t ld,
                                                         unsigned long long *keys) {
     const int b = blockIdx.y, tid = threadIdx.x;
     const float *lg = logits + (size_t)b * ld;
-    const int per = (vocab + gridDim.x - 1) / gridDim.x;
-    const int i0 = blockIdx.x * per, i1 = min(vocab, i0 + per);
+    // 64-bit slice bounds: vocab may be as large as 2^31 - 1, where i0 + per and i + blockDim.x leave int range
+    const int64_t per = ((int64_t)vocab + gridDim.x - 1) / gridDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * per, i1 = i0 + per < vocab ? i0 + per : (int64_t)vocab;
     unsigned long long best = 0ull;
-    for (int i = i0 + tid; i < i1; i += blockDim.x) {
+    for (int64_t i = i0 + tid; i < i1; i += blockDim.x) {
         const float v = lg[i];
         if (v == v) {
             const unsigned long long key = ((unsigned long long)float_key(v) << 32) | (0xFFFFFFFFu - (uint32_t)i);

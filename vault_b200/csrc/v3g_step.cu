@@ -822,7 +822,7 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
         ok = ok && tb < (int64_t)1 << 30;
         p.tbase[n] = (int)tb;
         max_rt = rb > max_rt ? rb : max_rt;
-        const size_t need = (size_t)(144 + (bs ? c.a.nblk * GEMV_MB : 0)) * 4 + (size_t)s->B * c.a.nblk * 64;
+        const size_t need = (size_t)(144 + (bs ? c.a.nblk * GEMV_MB : 0)) * 4 + (size_t)gemv_xrows(s->B) * c.a.nblk * 64;
         xr = need > xr ? need : xr;
         p.kind = MK_GEMV;
         p.epi = epi;

@@ -20,28 +20,7 @@ import torch
 
 from . import _lib
 from .config import VAULTv3Config
-from .vlt3 import VLT3Error
-
-
-def _aligned_bytes(src: Union[str, bytes, bytearray, memoryview]) -> np.ndarray:
-    """Host copy of a VLT3 file in a 64-byte aligned buffer (runtime/vault3.h:8 requires 64-byte alignment)."""
-    if isinstance(src, (bytes, bytearray, memoryview)):
-        data = np.frombuffer(src, dtype=np.uint8)
-        n = data.size
-    else:
-        with open(src, "rb") as f:
-            f.seek(0, 2)
-            n = f.tell()
-        data = None
-    raw = np.empty(n + 64, dtype=np.uint8)
-    off = (-raw.ctypes.data) % 64
-    buf = raw[off:off + n]
-    if data is not None:
-        buf[:] = data
-    else:
-        with open(src, "rb") as f:
-            f.readinto(memoryview(buf))
-    return buf
+from .vlt3 import VLT3Error, aligned_buffer
 
 
 def _stream() -> C.c_void_p:
@@ -153,7 +132,7 @@ class VAULTv3ForCausalLM:
         dev = torch.device("cuda", torch.cuda.current_device() if device is None else
                            (device.index if isinstance(device, torch.device) else int(device)))
         self.device = dev
-        buf = _aligned_bytes(vlt3)
+        buf = aligned_buffer(vlt3)
         L = _lib.lib()
         h = C.c_void_p()
         with torch.cuda.device(dev):

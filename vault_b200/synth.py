@@ -203,3 +203,27 @@ def full_config(**overrides) -> VAULTv3Config:
     for k, v in overrides.items():
         setattr(cfg, k, v)
     return cfg
+
+
+def full_model_file(fmt: str = "q8_0", seed: int = 0, directory: Optional[str] = None, **cfg_overrides) -> str:
+    """Path of a cached full-size synthetic model (the BASELINE architecture, `fmt` weights, seed `seed`), written
+    on first use with write_synthetic_vlt3_fast.  The directory is $VAULT_B200_BENCH_DIR (default: a folder in the
+    system temp dir); a `.done` marker next to the file says the export finished.  Extra keyword arguments override
+    config fields (for example n_sink=4, or the segment scorer fields) and become part of the file name."""
+    import tempfile
+    import time
+
+    d = directory or os.environ.get("VAULT_B200_BENCH_DIR", os.path.join(tempfile.gettempdir(), "vault_b200_bench"))
+    os.makedirs(d, exist_ok=True)
+    tag = "".join(f"_{k}{'-'.join(map(str, v)) if isinstance(v, (tuple, list)) else v}"
+                  for k, v in sorted(cfg_overrides.items()))
+    path = os.path.join(d, f"vault_v3_1p5b_{fmt}_seed{seed}{tag}.vlt3")
+    if not os.path.exists(path + ".done"):
+        import torch
+        cfg = full_config(**({"n_sink": 0} | cfg_overrides))
+        t0 = time.time()
+        write_synthetic_vlt3_fast(path, cfg, fmt, seed=seed, device="cuda" if torch.cuda.is_available() else "cpu")
+        open(path + ".done", "w").close()
+        print(f"[synth] wrote {path} ({os.path.getsize(path) / 1e9:.2f} GB) in {time.time() - t0:.1f}s",
+              flush=True)
+    return path

@@ -1,7 +1,9 @@
 """VLT3 checkpoint container: reader, validator, writer and Q8_0/Q4_0 block codecs.
 
-Host-side mirror of the reference's `tools/vlt3.py` (the VLT3 format is an on-disk contract, so the byte layout,
-field order, tensor ids, block layouts and validation rules are the same; the code is this project's own).
+Counterpart of the reference's `tools/vlt3.py`.  The VLT3 format is an on-disk contract, so the byte layout, field
+order, tensor ids, block layouts and the codecs' arithmetic are the same (the writer is checked byte-identical
+against the reference writer); validation is the engine's own C++ loader check (v3g_validate), shared with the
+device loader.
 
 Layout of a .vlt3 file (all little-endian):
     [ header: 4096 B, fixed fields, CRC32 of the first 4092 B in the last 4 B ]   tools/vlt3.py:64-74
@@ -90,6 +92,7 @@ Q4_BLOCK = np.dtype([("d", "<f2"), ("q", "u1", (QK // 2,))])
 # Candidate scale ratios searched by the clipped-MSE Q4_0 quantizer (tools/vlt3.py:123).
 _Q4_RATIOS = np.array([-1.0 / 8.0, -0.98 / 8.0, -0.96 / 8.0, -0.94 / 8.0, -0.92 / 8.0, -0.89 / 8.0,
                        1.0 / 7.5, 0.96 / 7.5], dtype=np.float32)
+_Q4_SLICE = 1 << 15   # blocks per candidate evaluation (8 x 32 x 4 B per block)
 
 
 class VLT3Error(ValueError):
@@ -142,35 +145,39 @@ def dequantize_q8_0(buf, n: int) -> np.ndarray:
     return (b["q"].astype(np.float32) * b["d"].astype(np.float32)[:, None]).reshape(-1)
 
 
+def _q4_candidates(xb: np.ndarray):
+    """Every candidate encoding of a stack of blocks: fp16 scales [n, R] (the block's signed absmax element times
+    each ratio of _Q4_RATIOS), their codes [n, R, 32] and squared reconstruction errors [n, R] (fp32 sums)."""
+    n = xb.shape[0]
+    peak = xb[np.arange(n), np.abs(xb).argmax(axis=1)]                 # signed element of largest magnitude
+    d16 = (peak[:, None] * _Q4_RATIOS[None, :]).astype(np.float16)     # [n, R]
+    d = d16.astype(np.float32)
+    inv = np.divide(np.float32(1.0), d, out=np.zeros_like(d), where=d != 0.0)
+    codes = np.clip(np.rint(xb[:, None, :] * inv[:, :, None] + np.float32(8.0)), 0.0, 15.0).astype(np.uint8)
+    recon = (codes.astype(np.float32) - np.float32(8.0)) * d[:, :, None]
+    err = np.square(recon - xb[:, None, :]).sum(axis=2)
+    return peak, d16, codes, err
+
+
 def quantize_q4_0(w: np.ndarray) -> bytes:
-    """Clipped-MSE Q4_0: for each block try 8 signed scale ratios of the absmax element and keep the first one
-    with the strictly smallest squared reconstruction error (tools/vlt3.py:119-149)."""
+    """Clipped-MSE Q4_0 (tools/vlt3.py:119-149): each block takes the candidate scale of smallest squared error,
+    the earliest ratio on ties; all-zero blocks (and blocks where no candidate has a finite error) keep d = 0 and
+    every code 8.  Blocks are processed in slices to bound the [n, 8, 32] candidate arrays."""
     x = np.ascontiguousarray(w, dtype=np.float32).reshape(-1, QK)
-    nb = x.shape[0]
-    blocks = np.empty(nb, dtype=Q4_BLOCK)
-    for s in range(0, nb, 262144):
-        xb = x[s:s + 262144]
+    blocks = np.zeros(x.shape[0], dtype=Q4_BLOCK)
+    blocks["q"] = 0x88
+    for lo in range(0, x.shape[0], _Q4_SLICE):
+        xb = x[lo:lo + _Q4_SLICE]
+        peak, d16, codes, err = _q4_candidates(xb)
+        err = np.where(np.isnan(err), np.float32(np.inf), err)
+        pick = err.argmin(axis=1)                                         # first minimum = earliest ratio on ties
         rows = np.arange(xb.shape[0])
-        mx = xb[rows, np.abs(xb).argmax(axis=1)]
-        best_err = np.full(xb.shape[0], np.inf, dtype=np.float32)
-        best_d = np.zeros(xb.shape[0], dtype=np.float16)
-        best_q = np.full((xb.shape[0], QK), 8, dtype=np.uint8)
-        nonzero = mx != 0.0
-        if nonzero.any():
-            for ratio in _Q4_RATIOS:
-                d16 = (mx * ratio).astype(np.float16)
-                d32 = d16.astype(np.float32)
-                inv = np.where(d32 != 0.0, np.float32(1.0) / np.where(d32 != 0.0, d32, np.float32(1.0)),
-                               np.float32(0.0))
-                qi = np.clip(np.rint(xb * inv[:, None] + np.float32(8.0)), 0.0, 15.0).astype(np.uint8)
-                err = np.square((qi.astype(np.float32) - np.float32(8.0)) * d32[:, None] - xb).sum(axis=1)
-                better = nonzero & (err < best_err)
-                if better.any():
-                    best_err[better] = err[better]
-                    best_d[better] = d16[better]
-                    best_q[better] = qi[better]
-        blocks["d"][s:s + 262144] = best_d
-        blocks["q"][s:s + 262144] = best_q[:, :QK // 2] | (best_q[:, QK // 2:] << 4)
+        ok = (peak != 0.0) & np.isfinite(err[rows, pick])
+        q = codes[rows, pick]                                             # [n, 32]: element j, j + 16 share a byte
+        sel = blocks[lo:lo + xb.shape[0]]
+        sel["d"] = np.where(ok, d16[rows, pick], np.float16(0.0))
+        sel["q"] = np.where(ok[:, None], q[:, :QK // 2] | (q[:, QK // 2:] << 4), np.uint8(0x88))
+        blocks[lo:lo + xb.shape[0]] = sel
     return blocks.tobytes()
 
 
@@ -291,56 +298,62 @@ def _letter_number_ranges() -> List[Tuple[int, int, int]]:
     return ranges
 
 
+# Roles of the ChatML control tokens in the header (tools/vlt3.py:299-305): role -> added-token text
+_CONTROL_ROLES = (("bos", "<|endoftext|>"), ("eos", "<|im_end|>"), ("im_start", "<|im_start|>"),
+                  ("im_end", "<|im_end|>"), ("pad", "<|endoftext|>"))
+_VTOK_HEAD, _VTOK_ALIGN = 128, 8
+
+
+def _token_strings(tj: dict) -> Dict[int, bytes]:
+    """id -> raw bytes of every vocabulary entry (byte-level strings decoded) and added token (UTF-8 text); an
+    added token overrides a vocabulary entry of the same id."""
+    decode = {ch: b for b, ch in byte_to_unicode().items()}
+    strings = {tid: bytes(decode[ch] for ch in text) for text, tid in tj["model"]["vocab"].items()}
+    strings.update({a["id"]: a["content"].encode("utf-8") for a in tj.get("added_tokens", [])})
+    return strings
+
+
+def _pack_sections(fixed: bytes, sections: Sequence[bytes]) -> bytes:
+    """VTOK container: `fixed` header fields, then the section offsets (u64 each), padded to _VTOK_HEAD bytes; each
+    section starts at the next multiple of _VTOK_ALIGN."""
+    offsets, end = [], _VTOK_HEAD
+    for sec in sections:
+        start = -(-end // _VTOK_ALIGN) * _VTOK_ALIGN
+        offsets.append(start)
+        end = start + len(sec)
+    out = bytearray(end)
+    head = fixed + struct.pack(f"<{len(offsets)}Q", *offsets)
+    out[:len(head)] = head
+    for start, sec in zip(offsets, sections):
+        out[start:start + len(sec)] = sec
+    return bytes(out)
+
+
 def build_tokenizer_blob(tokenizer_dir: str) -> Tuple[bytes, Dict[str, int]]:
+    """The VTOK tokenizer section of a VLT3 file from a byte-level BPE `tokenizer.json` (format of
+    tools/vlt3.py:246-305): a string table (offset, length per id) into one byte pool, the merge triples
+    (left, right, merged), the sorted control-token ids, the letter/number code-point runs of the pre-tokenizer and
+    the id of every single byte.  Returns the blob and the control-token ids of the header."""
     with open(os.path.join(tokenizer_dir, "tokenizer.json"), encoding="utf-8") as f:
         tj = json.load(f)
-    u2b = {u: b for b, u in byte_to_unicode().items()}
     vocab: Dict[str, int] = tj["model"]["vocab"]
+    strings = _token_strings(tj)
+    n_vocab = max(strings) + 1
+    ordered = [strings.get(i, b"") for i in range(n_vocab)]
+    lengths = np.fromiter((len(t) for t in ordered), dtype=np.int64, count=n_vocab)
+    starts = np.cumsum(lengths) - lengths
+    table = np.stack([starts, lengths], axis=1).astype("<u4")
+    pairs = (m.split(" ", 1) if isinstance(m, str) else m for m in tj["model"]["merges"])
+    merges = np.array([(vocab[l], vocab[r], vocab[l + r]) for l, r in pairs], dtype="<u4").reshape(-1, 3)
     added = {a["content"]: a["id"] for a in tj.get("added_tokens", [])}
-    n_vocab = max(max(vocab.values()), max(added.values()) if added else 0) + 1
-    tok_bytes: List[bytes] = [b""] * n_vocab
-    for s, i in vocab.items():
-        tok_bytes[i] = bytes(u2b[ch] for ch in s)
-    for s, i in added.items():
-        tok_bytes[i] = s.encode("utf-8")
-    merges = []
-    for m in tj["model"]["merges"]:
-        a, b = m.split(" ", 1) if isinstance(m, str) else m
-        merges.append((vocab[a], vocab[b], vocab[a + b]))
+    controls = np.array(sorted(added.values()), dtype="<u4")
+    runs = np.array(_letter_number_ranges(), dtype="<u4").reshape(-1, 3)
     b2u = byte_to_unicode()
-    byte_tok = [vocab[b2u[b]] for b in range(256)]
-    specials = sorted(added.values())
-    table = np.zeros((n_vocab, 2), dtype="<u4")
-    pool = bytearray()
-    for i, tb in enumerate(tok_bytes):
-        table[i] = (len(pool), len(tb))
-        pool += tb
-    sections = [
-        table.tobytes(), bytes(pool),
-        np.asarray(merges, dtype="<u4").tobytes(),
-        np.asarray(specials, dtype="<u4").tobytes(),
-        np.asarray(_letter_number_ranges(), dtype="<u4").tobytes(),
-        np.asarray(byte_tok, dtype="<u4").tobytes(),
-    ]
-    offsets, cur = [], 128
-    for s in sections:
-        cur = (cur + 7) & ~7
-        offsets.append(cur)
-        cur += len(s)
-    head = struct.pack("<4sIIIIII", b"VTOK", 1, n_vocab, len(merges), len(specials),
-                       len(sections[4]) // 12, 0) + struct.pack("<6Q", *offsets)
-    blob = bytearray(head.ljust(128, b"\0"))
-    for off, s in zip(offsets, sections):
-        blob += b"\0" * (off - len(blob))
-        blob += s
-    ids = {
-        "bos": added.get("<|endoftext|>", 0),
-        "eos": added.get("<|im_end|>", 0),
-        "im_start": added.get("<|im_start|>", 0),
-        "im_end": added.get("<|im_end|>", 0),
-        "pad": added.get("<|endoftext|>", 0),
-    }
-    return bytes(blob), ids
+    byte_ids = np.array([vocab[b2u[b]] for b in range(256)], dtype="<u4")
+    fixed = struct.pack("<4s6I", b"VTOK", 1, n_vocab, merges.shape[0], controls.size, runs.shape[0], 0)
+    blob = _pack_sections(fixed, [table.tobytes(), b"".join(ordered), merges.tobytes(), controls.tobytes(),
+                                  runs.tobytes(), byte_ids.tobytes()])
+    return blob, {role: added.get(text, 0) for role, text in _CONTROL_ROLES}
 
 
 def parse_token_bytes(blob, vocab_size: int) -> List[bytes]:
@@ -476,108 +489,59 @@ class VLT3File:
         return self.buf[h["tokenizer_offset"]: h["tokenizer_offset"] + h["tokenizer_size"]]
 
 
-def _finite_payload(buf, dt: int, n: int) -> bool:
-    if dt == F32:
-        return bool(np.isfinite(np.frombuffer(buf, dtype="<f4", count=n)).all())
-    if dt == F16:
-        return bool(np.isfinite(np.frombuffer(buf, dtype="<f2", count=n)).all())
-    if dt == BF16:
-        return not bool(((np.frombuffer(buf, dtype="<u2", count=n) & 0x7F80) == 0x7F80).any())
-    blocks = np.frombuffer(buf, dtype=Q8_BLOCK if dt == Q8_0 else Q4_BLOCK, count=n // QK)
-    return bool(np.isfinite(blocks["d"]).all())
+def aligned_buffer(src) -> np.ndarray:
+    """Host copy of a VLT3 file (path or bytes) in a 64-byte aligned uint8 buffer: the alignment the format's
+    readers require of a model buffer (runtime/vault3.h:8)."""
+    if isinstance(src, (bytes, bytearray, memoryview)):
+        data = np.frombuffer(src, dtype=np.uint8)
+        n = data.size
+    else:
+        data, n = None, os.path.getsize(src)
+    raw = np.empty(n + ALIGN, dtype=np.uint8)
+    off = (-raw.ctypes.data) % ALIGN
+    buf = raw[off:off + n]
+    if data is not None:
+        buf[:] = data
+    else:
+        with open(src, "rb") as f:
+            f.readinto(memoryview(buf))
+    return buf
+
+
+def _unpack_header(buf) -> Dict:
+    """Header fields by name (the _HEADER_FIELDS table; array fields as lists)."""
+    flat = iter(_HEADER_STRUCT.unpack_from(buf, 0))
+    out: Dict = {}
+    for fname, code in _HEADER_FIELDS:
+        count = int(code[:-1]) if code[:-1].isdigit() and code[-1] == "I" else 1
+        out[fname] = [next(flat) for _ in range(count)] if count > 1 else next(flat)
+    return out
+
+
+def _unpack_entry(buf, at: int) -> Dict:
+    tid, dt, ndim, d0, d1, d2, d3, _reserved, off, nb, crc, nm = _ENTRY_STRUCT.unpack_from(buf, at)
+    return dict(id=tid, dtype=dt, ndim=ndim, dims=[d0, d1, d2, d3], offset=off, nbytes=nb, crc=crc,
+                name=nm.rstrip(b"\0").decode("utf-8", "replace"))
 
 
 def read_vlt3(path_or_bytes, check_crc: bool = True) -> VLT3File:
-    """Parse and validate a VLT3 file (tools/vlt3.py:453-545).  Raises VLT3Error on any inconsistency."""
-    if isinstance(path_or_bytes, (bytes, bytearray, memoryview)):
-        data = bytes(path_or_bytes)
-    else:
-        with open(path_or_bytes, "rb") as f:
-            data = f.read()
-    size = len(data)
-    if size < HEADER_SIZE:
-        raise VLT3Error("file smaller than header")
-    if zlib.crc32(data[: HEADER_SIZE - 4]) != struct.unpack_from("<I", data, HEADER_SIZE - 4)[0]:
-        raise VLT3Error("header CRC mismatch")
-    vals = list(_HEADER_STRUCT.unpack_from(data, 0))
-    h: Dict = {}
-    for fname, code in _HEADER_FIELDS:
-        k = 8 if code == "8I" else (4 if code == "4I" else 1)
-        h[fname] = vals[:k] if k > 1 else vals[0]
-        del vals[:k]
-    if (h["magic"] != MAGIC or h["version"] != VERSION or h["header_size"] != HEADER_SIZE
-            or h["endian_tag"] != ENDIAN_TAG):
-        raise VLT3Error("bad magic/version/header_size/endianness")
-    if h["file_size"] != size:
-        raise VLT3Error(f"file_size {h['file_size']} != actual {size}")
-    if h["alignment"] != ALIGN:
-        raise VLT3Error("unsupported alignment")
-    for what, off_k, n_k in (("tensor directory", "tensor_dir_offset", "tensor_dir_size"),
-                             ("tokenizer", "tokenizer_offset", "tokenizer_size"),
-                             ("data", "data_offset", "data_size")):
-        off, n = h[off_k], h[n_k]
-        if off < HEADER_SIZE or off > size or n > size - off:
-            raise VLT3Error(f"{what} out of bounds")
-    if h["tensor_dir_size"] != h["n_tensors"] * ENTRY_SIZE:
-        raise VLT3Error("tensor_dir_size != n_tensors * 128")
-    if not (0 < h["n_layers"] <= 64) or not (0 < h["n_heads"] <= 256) or not (0 < h["head_dim"] <= 256):
-        raise VLT3Error("bad layer/head dimensions")
-    if h["n_kv_heads"] == 0 or h["n_heads"] % h["n_kv_heads"] or h["n_heads"] * h["head_dim"] != h["d_model"]:
-        raise VLT3Error("inconsistent GQA/d_model dimensions")
-    if h["n_sink"] > 512 or h["n_sink"] > h["window"]:
-        raise VLT3Error("bad n_sink")
-    if h["n_banks"] or h["n_cells"] or any(h["primes"]):
-        raise VLT3Error("bad vault bank description (expected 0 in Kenyon-free VLT3)")
-    if not (np.isfinite(h["rms_eps"]) and h["rms_eps"] > 0 and np.isfinite(h["rope_theta"])
-            and h["rope_theta"] > 1.0 and np.isfinite(h["vault_eps"])):
-        raise VLT3Error("non-finite or invalid eps/theta")
-    nf = h["seg_n_feat"]
-    if nf > 0:
-        if nf > 4 or not (0 < h["seg_hidden"] <= 1024) or not (0 < h["seg_min"] <= h["seg_max"] <= h["window"]):
-            raise VLT3Error("invalid segment scorer hyperparameters")
-        if h["seg_budget"] > 16384 or any(l >= h["n_layers"] for l in h["seg_layers"][:nf]):
-            raise VLT3Error("invalid segment budget or feature layers")
-    buf = memoryview(data)
-    entries: List[Dict] = []
-    by_id: Dict[int, Dict] = {}
-    spans = []
-    for k in range(h["n_tensors"]):
-        tid, dt, ndim, d0, d1, d2, d3, rsv, off, nb, crc, nm = _ENTRY_STRUCT.unpack_from(
-            data, h["tensor_dir_offset"] + k * ENTRY_SIZE)
-        dims = [d0, d1, d2, d3]
-        if rsv:
-            raise VLT3Error(f"tensor entry {k}: reserved field not zero")
-        if tid in by_id:
-            raise VLT3Error(f"duplicate tensor id {tid}")
-        if dt not in DTYPE_NAMES or not (1 <= ndim <= 4) or any(x == 0 for x in dims[:ndim]):
-            raise VLT3Error(f"bad dtype/ndim/zero-dim for tensor {tid}")
-        n = int(np.prod([int(x) for x in dims[:ndim]]))
-        if dt in (Q8_0, Q4_0) and n % QK:
-            raise VLT3Error(f"tensor {tid}: quantized size not a multiple of 32")
-        if nb != nbytes_for(dt, n):
-            raise VLT3Error(f"tensor {tid}: nbytes {nb} inconsistent with dtype/dims")
-        if off % ALIGN or off < h["data_offset"] or nb > h["data_offset"] + h["data_size"] - off:
-            raise VLT3Error(f"tensor {tid}: offset out of data region or misaligned")
-        if check_crc and zlib.crc32(buf[off: off + nb]) != crc:
-            raise VLT3Error(f"tensor {tid}: CRC mismatch")
-        if not _finite_payload(buf[off: off + nb], dt, n):
-            raise VLT3Error(f"tensor {tid}: non-finite values")
-        spans.append((off, off + nb))
-        e = dict(id=tid, dtype=dt, ndim=ndim, dims=dims, offset=off, nbytes=nb, crc=crc,
-                 name=nm.rstrip(b"\0").decode("utf-8", "replace"))
-        entries.append(e)
-        by_id[tid] = e
-    spans.sort()
-    for (_a0, a1), (b0, _b1) in zip(spans, spans[1:]):
-        if b0 < a1:
-            raise VLT3Error("overlapping tensors")
-    need = {1, 2} | {((l + 1) << 8) | (j + 1) for l in range(h["n_layers"]) for j in range(len(LAYER_KINDS))}
-    if nf > 0:
-        need |= set(SCORER_IDS)
-    missing = need - set(by_id)
-    if missing:
-        raise VLT3Error(f"missing tensors: {sorted(missing)[:5]}")
-    return VLT3File(h, entries, buf, by_id)
+    """Open a VLT3 file (the role of tools/vlt3.py:453-545 read_vlt3).
+
+    The file is validated by the engine's own loader checks (v3g_validate: the rules of the reference C runtime's
+    v3_load, runtime/vault3.c:273-455 -- bounds, alignment, dtypes and shapes of every required tensor, finite
+    scales and weights, CRCs when check_crc, the tokenizer section), so this reader and the device loader accept
+    exactly the same files.  A rejected file raises VLT3Error naming the status code and the failed check."""
+    from . import _lib
+
+    buf = aligned_buffer(path_or_bytes)
+    L = _lib.lib()
+    rc = L.v3g_validate(buf.ctypes.data, buf.size, int(bool(check_crc)))
+    if rc != 0:
+        raise VLT3Error(f"{L.v3g_error_string(rc).decode()} ({rc}): {_lib.last_error()}")
+    mv = memoryview(buf)
+    header = _unpack_header(mv)
+    entries = [_unpack_entry(mv, header["tensor_dir_offset"] + k * ENTRY_SIZE) for k in range(header["n_tensors"])]
+    return VLT3File(header, entries, mv, {e["id"]: e for e in entries})
 
 
 def vlt3_to_state_dict(vf: VLT3File) -> Dict[str, np.ndarray]:
