@@ -138,6 +138,15 @@ V3G_API int v3g_seq_info(v3g_state *s, uint32_t b, v3g_seq_info_t *info, int64_t
 /* Kernel-level entry points (tests and the kernel sweep).  tensor_id uses the VLT3 ids of tools/vlt3.py:34-57. */
 V3G_API int v3g_dequant(const v3g_model *m, uint32_t tensor_id, float *dev_out, void *stream);
 V3G_API int v3g_gemv(const v3g_model *m, uint32_t tensor_id, const float *dev_x, uint32_t batch, float *dev_y, void *stream);
+/* Tensor-core GEMM of one stored weight matrix against n_tok fp32 activation rows: dev_y[t, r] = sum_k W[r, k]
+ * dev_x[t, k] (row t of dev_x has the matrix's K entries; dev_y rows have the matrix's row count, gate/up as
+ * [gate; up]).  The kernel the chunked prefill and the batched decode step run for every projection: weights
+ * dequantized to fp16 in shared memory, tcgen05 MMA into tensor memory.  It is the many-token form of the
+ * reference's row_dot / matvec (runtime/vault3.c:499-624) and nn.Linear (src/vault_v3_model.py:1036-1039).
+ * dev_work: caller-owned device workspace (256-byte aligned) of v3g_gemm_work_size bytes. */
+V3G_API size_t v3g_gemm_work_size(const v3g_model *m, uint32_t tensor_id, uint32_t n_tok);
+V3G_API int v3g_gemm(const v3g_model *m, uint32_t tensor_id, const float *dev_x, uint32_t n_tok, float *dev_y,
+                     void *dev_work, size_t work_bytes, void *stream);
 /* One launch of the persistent decode kernel (every layer of the current position, plus the lm head when want_lm)
  * on a state whose steps use it, without the step's token bookkeeping: for timing the kernel alone.  It rewrites
  * the current position's activations and KV rows, so reset the state before decoding again. */

@@ -51,6 +51,7 @@ struct MatW {
     int rowmap = ROWS_IDENTITY;
     uint64_t file_bytes = 0;         // payload bytes of the source tensor(s) in the VLT3 file
     float wscale = 1.f;              // tile values x wscale = weights (2^-s for BF16 / F32 tiles, else 1)
+    int dexp = 0;                    // Q8_0 / Q4_0: the tensor-core GEMM dequantizes to fp16 q d 2^dexp (no subnormals)
 };
 
 constexpr int MAX_LAYERS = 64;

@@ -1,0 +1,210 @@
+// Host side of the tensor-core GEMM (launch planning, activation tensor maps), the activation operand kernel, and
+// the kernel-level entry point v3g_gemm used by the tests and the kernel sweep.
+#include <string.h>
+
+#include <cmath>
+
+#include <mutex>
+
+#include "../../include/vault_b200.h"
+#include "v3g_gemm.cuh"
+#include "v3g_internal.h"
+
+namespace v3g {
+
+// ------------------------------------------------------------------------------------------ activation operand
+__global__ void __launch_bounds__(256) k_tc_prep(const float *x, int64_t ld_x, int K, const float *norm_w, float eps,
+                                                 __half *out, int ldo, float *xscale) {
+    const int r = blockIdx.x, tid = threadIdx.x;
+    const float *xr = x + (int64_t)r * ld_x;
+    __shared__ float red[2][8];
+    float ss = 0.f, mx = 0.f;
+    for (int k = tid; k < K; k += blockDim.x) {
+        const float v = xr[k];
+        ss = fmaf(v, v, ss);
+        mx = fmaxf(mx, fabsf(norm_w ? v * norm_w[k] : v));
+    }
+    ss = warp_sum(ss);
+    mx = warp_max(mx);
+    if ((tid & 31) == 0) {
+        red[0][tid >> 5] = ss;
+        red[1][tid >> 5] = mx;
+    }
+    __syncthreads();
+    float S = 0.f, M = 0.f;
+    for (int w = 0; w < (int)blockDim.x / 32; ++w) {
+        S += red[0][w];
+        M = fmaxf(M, red[1][w]);
+    }
+    const float inv = norm_w ? rsqrtf(S / (float)K + eps) : 1.f;
+    // largest |value| into (2^13, 2^14]: exponent from the float bits (zero / subnormal maxima keep e = 0)
+    const int be = (__float_as_int(M * inv) >> 23) & 0xff;
+    int e = be > 0 ? be - 140 : 0;
+    e = e < -126 ? -126 : (e > 126 ? 126 : e);
+    const float mul = inv * __int_as_float((127 - e) << 23);
+    __half *o = out + (int64_t)r * ldo;
+    for (int k = tid; k < ldo; k += blockDim.x) {
+        const float v = k < K ? xr[k] * (norm_w ? norm_w[k] : 1.f) * mul : 0.f;
+        o[k] = __float2half_rn(v);
+    }
+    if (tid == 0) xscale[r] = __int_as_float((127 + e) << 23);
+}
+
+cudaError_t tc_prep(const float *x, int64_t ld_x, int n, int K, const float *norm_w, float eps, __half *out, int ldo,
+                    float *xscale, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    k_tc_prep<<<n, 256, 0, st>>>(x, ld_x, K, norm_w, eps, out, ldo, xscale);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------ tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// fp16 matrix [rows, K] with row stride ld elements, loaded as (64 k) x (box_rows rows) boxes with the 128-byte
+// swizzle; reads past K or past the last row return zeros
+static cudaError_t make_xmap(CUtensorMap *map, const __half *x, int rows, int K, int ld, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ld * 2) % 16) return cudaErrorInvalidValue;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(x), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// ------------------------------------------------------------------------------------------------ launch plan
+cudaError_t tc_setup(TcLaunch &L, const MatW *const *mats, int n, const __half *x16, int ldx, const float *xscale,
+                     int n_tok, int *status, int n_sm) {
+    memset(&L, 0, sizeof(L));
+    TcArgs &a = L.a;
+    if (n < 1 || n > 3 || n_tok < 1) return cudaErrorInvalidValue;
+    bool has[16] = {};
+    int rb = 0;
+    for (int i = 0; i < n; ++i) {
+        const MatW &w = *mats[i];
+        if (!(w.fmt == FMT_Q8 || w.fmt == FMT_Q4 || w.fmt == FMT_BF16 || w.fmt == FMT_F16)) return cudaErrorNotSupported;
+        if (i > 0 && w.cols != mats[0]->cols) return cudaErrorInvalidValue;
+        has[w.fmt] = true;
+        a.seg[i].tiles = w.tiles;
+        a.seg[i].n_rtiles = w.n_rtiles;
+        a.seg[i].n_ktiles = w.n_ktiles;
+        a.seg[i].fmt = w.fmt;
+        a.seg[i].dexp = (w.fmt == FMT_Q8 || w.fmt == FMT_Q4) ? w.dexp : 0;
+        a.seg[i].wscale = (w.fmt == FMT_Q8 || w.fmt == FMT_Q4) ? std::ldexp(1.f, -w.dexp) : w.wscale;
+        a.rbase[i] = rb;
+        rb += w.n_rtiles;
+    }
+    a.n_seg = n;
+    a.rbase[n] = rb;
+    int nf = 0;
+    for (bool h : has) nf += h ? 1 : 0;
+    if (nf == 1) {
+        L.fa = L.fb = mats[0]->fmt;
+    } else if (nf == 2 && has[FMT_Q4] && has[FMT_Q8]) {
+        L.fa = FMT_Q4;
+        L.fb = FMT_Q8;
+    } else {
+        return cudaErrorNotSupported;
+    }
+    a.K = mats[0]->cols;
+    if (ldx < a.K) return cudaErrorInvalidValue;
+    a.kstages = (a.K + TC_BK - 1) / TC_BK;
+    a.m_tiles = (rb + 7) / 8;
+    a.n_tok = n_tok;
+    // token tile: the smallest multiple of 16 covering n_tok, at most 256 (the MMA's N range for M = 128)
+    a.bn = n_tok >= 256 ? 256 : (n_tok + 15) / 16 * 16;
+    a.n_tiles = (n_tok + a.bn - 1) / a.bn;
+    a.xscale = xscale;
+    a.status = status;
+    a.seg_base = 0;
+    a.stage_a = TC_BM * TC_BK * 2;
+    a.stage_x = a.bn * TC_BK * 2;
+    a.stage_raw = 8 * TC_RAW_ROW;
+    const int per_stage = a.stage_a + a.stage_x + a.stage_raw;
+    const int budget = 227 * 1024 - 1024 - 256;
+    a.stages = budget / per_stage < TC_MAX_STAGES ? budget / per_stage : TC_MAX_STAGES;
+    if (a.stages < 2) return cudaErrorInvalidValue;
+    a.a_off = 0;
+    a.x_off = a.stages * a.stage_a;
+    a.raw_off = a.x_off + a.stages * a.stage_x;
+    a.bar_off = a.raw_off + a.stages * a.stage_raw;
+    L.smem = (size_t)a.bar_off + 8 * (3 * a.stages + 4) + 16 + 1024;   // + slack for the 1024-byte alignment
+    const int work = a.m_tiles * a.n_tiles;
+    L.grid = work < n_sm ? work : n_sm;
+    return make_xmap(&L.xmap, x16, n_tok, a.K, ldx, a.bn);
+}
+
+// ------------------------------------------------------------------------------------------- test epilogue
+// y[token, source row] = value: undoes the RoPE-pair / gate-up row order of the tiles (seg = matrix index)
+struct TcEpiStore {
+    float *y;
+    int64_t ld;
+    int rowmap, head_dim, src_rows;
+    __device__ void operator()(int, int rt, int g, int tok, float y0, float y1) const {
+        int src, row;
+        if (map_tile_row(rowmap, head_dim, src_rows, TILE_ROWS * rt + g, src, row))
+            y[tok * ld + src * src_rows + row] = y0;
+        if (map_tile_row(rowmap, head_dim, src_rows, TILE_ROWS * rt + g + 8, src, row))
+            y[tok * ld + src * src_rows + row] = y1;
+    }
+};
+
+}  // namespace v3g
+
+using namespace v3g;
+
+static const MatW *tc_find_mat(const v3g_model *m, uint32_t id) {
+    for (auto &p : m->tensor_index)
+        if (p.first == id) return p.second;
+    return nullptr;
+}
+
+extern "C" size_t v3g_gemm_work_size(const v3g_model *m, uint32_t tensor_id, uint32_t n_tok) {
+    const MatW *w = m ? tc_find_mat(m, tensor_id) : nullptr;
+    if (!w || n_tok == 0) return 0;
+    const size_t ldx = (size_t)(w->cols + 63) / 64 * 64;
+    return ((size_t)n_tok * ldx * 2 + 255) / 256 * 256 + ((size_t)n_tok * 4 + 255) / 256 * 256 + 256;
+}
+
+extern "C" int v3g_gemm(const v3g_model *m, uint32_t tensor_id, const float *dev_x, uint32_t n_tok, float *dev_y,
+                        void *dev_work, size_t work_bytes, void *stream) {
+    if (!m || !dev_x || !dev_y || !dev_work || n_tok == 0) return v3g_fail(V3G_E_ARG, "null argument or zero tokens");
+    const MatW *w = tc_find_mat(m, tensor_id);
+    if (!w) return v3g_fail(V3G_E_MISSING, "no device matrix for this tensor id");
+    if (work_bytes < v3g_gemm_work_size(m, tensor_id, n_tok) || (reinterpret_cast<uintptr_t>(dev_work) & 255))
+        return v3g_fail(V3G_E_ARG, "workspace too small or not 256-byte aligned (v3g_gemm_work_size)");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int ldx = (w->cols + 63) / 64 * 64;
+    uint8_t *wp = static_cast<uint8_t *>(dev_work);
+    __half *x16 = reinterpret_cast<__half *>(wp);
+    float *xs = reinterpret_cast<float *>(wp + ((size_t)n_tok * ldx * 2 + 255) / 256 * 256);
+    int *status = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(xs) + ((size_t)n_tok * 4 + 255) / 256 * 256);
+    cudaError_t e = cudaMemsetAsync(status, 0, 4, st);
+    if (e == cudaSuccess) e = tc_prep(dev_x, w->cols, (int)n_tok, w->cols, nullptr, 0.f, x16, ldx, xs, st);
+    const MatW *mats[1] = {w};
+    const int src_rows = w->rowmap == ROWS_GATE_UP ? w->rows / 2 : w->rows;
+    TcEpiStore epi{dev_y, (int64_t)w->rows, w->rowmap, m->host.D, src_rows};
+    if (e == cudaSuccess) e = tc_gemm(mats, 1, x16, ldx, xs, (int)n_tok, status, m->n_sm, epi, st);
+    if (e == cudaErrorNotSupported) return v3g_fail(V3G_E_UNSUPPORTED, "matrix format has no tensor-core path (F32)");
+    if (e != cudaSuccess) return v3g_fail(V3G_E_CUDA, std::string("v3g_gemm: ") + cudaGetErrorString(e));
+    return V3G_OK;
+}

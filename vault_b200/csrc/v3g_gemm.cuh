@@ -1,0 +1,432 @@
+// Tensor-core (tcgen05) GEMM over the engine's quantized weight tiles, for work with many tokens per weight row:
+// chunked prefill and batched decode.
+//
+//   Y[token, row] = epilogue( sum_k W[row, k] * X[token, k] )
+//
+// W is one or more re-tiled weight matrices of the same K (v3g.cuh tile formats; several matrices are stacked row
+// tile after row tile, e.g. q | k | v), X the activations of n_tok tokens as fp16 rows [n_tok, K] with a per-token
+// power-of-two scale (k_tc_prep writes them).  The weights are the MMA's A operand (M = 128 rows = 8 row tiles per
+// CTA tile), the tokens its B operand (N = bn tokens, 16..256), the fp32 accumulator lives in tensor memory.
+//
+// One persistent CTA per SM walks the (128-row, bn-token) output tiles with warp-specialised roles:
+//   warp 0      producer: for every 64-wide k stage, bulk-copies the 8 row tiles' stored weight bytes (their
+//               k tiles are contiguous in HBM) and loads the bn x 64 activation box with the tensor map (TMA,
+//               128-byte swizzle), all completing on the stage's `full` mbarrier;
+//   warps 2-5   converters: dequantize the stage's weight bytes into the A operand (fp16, K-major, 128-byte
+//               swizzle) -- Q8_0 codes and Q4_0 nibbles times their fp16 block scale (times a per-matrix power of two
+//               that keeps small scales out of the fp16 subnormal range), 16-bit tiles copied -- then fence the
+//               writes to the async proxy and arrive on `conv`;
+//   warp 1      allocates 512 TMEM columns (two accumulator buffers) and issues, from one thread, the four
+//               tcgen05.mma (K = 16 each) of every stage, committing the stage's `empty` barrier (its buffers may be
+//               refilled) and, after a tile's last stage, the buffer's `acc_full` barrier;
+//   warps 6-9   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32 (w % 4) ..), scale each token's
+//               column by its activation scale and the matrix's weight scale, and hand (row g, row g+8) pairs of a
+//               16-row tile to the fused epilogue -- the partners of the RoPE / gate-up row order sit 8 lanes apart;
+//               then release the accumulator buffer (`acc_empty`).
+// Every wait is bounded: a wait that runs out records status bit 4 (timeout) and its role stops.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include "v3g.cuh"
+#include "v3g_tc.cuh"
+
+namespace v3g {
+
+constexpr int TC_BM = 128;            // weight rows per CTA tile (8 row tiles)
+constexpr int TC_BK = 64;             // k per stage (one 128-byte swizzled row)
+constexpr int TC_THREADS = 320;       // 10 warps
+constexpr int TC_CONV_WARPS = 4;
+constexpr int TC_RAW_ROW = 2048;      // stored weight bytes of one row tile per stage (16-bit tiles: 4 x 512)
+constexpr int TC_MAX_STAGES = 4;
+constexpr int TC_TMEM_COLS = 512;
+
+struct TcSeg {
+    const uint8_t *tiles;
+    int n_rtiles, n_ktiles, fmt;
+    float wscale;     // output multiplier of this matrix (16-bit tiles: MatW::wscale; integer formats: 2^-dexp)
+    int dexp;         // integer formats: the converter multiplies block scales by 2^dexp
+};
+
+struct TcArgs {
+    TcSeg seg[3];
+    int n_seg;
+    int rbase[4];     // flat row tile where segment s starts; rbase[n_seg] = total row tiles
+    int m_tiles;      // ceil(total row tiles / 8)
+    int K, kstages;   // logical K, ceil(K / 64)
+    int n_tok, bn, n_tiles;
+    int stages;
+    int seg_base;          // segment index the epilogue receives for seg[0]
+    const float *xscale;   // [n_tok] multiplier undoing each token's activation scale
+    int *status;           // sticky error word (bit 4: a bounded wait ran out)
+    // shared-memory layout (bytes from the 1024-aligned base)
+    int a_off, x_off, raw_off, bar_off, stage_a, stage_x, stage_raw;
+};
+
+__host__ __device__ inline int tc_stage_raw_bytes(int fmt) {
+    return fmt == FMT_Q8 ? 2 * 544 : (fmt == FMT_Q4 ? 576 : 4 * 512);
+}
+
+// ---------------------------------------------------------------------------------------------- weight converters
+// byte offset inside a 128-row x 64-k SW128 operand tile of the 4-byte pair at (row p, k = 8 j + 2 t)
+__device__ __forceinline__ uint32_t sw128_pair_off(int p, int j, int t) {
+    return (uint32_t)(p * 128 + ((j ^ (p & 7)) << 4) + 4 * t);
+}
+
+// fp16x2 {1152 + q0, 1152 + q1} (biased codes through the byte-permute of v3g_gemv.cuh) -> {q0 d, q1 d} rounded
+__device__ __forceinline__ uint32_t q8_dequant_pair(uint32_t w, uint32_t sel, __half2 d2) {
+    const uint32_t v = __byte_perm(w, 0x64646464u, sel);
+    __half2 h = *reinterpret_cast<const __half2 *>(&v);
+    h = __hsub2(h, __float2half2_rn(1152.f));
+    h = __hmul2(h, d2);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+template <int SH>
+__device__ __forceinline__ uint32_t q4_dequant_pair(uint32_t w, __half2 d2) {
+    const uint32_t v = ((w >> SH) & 0x000F000Fu) | 0x64006400u;   // {1024 + n}
+    __half2 h = *reinterpret_cast<const __half2 *>(&v);
+    h = __hsub2(h, __float2half2_rn(1032.f));                      // n - 8, exact
+    h = __hmul2(h, d2);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// One stored tile (this lane's 16 bytes at `tb`) into the A operand at row tile rl (0..7), k offset k0 in the
+// stage (0, 16, 32 or 48 for 16-bit tiles; 0 or 32 for Q8_0; 0 for Q4_0).  tb == nullptr writes zeros (k past K).
+template <int FMT>
+__device__ __forceinline__ void tc_convert_tile(uint8_t *A, const uint8_t *tb, int rl, int k0, int lane, __half2 dmul) {
+    const int g = lane >> 2, t = lane & 3;
+    const int p0 = 16 * rl + g, p1 = p0 + 8;
+    if constexpr (FMT == FMT_Q8) {
+        uint4 q = make_uint4(0u, 0u, 0u, 0u);
+        __half2 dg = __float2half2_rn(0.f), dh = dg;
+        if (tb) {
+            q = *reinterpret_cast<const uint4 *>(tb + lane * 16);
+            const uint32_t sw = *reinterpret_cast<const uint32_t *>(tb + 512 + g * 4);
+            const __half2 s2 = __hmul2(*reinterpret_cast<const __half2 *>(&sw), dmul);   // {d(row g), d(row g+8)}
+            dg = __low2half2(s2);
+            dh = __high2half2(s2);
+        }
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        // lane bytes: [s (k16 step)][reg][half]; reg bit 0 = row g+8, bit 1 = k + 8
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+            const int j0 = (k0 >> 3) + 2 * s;
+            *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p0, j0, t)) = q8_dequant_pair(w[2 * s], 0x4140u, dg);
+            *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p1, j0, t)) = q8_dequant_pair(w[2 * s], 0x4342u, dh);
+            *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p0, j0 + 1, t)) = q8_dequant_pair(w[2 * s + 1], 0x4140u, dg);
+            *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p1, j0 + 1, t)) = q8_dequant_pair(w[2 * s + 1], 0x4342u, dh);
+        }
+    } else if constexpr (FMT == FMT_Q4) {
+        uint4 q = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+        __half2 dg[2], dh[2];
+        dg[0] = dg[1] = dh[0] = dh[1] = __float2half2_rn(0.f);
+        if (tb) {
+            q = *reinterpret_cast<const uint4 *>(tb + lane * 16);
+            const uint2 sw = *reinterpret_cast<const uint2 *>(tb + 512 + g * 8);
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                const uint32_t wb = b ? sw.y : sw.x;
+                const __half2 s2 = __hmul2(*reinterpret_cast<const __half2 *>(&wb), dmul);
+                dg[b] = __low2half2(s2);
+                dh[b] = __high2half2(s2);
+            }
+        }
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        // word s = k16 step s; nibble (reg, half) at bit 4 reg + 16 half; block = s >> 1
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const int j0 = 2 * s, b = s >> 1;
+            *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p0, j0, t)) = q4_dequant_pair<0>(w[s], dg[b]);
+            *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p1, j0, t)) = q4_dequant_pair<4>(w[s], dh[b]);
+            *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p0, j0 + 1, t)) = q4_dequant_pair<8>(w[s], dg[b]);
+            *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p1, j0 + 1, t)) = q4_dequant_pair<12>(w[s], dh[b]);
+        }
+    } else {   // 16-bit tiles (fp16 values, already scaled): copy the fragment pairs
+        uint4 q = make_uint4(0u, 0u, 0u, 0u);
+        if (tb) q = *reinterpret_cast<const uint4 *>(tb + lane * 16);
+        const int j0 = k0 >> 3;
+        *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p0, j0, t)) = q.x;
+        *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p1, j0, t)) = q.y;
+        *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p0, j0 + 1, t)) = q.z;
+        *reinterpret_cast<uint32_t *>(A + sw128_pair_off(p1, j0 + 1, t)) = q.w;
+    }
+}
+
+// segment and segment-local row tile of flat row tile R
+__device__ __forceinline__ int tc_seg_of(const TcArgs &a, int R, int &rt) {
+    int s = 0;
+    while (s + 1 < a.n_seg && R >= a.rbase[s + 1]) ++s;
+    rt = R - a.rbase[s];
+    return s;
+}
+
+template <int FA, int FB>
+__device__ __forceinline__ void tc_convert_row_tile(const TcArgs &a, uint8_t *A, const uint8_t *raw_row, int R, int rl,
+                                                    int ks, int lane) {
+    int rt;
+    const int si = tc_seg_of(a, R, rt);
+    const TcSeg &sg = a.seg[si];
+    const __half2 dmul = __float2half2_rn(__int_as_float((sg.dexp + 127) << 23));
+    const int fmt = FA == FB ? FA : sg.fmt;
+    const int tk = tile_k(fmt), per = TC_BK / tk, kt0 = ks * per;
+    const int tb = tile_bytes(fmt);
+    for (int i = 0; i < per; ++i) {
+        const uint8_t *src = kt0 + i < sg.n_ktiles ? raw_row + i * tb : nullptr;
+        if (fmt == FA) tc_convert_tile<FA>(A, src, rl, i * tk, lane, dmul);
+        else tc_convert_tile<FB>(A, src, rl, i * tk, lane, dmul);
+    }
+}
+
+// --------------------------------------------------------------------------------------------------- the kernel
+template <int FA, int FB, class Epi>
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ TcArgs a,
+                                                          const __grid_constant__ CUtensorMap xmap, Epi epi) {
+    extern __shared__ uint8_t smem_raw[];
+    // operand tiles need 1024-byte aligned shared-memory addresses (the swizzle reads address bits 7-9)
+    uint8_t *smem = smem_raw + ((1024u - (tc::smem_addr(smem_raw) & 1023u)) & 1023u);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = a.stages;
+    const uint32_t bars = tc::smem_addr(smem + a.bar_off);
+    // barrier slots: full[S], conv[S], empty[S], acc_full[2], acc_empty[2]; then the TMEM address
+    auto FULL = [&](int s) { return bars + 8u * s; };
+    auto CONV = [&](int s) { return bars + 8u * (S + s); };
+    auto EMPTY = [&](int s) { return bars + 8u * (2 * S + s); };
+    auto ACCF = [&](int b) { return bars + 8u * (3 * S + b); };
+    auto ACCE = [&](int b) { return bars + 8u * (3 * S + 2 + b); };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + a.bar_off + 8 * (3 * S + 4));
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            tc::mbar_init(FULL(s), 1);
+            tc::mbar_init(CONV(s), TC_CONV_WARPS);
+            tc::mbar_init(EMPTY(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(ACCF(b), 1);
+            tc::mbar_init(ACCE(b), 4);
+        }
+        tc::mbar_fence_init();
+    }
+    if (warp == 1) tc::tmem_alloc(tc::smem_addr(tmem_slot), TC_TMEM_COLS);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int n_work = a.m_tiles * a.n_tiles;
+
+    if (warp == 0) {   // ------------------------------------------------------------------------- producer
+        if (lane == 0) {
+            tc::prefetch_tmap(&xmap);
+            const uint64_t pol = tc::l2_evict_first_policy();
+            int it = 0;
+            bool ok = true;
+            for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
+                const int mt = w / a.n_tiles, nt = w - mt * a.n_tiles;
+                for (int ks = 0; ks < a.kstages; ++ks, ++it) {
+                    const int s = it % S;
+                    if (it >= S && !tc::mbar_wait(EMPTY(s), ((it / S) - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    uint32_t bytes = (uint32_t)a.bn * TC_BK * 2;
+                    const uint8_t *src[8];
+                    uint32_t nb[8];
+                    for (int r = 0; r < 8; ++r) {
+                        const int R = mt * 8 + r;
+                        src[r] = nullptr;
+                        nb[r] = 0;
+                        if (R >= a.rbase[a.n_seg]) continue;
+                        int rt;
+                        const int si = tc_seg_of(a, R, rt);
+                        const TcSeg &sg = a.seg[si];
+                        const int tk = tile_k(sg.fmt), per = TC_BK / tk, kt0 = ks * per;
+                        const int n = min(per, sg.n_ktiles - kt0);
+                        if (n <= 0) continue;
+                        src[r] = sg.tiles + ((size_t)rt * sg.n_ktiles + kt0) * tile_bytes(sg.fmt);
+                        nb[r] = (uint32_t)(n * tile_bytes(sg.fmt));
+                        bytes += nb[r];
+                    }
+                    tc::mbar_expect_tx(FULL(s), bytes);
+                    const uint32_t raw = tc::smem_addr(smem + a.raw_off + s * a.stage_raw);
+                    for (int r = 0; r < 8; ++r)
+                        if (src[r]) tc::bulk_g2s(raw + r * TC_RAW_ROW, src[r], nb[r], FULL(s), pol);
+                    tc::tma_load_2d(tc::smem_addr(smem + a.x_off + s * a.stage_x), &xmap, ks * TC_BK, nt * a.bn,
+                                    FULL(s));
+                }
+            }
+            if (!ok) atomicOr(a.status, 4);
+        }
+    } else if (warp == 1) {   // ------------------------------------------------------------------ MMA issuer
+        const uint32_t idesc = tc::idesc_f16(TC_BM, a.bn);
+        int it = 0, tcount = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x, ++tcount) {
+            const int buf = tcount & 1;
+            if (tcount >= 2 && !tc::mbar_wait(ACCE(buf), ((tcount >> 1) - 1) & 1)) {
+                ok = false;
+                break;
+            }
+            tc::tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)(buf * a.bn);
+            for (int ks = 0; ks < a.kstages; ++ks, ++it) {
+                const int s = it % S;
+                if (!tc::mbar_wait(CONV(s), (it / S) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t sa = tc::smem_addr(smem + a.a_off + s * a.stage_a);
+                    const uint32_t sx = tc::smem_addr(smem + a.x_off + s * a.stage_x);
+#pragma unroll
+                    for (int k16 = 0; k16 < TC_BK / 16; ++k16)
+                        tc::mma_f16(d, tc::sw128_desc(sa + 32 * k16), tc::sw128_desc(sx + 32 * k16), idesc,
+                                    (ks | k16) != 0 ? 1u : 0u);
+                    tc::mma_commit(EMPTY(s));
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (lane == 0) tc::mma_commit(ACCF(buf));
+            __syncwarp();
+        }
+        if (!ok && lane == 0) atomicOr(a.status, 4);
+    } else if (warp < 2 + TC_CONV_WARPS) {   // ---------------------------------------------------- converters
+        const int cw = warp - 2;
+        int it = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
+            const int mt = w / a.n_tiles;
+            for (int ks = 0; ks < a.kstages; ++ks, ++it) {
+                const int s = it % S;
+                if (!tc::mbar_wait(FULL(s), (it / S) & 1)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *A = smem + a.a_off + s * a.stage_a;
+                const uint8_t *raw = smem + a.raw_off + s * a.stage_raw;
+                for (int rl = 2 * cw; rl < 2 * cw + 2; ++rl) {
+                    const int R = mt * 8 + rl;
+                    if (R < a.rbase[a.n_seg]) tc_convert_row_tile<FA, FB>(a, A, raw + rl * TC_RAW_ROW, R, rl, ks, lane);
+                }
+                tc::fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(CONV(s));
+            }
+        }
+        if (!ok && lane == 0) atomicOr(a.status, 4);
+    } else {   // ------------------------------------------------------------------------------------- epilogue
+        const int q = warp & 3;                       // TMEM lane quarter this warp may read
+        const int row = 32 * q + lane;                // weight row inside the CTA tile
+        int tcount = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x, ++tcount) {
+            const int mt = w / a.n_tiles, nt = w - mt * a.n_tiles;
+            const int buf = tcount & 1;
+            if (!tc::mbar_wait(ACCF(buf), (tcount >> 1) & 1)) {
+                ok = false;
+                break;
+            }
+            tc::tc_fence_after();
+            const int R = mt * 8 + (row >> 4), tr = row & 15;
+            const bool live = R < a.rbase[a.n_seg] && tr < 8;
+            int rt = 0, si = 0;
+            if (R < a.rbase[a.n_seg]) si = tc_seg_of(a, R, rt);
+            const float ws = a.seg[si].wscale;
+            for (int c0 = 0; c0 < a.bn; c0 += 16) {
+                uint32_t v[16];
+                tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * a.bn + c0), v);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float y = __uint_as_float(v[j]);
+                    const float yp = __shfl_xor_sync(0xffffffffu, y, 8);
+                    const int tok = nt * a.bn + c0 + j;
+                    if (live && tok < a.n_tok) {
+                        const float sc = __ldg(a.xscale + tok) * ws;
+                        epi(si + a.seg_base, rt, tr, tok, y * sc, yp * sc);
+                    }
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(ACCE(buf));
+        }
+        if (!ok && lane == 0) atomicOr(a.status, 4);
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, TC_TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ host launch
+// One GEMM launch: the kernel arguments, the activation tensor map and the weight-format pair of the kernel.
+struct TcLaunch {
+    TcArgs a;
+    CUtensorMap xmap;
+    int fa, fb;
+    int grid;
+    size_t smem;
+};
+
+// Fill `L` for the stacked matrices mats[0..n) (all of one K) against n_tok fp16 activation rows x16 (row stride
+// ldx elements, ldx >= K, 16-byte aligned rows).  Returns cudaErrorNotSupported when a matrix is not in a
+// tensor-core format (F32 tiles) or the formats do not form one kernel's pair (the caller then splits by matrix).
+cudaError_t tc_setup(TcLaunch &L, const MatW *const *mats, int n, const __half *x16, int ldx, const float *xscale,
+                     int n_tok, int *status, int n_sm);
+
+template <int FA, int FB, class Epi>
+cudaError_t tc_launch_t(const TcLaunch &L, const Epi &epi, cudaStream_t st) {
+    static bool attr_set = false;   // large dynamic shared memory: set once per instantiation (outside capture)
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<FA, FB, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    k_gemm_tc<FA, FB, Epi><<<L.grid, TC_THREADS, L.smem, st>>>(L.a, L.xmap, epi);
+    return cudaGetLastError();
+}
+
+template <class Epi>
+cudaError_t tc_launch(const TcLaunch &L, const Epi &epi, cudaStream_t st) {
+    if (L.fa == FMT_Q8 && L.fb == FMT_Q8) return tc_launch_t<FMT_Q8, FMT_Q8>(L, epi, st);
+    if (L.fa == FMT_Q4 && L.fb == FMT_Q8) return tc_launch_t<FMT_Q4, FMT_Q8>(L, epi, st);
+    if (L.fa == FMT_Q4 && L.fb == FMT_Q4) return tc_launch_t<FMT_Q4, FMT_Q4>(L, epi, st);
+    if (L.fa == FMT_BF16 && L.fb == FMT_BF16) return tc_launch_t<FMT_BF16, FMT_BF16>(L, epi, st);
+    if (L.fa == FMT_F16 && L.fb == FMT_F16) return tc_launch_t<FMT_F16, FMT_F16>(L, epi, st);
+    return cudaErrorNotSupported;
+}
+
+// Stacked matrices through the tensor-core GEMM: one launch when the formats form a kernel pair, else one launch
+// per matrix (the epilogue still receives the matrix index as its segment).
+template <class Epi>
+cudaError_t tc_gemm(const MatW *const *mats, int n, const __half *x16, int ldx, const float *xscale, int n_tok,
+                    int *status, int n_sm, const Epi &epi, cudaStream_t st) {
+    TcLaunch L;
+    cudaError_t e = tc_setup(L, mats, n, x16, ldx, xscale, n_tok, status, n_sm);
+    if (e == cudaSuccess) return tc_launch(L, epi, st);
+    if (e != cudaErrorNotSupported || n == 1) return e;
+    for (int i = 0; i < n; ++i) {
+        e = tc_setup(L, mats + i, 1, x16, ldx, xscale, n_tok, status, n_sm);
+        if (e != cudaSuccess) return e;
+        L.a.seg_base = i;
+        e = tc_launch(L, epi, st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+// ------------------------------------------------------------------------------------------ activation operand
+// Row r of x (fp32, stride ld_x; RMSNorm with gain norm_w when it is non-null) -> fp16 row of out (stride ldo,
+// zero-padded to ldo) scaled by a power of two that puts the row's largest |value| into (2^13, 2^14]; xscale[r]
+// receives the multiplier that undoes it.  One CTA per row.
+__global__ void k_tc_prep(const float *x, int64_t ld_x, int K, const float *norm_w, float eps, __half *out, int ldo,
+                          float *xscale);
+// rows 0..n-1 of x through k_tc_prep
+cudaError_t tc_prep(const float *x, int64_t ld_x, int n, int K, const float *norm_w, float eps, __half *out, int ldo,
+                    float *xscale, cudaStream_t st);
+
+}  // namespace v3g

@@ -1,5 +1,6 @@
 // Load-time weight re-tiling (VLT3 payload -> fragment-ordered 16-row tiles, layout in v3g.cuh), the inverse
 // dequantizer used by the bit-exact tests, and the GEMV launch planner.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 
@@ -48,13 +49,17 @@ __device__ __forceinline__ uint32_t f16_bits_rn(float v) { return __half_as_usho
 __device__ __forceinline__ float f16_bits_to_f(uint32_t b) { return __half2float(__ushort_as_half((uint16_t)b)); }
 __device__ __forceinline__ float bf16_bits_to_f(uint32_t b) { return __uint_as_float(b << 16); }
 
-// largest |w| of a BF16 / F32 payload as order-preserving bits (non-negative floats compare as integers)
+// largest |w| of a BF16 / F32 payload (n values), or largest |d| of a Q8_0 / Q4_0 payload's fp16 block scales (n
+// blocks), as order-preserving bits (non-negative floats compare as integers)
 __global__ void absmax_kernel(const uint8_t *src, int fmt, int64_t n, unsigned int *out) {
     float mx = 0.f;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         float v;
         if (fmt == FMT_BF16) v = bf16_bits_to_f((uint32_t)(src[2 * i] | (src[2 * i + 1] << 8)));
-        else memcpy(&v, src + 4 * i, 4);
+        else if (fmt == FMT_Q8 || fmt == FMT_Q4) {
+            const uint8_t *b = src + i * (fmt == FMT_Q8 ? 34 : 18);
+            v = f16_bits_to_f((uint32_t)(b[0] | (b[1] << 8)));
+        } else memcpy(&v, src + 4 * i, 4);
         mx = fmaxf(mx, fabsf(v));
     }
     mx = warp_max(mx);
@@ -210,6 +215,27 @@ int repack_matrix(MatW &w, const uint8_t *dev_src0, const uint8_t *dev_src1, int
             const int sh = 15 - ex;
             a.up = std::ldexp(1.f, sh);
             w.wscale = std::ldexp(1.f, -sh);
+        }
+    }
+    w.dexp = 0;
+    if (fmt == FMT_Q8 || fmt == FMT_Q4) {   // tensor-core path: block scales times 2^dexp, max |q d| 2^dexp ~ 2^13
+        unsigned int *d_mx = nullptr, mx = 0;
+        if (cudaMallocAsync(&d_mx, 4, st) != cudaSuccess) return -1;
+        cudaMemsetAsync(d_mx, 0, 4, st);
+        const int64_t nb = (int64_t)src_rows * cols / 32;
+        absmax_kernel<<<256, 256, 0, st>>>(dev_src0, fmt, nb, d_mx);
+        if (dev_src1) absmax_kernel<<<256, 256, 0, st>>>(dev_src1, fmt, nb, d_mx);
+        cudaMemcpyAsync(&mx, d_mx, 4, cudaMemcpyDeviceToHost, st);
+        cudaFreeAsync(d_mx, st);
+        if (cudaStreamSynchronize(st) != cudaSuccess) return -1;
+        float fm;
+        memcpy(&fm, &mx, 4);
+        fm *= fmt == FMT_Q8 ? 127.f : 8.f;
+        if (fm > 0.f && std::isfinite(fm)) {
+            int ex;
+            std::frexp(fm, &ex);                 // largest |value| in [2^(ex-1), 2^ex)
+            // 2^dexp is applied to fp16 block scales by an fp16 multiply: keep it inside fp16's normal range
+            w.dexp = std::max(-14, std::min(15, 14 - ex));
         }
     }
     const int64_t n = (int64_t)a.n_rtiles * a.n_ktiles * 32;

@@ -241,6 +241,18 @@ class VAULTv3ForCausalLM:
         _lib.check(_lib.lib().v3g_dequant(self._h, tensor_id, C.c_void_p(out.data_ptr()), _stream()), "v3g_dequant")
         return out
 
+    def gemm(self, tensor_id: int, x: torch.Tensor, rows: int) -> torch.Tensor:
+        """y [n_tok, rows] = x [n_tok, K] @ W^T on the tensor-core GEMM (the prefill / batched-decode kernel)."""
+        x = x.to(device=self.device, dtype=torch.float32).contiguous()
+        L = _lib.lib()
+        n = x.shape[0]
+        nbytes = int(L.v3g_gemm_work_size(self._h, tensor_id, n))
+        work = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        y = torch.empty(n, rows, dtype=torch.float32, device=self.device)
+        _lib.check(L.v3g_gemm(self._h, tensor_id, C.c_void_p(x.data_ptr()), n, C.c_void_p(y.data_ptr()),
+                              C.c_void_p(work.data_ptr()), nbytes, _stream()), "v3g_gemm")
+        return y
+
     def gemv(self, tensor_id: int, x: torch.Tensor, rows: int) -> torch.Tensor:
         x = x.to(device=self.device, dtype=torch.float32).contiguous()
         B = x.shape[0]
