@@ -64,7 +64,9 @@ enum {
                                      runs those only at batch 1, src/vault_v3_model.py:1944,2222) */
     V3G_STATE_NO_AUTOPIN = 2,     /* keep n_pin = n_sink (runtime/vault3_host.c --no-autopin) */
     V3G_STATE_NO_GRAPHS = 4,      /* launch kernels directly instead of replaying captured CUDA graphs */
-    V3G_STATE_NO_PERSISTENT = 8   /* run a step as one kernel per layer phase instead of the persistent kernel */
+    V3G_STATE_NO_PERSISTENT = 8,  /* run a step as one kernel per layer phase instead of the persistent kernel */
+    V3G_STATE_TOKEN_PREFILL = 16  /* v3g_prefill streams the prompt one decode step per token instead of the chunked
+                                     tensor-core prefill */
 };
 
 typedef struct v3g_model v3g_model;
@@ -116,7 +118,10 @@ V3G_API int v3g_step(v3g_state *s, const int32_t *dev_tokens, float *dev_logits,
  * copies in, steps, copies out and synchronizes `stream`.  The v3_step calling convention for C callers. */
 V3G_API int v3g_step_host(v3g_state *s, const uint32_t *tokens, float *logits, uint32_t *next, void *stream);
 /* Stream n_tokens ids per sequence (device int32, row b at dev_ids + b * ld) through the state, computing the
- * lm head only for the last one (src/vault_v3_model.py:2163 prefill). */
+ * lm head only for the last one (src/vault_v3_model.py:2163 prefill; the chunk-recurrent forward :1938-2116).
+ * The prompt runs in window-aligned pieces (each layer's projections as tensor-core GEMMs over all of a piece's
+ * tokens, one block-window attention launch) unless V3G_STATE_TOKEN_PREFILL is set or the model / state needs the
+ * per-token path (F32 weight matrices, segment memory). */
 V3G_API int v3g_prefill(v3g_state *s, const int32_t *dev_ids, uint32_t n_tokens, uint64_t ld, float *dev_logits,
                 int32_t *dev_next, void *stream);
 /* Greedy decode on the device: feeds dev_first [batch], then each step's argmax, for n_steps steps, writing the

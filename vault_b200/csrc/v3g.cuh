@@ -285,4 +285,35 @@ __host__ __device__ __forceinline__ bool map_tile_row(int rowmap, int head_dim, 
     return row < src_rows;
 }
 
+// ChatML system-prompt auto-pin state machine for one token (src/vault_v3_model.py:2224-2252)
+__device__ inline void auto_pin_update(const ModelDev &m, SeqCtl &q, int64_t pos, int tid) {
+    if (q.pin_locked || !q.auto_pin) return;
+    const int limit = min(min(m.max_sink, m.W), m.sink_cap);
+    if (pos == 0) {
+        if (tid == m.im_start_id && limit >= 2) q.saw_im_start = 1;
+        else q.pin_locked = 1;
+    } else if (pos == 1 && q.saw_im_start) {
+        if (tid != m.system_id) {
+            q.saw_im_start = 0;
+            q.pin_locked = 1;
+        }
+    } else if (q.saw_im_start && pos < limit) {
+        if (q.awaiting_sys_nl) {
+            const int cand = (tid == m.newline_id) ? (int)pos + 1 : (int)pos;
+            q.n_pin = max(q.n_pin, cand);
+            q.pin_locked = 1;
+            q.awaiting_sys_nl = 0;
+        } else if (tid == m.im_end_id) {
+            q.n_pin = max(q.n_pin, (int)pos + 1);
+            if (pos + 1 < limit) q.awaiting_sys_nl = 1;
+            else q.pin_locked = 1;
+        }
+    } else if (pos >= limit) {
+        if (q.saw_im_start && !q.awaiting_sys_nl) q.n_pin = max(q.n_pin, limit);
+        q.pin_locked = 1;
+        q.awaiting_sys_nl = 0;
+    }
+}
+
+
 }  // namespace v3g

@@ -538,6 +538,9 @@ struct Layout {
     uint64_t off_seq, off_step, off_tok_in, off_tok_ring, off_sc_ring, off_seg_ring, off_mem_pos, off_mem_score,
         off_mem_tok, off_mem_seg, off_mem_src, off_ema, off_feat, off_x, off_attn, off_h, off_qc, off_qf, off_part,
         off_cnt, off_logits, off_amax, off_scz, off_bar;
+    // chunked-prefill workspace: pf_cap tokens
+    uint64_t off_pf_x, off_pf_qc, off_pf_qf, off_pf_attn, off_pf_h, off_pf_x16, off_pf_xs;
+    int pf_cap, pf_ldx16;
     uint64_t total;
     int max_splits, seg_cap, feat_dim;
 };
@@ -588,6 +591,17 @@ Layout make_layout(const ModelDev &md, int B, int seg_cap) {
     L.off_amax = take((uint64_t)B * 8);
     L.off_scz = take((uint64_t)B * 2 * std::max(1, md.seg_hidden) * 4);
     L.off_bar = take(64);
+    // chunked prefill: a piece holds at most min(2048, batch x W) tokens (all sequences together)
+    L.pf_cap = (int)std::min<int64_t>(2048, (int64_t)B * md.W);
+    const uint64_t T = (uint64_t)L.pf_cap, HD = (uint64_t)md.H * md.D;
+    L.pf_ldx16 = (int)((std::max<uint64_t>(std::max<uint64_t>(md.d, HD), md.F) + 63) / 64 * 64);
+    L.off_pf_x = take(T * md.d * 4);
+    L.off_pf_qc = take(T * HD * 4);
+    L.off_pf_qf = take(T * HD * 4);
+    L.off_pf_attn = take(T * HD * 4);
+    L.off_pf_h = take(T * md.F * 4);
+    L.off_pf_x16 = take(T * L.pf_ldx16 * 2);
+    L.off_pf_xs = take(T * 4);
     L.total = cur;
     return L;
 }
@@ -625,6 +639,7 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
     if (md.seg_n_feat > 0 && md.seg_budget_default == 0 && cap > 0) budget = cap;
     s->seg_budget = batch_mode_ref ? 0 : budget;
     s->use_graphs = (flags & V3G_STATE_NO_GRAPHS) ? 0 : 1;
+    s->chunked_prefill = (flags & V3G_STATE_TOKEN_PREFILL) ? 0 : 1;
     StateDev &sd = s->host;
     memset(&sd, 0, sizeof(sd));
     uint8_t *A = s->arena;
@@ -660,6 +675,15 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
     sd.amax = reinterpret_cast<unsigned long long *>(A + L.off_amax);
     sd.sc_z = reinterpret_cast<float *>(A + L.off_scz);
     sd.bar = reinterpret_cast<unsigned int *>(A + L.off_bar);
+    s->pf.cap = L.pf_cap;
+    s->pf.x = reinterpret_cast<float *>(A + L.off_pf_x);
+    s->pf.qc = reinterpret_cast<float *>(A + L.off_pf_qc);
+    s->pf.qf = reinterpret_cast<float *>(A + L.off_pf_qf);
+    s->pf.attn = reinterpret_cast<float *>(A + L.off_pf_attn);
+    s->pf.h = reinterpret_cast<float *>(A + L.off_pf_h);
+    s->pf.x16 = reinterpret_cast<__half *>(A + L.off_pf_x16);
+    s->pf.ldx16 = L.pf_ldx16;
+    s->pf.xscale = reinterpret_cast<float *>(A + L.off_pf_xs);
     if (cudaSetDevice(m->device) != cudaSuccess || cudaMalloc(&s->dev, sizeof(StateDev)) != cudaSuccess ||
         cudaMemcpy(s->dev, &sd, sizeof(StateDev), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaStreamCreateWithFlags(&s->cap_stream, cudaStreamNonBlocking) != cudaSuccess) {
@@ -823,6 +847,23 @@ extern "C" int v3g_prefill(v3g_state *s, const int32_t *dev_ids, uint32_t n, uin
                            int32_t *dev_next, void *stream) {
     if (!s || !dev_ids || n == 0) return fail(V3G_E_ARG, "invalid prefill arguments");
     cudaStream_t st = (cudaStream_t)stream;
+    const ModelDev &md = s->m->host;
+    if (s->chunked_prefill && piece_supported(s->m, s)) {
+        // window-aligned pieces of at most pf_cap tokens over all sequences
+        const int per_piece = std::max(1, s->pf.cap / s->B);
+        uint32_t done = 0;
+        while (done < n) {
+            const uint64_t c = s->pos % md.W;
+            const uint32_t take = (uint32_t)std::min<uint64_t>(std::min<uint64_t>(n - done, md.W - c), per_piece);
+            CUDA_TRY(launch_piece(s->m, s, dev_ids, (int64_t)ld, done, (int)take, (int64_t)s->pos, done + take == n, st));
+            s->pos += take;
+            done += take;
+        }
+        if (dev_logits)
+            CUDA_TRY(cudaMemcpyAsync(dev_logits, s->host.logits, (size_t)s->B * md.vocab * 4, cudaMemcpyDeviceToDevice, st));
+        if (dev_next) CUDA_TRY(cudaMemcpyAsync(dev_next, s->host.tok_in, (size_t)s->B * 4, cudaMemcpyDeviceToDevice, st));
+        return V3G_OK;
+    }
     int rc = set_step_io(s, dev_ids, (int64_t)ld, nullptr, 0, st);
     if (rc != V3G_OK) return rc;
     for (uint32_t i = 0; i < n; ++i)
@@ -830,7 +871,6 @@ extern "C" int v3g_prefill(v3g_state *s, const int32_t *dev_ids, uint32_t n, uin
     int rc2 = set_step_io(s, nullptr, 0, nullptr, 0, st);
     if (rc != V3G_OK) return rc;
     if (rc2 != V3G_OK) return rc2;
-    const ModelDev &md = s->m->host;
     if (dev_logits)
         CUDA_TRY(cudaMemcpyAsync(dev_logits, s->host.logits, (size_t)s->B * md.vocab * 4, cudaMemcpyDeviceToDevice, st));
     if (dev_next) CUDA_TRY(cudaMemcpyAsync(dev_next, s->host.tok_in, (size_t)s->B * 4, cudaMemcpyDeviceToDevice, st));

@@ -89,6 +89,11 @@ cudaError_t launch_attention(const v3g_model *m, v3g_state *s, int layer, bool p
     }
 }
 
+cudaError_t launch_argmax_only(const v3g_model *m, v3g_state *s, cudaStream_t st) {
+    return launch_k(false, k_argmax_partial, dim3(32, s->B), dim3(256), 0, st, (const ModelDev *)m->dev,
+                    (const StateDev *)s->dev);
+}
+
 cudaError_t launch_argmax_finish(const v3g_model *m, v3g_state *s, bool want_lm, bool pdl, cudaStream_t st) {
     cudaError_t e = cudaSuccess;
     if (want_lm) e = launch_k(pdl, k_argmax_partial, dim3(32, s->B), dim3(256), 0, st, (const ModelDev *)m->dev,

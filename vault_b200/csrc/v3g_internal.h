@@ -1,5 +1,6 @@
 // Host-side structures and cross-file entry points of the engine (not part of the public C ABI).
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -22,6 +23,19 @@ struct v3g_model {
     uint32_t file_seg_budget = 0;
     std::vector<std::pair<uint32_t, v3g::MatW *>> tensor_index;  // tensor id -> matrix (tests / sweeps)
     std::string last_error;
+};
+
+// chunked-prefill workspace inside the state arena: up to `cap` tokens (all sequences of a piece together)
+struct PfBuf {
+    int cap = 0;
+    float *x = nullptr;      // [cap][d] residual stream of the piece's tokens
+    float *qc = nullptr;     // [cap][H][D] queries rotated at their chunk position c
+    float *qf = nullptr;     // [cap][H][D] queries rotated at W + c
+    float *attn = nullptr;   // [cap][H D] attention outputs
+    float *h = nullptr;      // [cap][F] SwiGLU activations
+    __half *x16 = nullptr;   // [cap][ldx16] fp16 GEMM operand
+    int ldx16 = 0;
+    float *xscale = nullptr; // [cap] per-token operand scale
 };
 
 struct v3g_state {
@@ -50,6 +64,8 @@ struct v3g_state {
     int mk_ph_off = 0, mk_lite_off = 0, mk_part_off = 0, mk_misc_off = 0, mk_nw_off = 0, mk_ring_off = 0,
         mk_bar_off = 0;
     size_t mk_smem = 0;
+    PfBuf pf;
+    int chunked_prefill = 1;         // v3g_prefill runs window-aligned pieces through the tensor-core GEMMs
     std::string last_error;
 };
 
@@ -74,4 +90,14 @@ cudaError_t launch_attention(const v3g_model *m, v3g_state *s, int layer, bool p
 cudaError_t launch_argmax_finish(const v3g_model *m, v3g_state *s, bool want_lm, bool pdl, cudaStream_t st);
 cudaError_t launch_gemv_mapped(const v3g_model *m, const MatW &w, const float *x, int B, float *y, cudaStream_t st);
 cudaError_t launch_gemv_store(const v3g_model *m, const MatW &w, const float *x, int B, float *y, cudaStream_t st);
+// chunk-boundary kernels of a step at a window boundary (auto-pin of the boundary token, segment eviction, prefix
+// re-rotation); the step's own kernels follow
+cudaError_t launch_boundary(const v3g_model *m, v3g_state *s, cudaStream_t st);
+// final RMSNorm + tied lm head of B rows (row b at x + b * x_ld) into the state's logits, and their argmax keys
+cudaError_t launch_lm_head(const v3g_model *m, v3g_state *s, const float *x, int x_ld, cudaStream_t st);
+cudaError_t launch_argmax_only(const v3g_model *m, v3g_state *s, cudaStream_t st);
+// chunked prefill (v3g_prefill.cu)
+bool piece_supported(const v3g_model *m, const v3g_state *s);
+cudaError_t launch_piece(const v3g_model *m, v3g_state *s, const int32_t *dev_ids, int64_t ld, int64_t i0, int n,
+                         int64_t p0, bool want_lm, cudaStream_t st);
 }  // namespace v3g

@@ -1,0 +1,450 @@
+// Chunked prefill: a piece of up to one window chunk of prompt tokens per sequence goes through every layer as
+// tensor-core GEMMs (v3g_gemm.cuh) and one block-window attention kernel, instead of one decode step per token.
+//
+// Reference semantics: VAULTv3ForCausalLM._forward_chunk_recurrent (src/vault_v3_model.py:1938-2116) for batch 1
+// and the batched sliding-window path (block_sliding_attention, :812-863, through prefill :2163-2212) for batch > 1:
+// a token at chunk position c attends to [pinned sinks | segment bank | previous chunk] (all tokens of the chunk
+// see the same prefix) and causally to the current chunk's positions 0..c.  A piece never crosses a window
+// boundary, so the chunk-boundary work (auto-pin of the boundary token, segment eviction and merge, prefix
+// re-rotation) runs before it exactly as in a decode step, and every token of a piece shares one key prefix.
+// Keys are stored rotated at their chunk position and queries rotated twice (at c and at W + c) -- the relative
+// positions of the reference's re-based RoPE (see v3g_step.cu).
+#include <math.h>
+
+#include <string>
+
+#include "../../include/vault_b200.h"
+#include "v3g_attn.cuh"
+#include "v3g_gemm.cuh"
+#include "v3g_internal.h"
+
+namespace v3g {
+
+// ------------------------------------------------------------------------------------------ per-piece control
+// token bookkeeping of a piece (the sequential part of src/vault_v3_model.py:2224-2268 / :1952-2022 for every
+// token), then the embedding rows of all its tokens.  pin_first = 0 when a boundary piece's first token was
+// already auto-pinned before the eviction (k_pin).
+__global__ void __launch_bounds__(256) k_piece_begin(const ModelDev *mp, const StateDev *sp, const int32_t *ids,
+                                                     int64_t ld, int64_t i0, int n, int64_t p0, int pin_first,
+                                                     float *X) {
+    const ModelDev &m = *mp;
+    const StateDev &s = *sp;
+    const int b = blockIdx.x;
+    extern __shared__ int s_tok[];   // [n]
+    const int W = m.W;
+    if (threadIdx.x == 0) {
+        SeqCtl &q = s.seq[b];
+        const bool seg = q.seg_on && q.seg_budget > 0;
+        const int t2 = max(m.seg_min, (m.seg_max * 2) / 3);
+        const int t3 = max(m.seg_min, m.seg_max > 8 ? m.seg_max - 8 : m.seg_min);
+        for (int j = 0; j < n; ++j) {
+            const int64_t pos = p0 + j;
+            const int c = (int)(pos % W), par = (int)((pos / W) & 1);
+            int tok = ids[(int64_t)b * ld + i0 + j];
+            if (tok < 0 || tok >= m.vocab) tok = m.pad_id;   // runtime/vault3.c:2041
+            if (j > 0 || pin_first) auto_pin_update(m, q, pos, tok);
+            if (c == 0) {
+                q.cur_seg_id = 0;
+                q.seg_len = 0;
+            }
+            s.tok_ring[((size_t)b * 2 + par) * W + c] = tok;
+            if (seg) {
+                const int tr = m.tier[tok];
+                s.seg_ring[((size_t)b * 2 + par) * W + c] = q.cur_seg_id;
+                q.seg_len += 1;
+                const bool brk = (tr == 1 && q.seg_len >= m.seg_min) || (tr == 2 && q.seg_len >= t2) ||
+                                 (tr == 3 && q.seg_len >= t3);
+                if (c == W - 1 || brk || q.seg_len >= m.seg_max) {
+                    q.cur_seg_id += 1;
+                    q.seg_len = 0;
+                }
+                if (pos >= 2 * W && q.mem_cnt > 0 && q.n_uniq_segs > 2) {   // resonance trigger (see k_begin)
+                    const int hi = W + c;
+                    for (int p = hi; p >= max(0, hi - 37); --p) {
+                        const int tk = p < W ? s.tok_ring[((size_t)b * 2 + (par ^ 1)) * W + p]
+                                             : s.tok_ring[((size_t)b * 2 + par) * W + (p - W)];
+                        if (tk == m.im_end_id) {
+                            if (p > 0 && pos - (hi - p) >= q.n_pin) atomicOr(&s.step->status, STATUS_RESONANCE);
+                            break;
+                        }
+                    }
+                }
+            }
+            s_tok[j] = tok;
+        }
+        s.amax[b] = 0ull;
+    }
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < (int64_t)n * m.d; i += blockDim.x) {
+        const int j = (int)(i / m.d), k = (int)(i - (int64_t)j * m.d);
+        X[((int64_t)b * n + j) * m.d + k] = tile_value(m.embed.tiles, m.embed.fmt, m.embed.n_ktiles, m.embed.wscale,
+                                                       s_tok[j], k);
+    }
+}
+
+// end of a piece: position, prefill id cursor and (with the lm head) each sequence's greedy next token
+__global__ void k_piece_finish(const StateDev *sp, int n, int want_lm) {
+    const StateDev &s = *sp;
+    StepCtl &sc = *s.step;
+    for (int b = threadIdx.x; b < s.B && want_lm; b += blockDim.x) {
+        const unsigned long long key = __ldcg(&s.amax[b]);
+        s.tok_in[b] = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu)) : 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        sc.pos += n;
+        if (sc.ids) sc.ids_idx += n;
+    }
+}
+
+// ------------------------------------------------------------------------------------------ GEMM epilogues
+// Token t of a piece = (sequence t / n, position p0 + t % n).
+struct PieceQKV {   // bias + RoPE + KV / sink writes + both query rotations (the QKV epilogue of v3g_step.cu per token)
+    const ModelDev *m;
+    const StateDev *s;
+    int layer, n;
+    int64_t p0;
+    const float *bq, *bk, *bv;
+    float *qc, *qf;   // [tokens][H][D]
+    __device__ void operator()(int seg, int rt, int g, int tok, float y0, float y1) const {
+        const int D = s->D, W = s->W, hd = D / 2;
+        const int b = tok / n;
+        const int64_t pos = p0 + (tok - b * n);
+        const int c = (int)(pos % W), par = (int)((pos / W) & 1);
+        const int head = rt / (D / TILE_ROWS), j = rt % (D / TILE_ROWS), i = 8 * j + g;
+        const int r0 = head * D + i, r1 = r0 + hd;
+        const float *rc = rope_row(*m, c);
+        const float cs = rc[i], sn = rc[hd + i];
+        const float *bsrc = seg == 0 ? bq : (seg == 1 ? bk : bv);
+        const float a = y0 + bsrc[r0], bb = y1 + bsrc[r1];
+        if (seg == 0) {
+            float *q = qc + ((size_t)tok * s->H + head) * D;
+            q[i] = a * cs - bb * sn;
+            q[i + hd] = bb * cs + a * sn;
+            if (pos >= W) {
+                const float *rf = rope_row(*m, W + c);
+                float *qq = qf + ((size_t)tok * s->H + head) * D;
+                qq[i] = a * rf[i] - bb * rf[hd + i];
+                qq[i + hd] = bb * rf[i] + a * rf[hd + i];
+            }
+        } else if (seg == 1) {
+            kv_t *kr = kvp(*s, layer, b, ring_off(*s, par, 1, head, c));
+            kv_t *ko = kvp(*s, layer, b, ring_off(*s, par, 0, head, c));
+            kr[i] = f2kv(a);
+            kr[i + hd] = f2kv(bb);
+            ko[i] = f2kv(a * cs - bb * sn);
+            ko[i + hd] = f2kv(bb * cs + a * sn);
+            if (pos < s->sink_cap) {
+                kv_t *sk = kvp(*s, layer, b, sink_off(*s, 0, head, (int)pos));
+                sk[i] = f2kv(a);
+                sk[i + hd] = f2kv(bb);
+            }
+        } else {
+            kv_t *vv = kvp(*s, layer, b, ring_off(*s, par, 2, head, c));
+            vv[i] = f2kv(a);
+            vv[i + hd] = f2kv(bb);
+            if (pos < s->sink_cap) {
+                kv_t *sv = kvp(*s, layer, b, sink_off(*s, 2, head, (int)pos));
+                sv[i] = f2kv(a);
+                sv[i + hd] = f2kv(bb);
+            }
+        }
+    }
+};
+
+struct TokResid {   // x[t, row] += y (identity row order)
+    float *x;
+    int ld, rows;
+    __device__ void operator()(int, int rt, int g, int tok, float y0, float y1) const {
+        const int r = TILE_ROWS * rt + g;
+        float *xr = x + (size_t)tok * ld;
+        if (r < rows) xr[r] += y0;
+        if (r + 8 < rows) xr[r + 8] += y1;
+    }
+};
+
+struct TokGateUp {   // h[t, f] = silu(gate_f) * up_f  (src/vault_v3_model.py:1149-1150)
+    float *h;
+    int F;
+    __device__ void operator()(int, int rt, int g, int tok, float gt, float u) const {
+        const int f = 8 * rt + g;
+        if (f < F) h[(size_t)tok * F + f] = gt / (1.0f + expf(-gt)) * u;
+    }
+};
+
+// ------------------------------------------------------------------------------------------ block-window attention
+// One CTA per (16 query tokens, KV head g, sequence b) with one warp per query head of the group: the group's K and V
+// rows are staged once in shared memory (cp.async, double-buffered 64-key tiles) and shared by its query heads
+// (GQA).  Scores and P V run on the tensor cores (mma.sync m16n8k16): queries and probabilities enter as high + low
+// fp16 parts (about 22 significant bits), keys and values are the fp16 cache; online softmax in fp32.  Phase 1
+// scores the prefix (sinks, bank, previous chunk) with the queries rotated at W + c, phase 2 the current chunk's
+// keys 0..c with the queries rotated at c.
+template <int D>
+__global__ void __launch_bounds__(256) k_prefill_attn(const StateDev *sp, int layer, float scale, int n, int64_t p0,
+                                                      const float *Qc, const float *Qf, float *out) {
+    constexpr int KP = D + 8, NS = D / 16, NB = D / 8, TK = 64;
+    extern __shared__ __align__(16) uint8_t smraw[];
+    kv_t *Ks = reinterpret_cast<kv_t *>(smraw);   // [2][TK][KP]
+    kv_t *Vs = Ks + 2 * TK * KP;                  // [2][TK][KP]
+    const StateDev &s = *sp;
+    const int b = blockIdx.z, g = blockIdx.y, j0 = blockIdx.x * 16;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, t = lane & 3;
+    const int H = s.H, grp = H / s.G, h = g * grp + warp;
+    const int W = s.W, c0 = (int)(p0 % W);
+    const KeySpan ks = key_span(s, b, p0);
+    const int nfar = ks.n_sk + ks.n_seg + ks.n_prev;
+    const int jmax = min(n, j0 + 16);
+    const int ncur = c0 + jmax;
+    const int r0 = j0 + gq, r1 = r0 + 8;
+    const int cr0 = c0 + r0, cr1 = c0 + r1;
+    float o[NB][4];
+#pragma unroll
+    for (int i = 0; i < NB; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    uint32_t qh[NS][4], ql[NS][4];
+
+    auto load_q = [&](const float *Q) {
+#pragma unroll
+        for (int st = 0; st < NS; ++st) {
+#pragma unroll
+            for (int reg = 0; reg < 4; ++reg) {
+                const int r = (reg & 1) ? r1 : r0;
+                const int d0 = 16 * st + 2 * t + ((reg & 2) ? 8 : 0);
+                float2 v = make_float2(0.f, 0.f);
+                if (r < n) v = __ldg(reinterpret_cast<const float2 *>(Q + (((size_t)b * n + r) * H + h) * D + d0));
+                const __half2 hv = __floats2half2_rn(v.x, v.y);
+                const float2 back = __half22float2(hv);
+                const __half2 lv = __floats2half2_rn(v.x - back.x, v.y - back.y);
+                qh[st][reg] = *reinterpret_cast<const uint32_t *>(&hv);
+                ql[st][reg] = *reinterpret_cast<const uint32_t *>(&lv);
+            }
+        }
+    };
+    // stage keys [k0, k0 + TK) of the phase (visible-key index base + k) into buffer bufi
+    auto stage = [&](int bufi, int k0, int nkeys, int base) {
+        kv_t *kd = Ks + bufi * TK * KP, *vd = Vs + bufi * TK * KP;
+        for (int c = threadIdx.x; c < TK * (D / 8); c += blockDim.x) {
+            const int kk = c / (D / 8), part = c - kk * (D / 8);
+            if (k0 + kk < nkeys) {
+                bool far;
+                cp_async16(kd + kk * KP + part * 8, kv_row(s, layer, b, g, ks, base + k0 + kk, false, far) + part * 8);
+                cp_async16(vd + kk * KP + part * 8, kv_row(s, layer, b, g, ks, base + k0 + kk, true, far) + part * 8);
+            } else {   // past the keys: zero values (probability 0 must meet a finite value)
+                *reinterpret_cast<uint4 *>(vd + kk * KP + part * 8) = make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4 *>(kd + kk * KP + part * 8) = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    auto run = [&](int nkeys, int base, bool causal) {
+        const int ntiles = (nkeys + TK - 1) / TK;
+        if (ntiles == 0) return;
+        stage(0, 0, nkeys, base);
+        for (int tile = 0; tile < ntiles; ++tile) {
+            const int bi = tile & 1;
+            if (tile + 1 < ntiles) {
+                stage(bi ^ 1, (tile + 1) * TK, nkeys, base);
+                asm volatile("cp.async.wait_group 1;" ::: "memory");
+            } else {
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+            }
+            __syncthreads();
+            const kv_t *kt = Ks + bi * TK * KP, *vt = Vs + bi * TK * KP;
+            float sc[8][4];
+#pragma unroll
+            for (int st8 = 0; st8 < 8; ++st8) {
+                float c[4] = {0.f, 0.f, 0.f, 0.f};
+                const kv_t *krow = kt + (st8 * 8 + gq) * KP + 2 * t;
+#pragma unroll
+                for (int st = 0; st < NS; ++st) {
+                    const uint32_t b0 = ld_h2(krow + 16 * st), b1 = ld_h2(krow + 16 * st + 8);
+                    mma16816(c, qh[st][0], qh[st][1], qh[st][2], qh[st][3], b0, b1);
+                    mma16816(c, ql[st][0], ql[st][1], ql[st][2], ql[st][3], b0, b1);
+                }
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int kidx = tile * TK + st8 * 8 + 2 * t + e;
+                    const bool ok = kidx < nkeys;
+                    sc[st8][e] = (ok && (!causal || kidx <= cr0)) ? c[e] * scale : -INFINITY;
+                    sc[st8][2 + e] = (ok && (!causal || kidx <= cr1)) ? c[2 + e] * scale : -INFINITY;
+                }
+            }
+            // online softmax for rows r0 (elements 0, 1) and r1 (elements 2, 3)
+            float mx0 = m0, mx1 = m1;
+#pragma unroll
+            for (int st8 = 0; st8 < 8; ++st8) {
+                mx0 = fmaxf(mx0, fmaxf(sc[st8][0], sc[st8][1]));
+                mx1 = fmaxf(mx1, fmaxf(sc[st8][2], sc[st8][3]));
+            }
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+            const float al0 = mx0 == -INFINITY ? 1.f : expf(m0 - mx0), al1 = mx1 == -INFINITY ? 1.f : expf(m1 - mx1);
+            m0 = mx0;
+            m1 = mx1;
+            float ps0 = 0.f, ps1 = 0.f;
+            uint32_t ph[4][4], pl[4][4];   // P as A fragments of the 4 key steps of 16, high and low parts
+#pragma unroll
+            for (int st8 = 0; st8 < 8; ++st8) {
+                const float p00 = sc[st8][0] == -INFINITY ? 0.f : expf(sc[st8][0] - mx0);
+                const float p01 = sc[st8][1] == -INFINITY ? 0.f : expf(sc[st8][1] - mx0);
+                const float p10 = sc[st8][2] == -INFINITY ? 0.f : expf(sc[st8][2] - mx1);
+                const float p11 = sc[st8][3] == -INFINITY ? 0.f : expf(sc[st8][3] - mx1);
+                ps0 += p00 + p01;
+                ps1 += p10 + p11;
+                const __half2 h0 = __floats2half2_rn(p00, p01), h1 = __floats2half2_rn(p10, p11);
+                const float2 b0 = __half22float2(h0), b1 = __half22float2(h1);
+                const __half2 lo0 = __floats2half2_rn(p00 - b0.x, p01 - b0.y), lo1 = __floats2half2_rn(p10 - b1.x, p11 - b1.y);
+                const int kk = st8 >> 1, hi8 = st8 & 1;   // key step, second half of its 16 keys
+                ph[kk][0 + 2 * hi8] = *reinterpret_cast<const uint32_t *>(&h0);
+                ph[kk][1 + 2 * hi8] = *reinterpret_cast<const uint32_t *>(&h1);
+                pl[kk][0 + 2 * hi8] = *reinterpret_cast<const uint32_t *>(&lo0);
+                pl[kk][1 + 2 * hi8] = *reinterpret_cast<const uint32_t *>(&lo1);
+            }
+            ps0 += __shfl_xor_sync(0xffffffffu, ps0, 1);
+            ps0 += __shfl_xor_sync(0xffffffffu, ps0, 2);
+            ps1 += __shfl_xor_sync(0xffffffffu, ps1, 1);
+            ps1 += __shfl_xor_sync(0xffffffffu, ps1, 2);
+            l0 = l0 * al0 + ps0;
+            l1 = l1 * al1 + ps1;
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb) {
+                o[nb][0] *= al0;
+                o[nb][1] *= al0;
+                o[nb][2] *= al1;
+                o[nb][3] *= al1;
+            }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    uint32_t b0, b1;
+                    ldsm_x2_trans(b0, b1, vt + (16 * kk + (lane & 15)) * KP + 8 * nb);
+                    mma16816(o[nb], ph[kk][0], ph[kk][1], ph[kk][2], ph[kk][3], b0, b1);
+                    mma16816(o[nb], pl[kk][0], pl[kk][1], pl[kk][2], pl[kk][3], b0, b1);
+                }
+            }
+            __syncthreads();   // every warp is done with this buffer before it is refilled
+        }
+    };
+    if (nfar > 0) {
+        load_q(Qf);
+        run(nfar, 0, false);
+    }
+    load_q(Qc);
+    run(ncur, nfar, true);
+    const float i0 = 1.f / l0, i1 = 1.f / l1;
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+        const int d0 = 8 * nb + 2 * t;
+        if (r0 < n)
+            *reinterpret_cast<float2 *>(out + (((size_t)b * n + r0) * H + h) * D + d0) = make_float2(o[nb][0] * i0, o[nb][1] * i0);
+        if (r1 < n)
+            *reinterpret_cast<float2 *>(out + (((size_t)b * n + r1) * H + h) * D + d0) = make_float2(o[nb][2] * i1, o[nb][3] * i1);
+    }
+}
+
+template <int D>
+static cudaError_t launch_prefill_attn(const v3g_model *m, v3g_state *s, int layer, int n, int64_t p0,
+                                       cudaStream_t st) {
+    static bool attr = false;
+    const size_t smem = (size_t)4 * 64 * (D + 8) * sizeof(kv_t);
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(k_prefill_attn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    const PfBuf &pf = s->pf;
+    dim3 grid((n + 15) / 16, m->host.G, s->B);
+    k_prefill_attn<D><<<grid, 32 * (m->host.H / m->host.G), smem, st>>>(s->dev, layer, (float)(1.0 / sqrt((double)D)), n, p0,
+                                                                        pf.qc, pf.qf, pf.attn);
+    return cudaGetLastError();
+}
+
+static cudaError_t prefill_attention(const v3g_model *m, v3g_state *s, int layer, int n, int64_t p0, cudaStream_t st) {
+    switch (m->host.D) {
+        case 16: return launch_prefill_attn<16>(m, s, layer, n, p0, st);
+        case 32: return launch_prefill_attn<32>(m, s, layer, n, p0, st);
+        case 64: return launch_prefill_attn<64>(m, s, layer, n, p0, st);
+        case 128: return launch_prefill_attn<128>(m, s, layer, n, p0, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// ------------------------------------------------------------------------------------------ host orchestration
+bool piece_supported(const v3g_model *m, const v3g_state *s) {
+    const ModelDev &md = m->host;
+    if (!s->pf.x || s->pf.cap < 1) return false;
+    if (md.seg_n_feat > 0 && s->seg_budget > 0) return false;   // segment memory: token path (scorer per token)
+    auto ok = [](const MatW &w) { return w.fmt == FMT_Q8 || w.fmt == FMT_Q4 || w.fmt == FMT_BF16 || w.fmt == FMT_F16; };
+    for (int l = 0; l < md.n_layers; ++l) {
+        const LayerW &L = md.layers[l];
+        if (!ok(L.q) || !ok(L.k) || !ok(L.v) || !ok(L.o) || !ok(L.gu) || !ok(L.down)) return false;
+    }
+    return true;
+}
+
+// n tokens per sequence (ids row b at dev_ids + b ld, columns i0 ..), starting at host position p0; the piece stays
+// inside one window chunk.  want_lm: the last token's logits into s.logits and its greedy token into tok_in.
+cudaError_t launch_piece(const v3g_model *m, v3g_state *s, const int32_t *dev_ids, int64_t ld, int64_t i0, int n,
+                         int64_t p0, bool want_lm, cudaStream_t st) {
+    const ModelDev &md = m->host;
+    const StateDev &sd = s->host;
+    const PfBuf &pf = s->pf;
+    const int B = s->B, T = B * n;
+    const bool boundary = p0 > 0 && p0 % md.W == 0;
+    int *status = &sd.step->status;
+    cudaError_t e;
+#define PF_TRY(x)                               \
+    do {                                        \
+        if ((e = (x)) != cudaSuccess) return e; \
+    } while (0)
+    if (boundary) {   // the boundary kernels read each sequence's boundary token from tok_in (k_pin)
+        PF_TRY(cudaMemcpy2DAsync(sd.tok_in, sizeof(int32_t), dev_ids + i0, (size_t)ld * sizeof(int32_t), sizeof(int32_t),
+                                 (size_t)B, cudaMemcpyDeviceToDevice, st));
+        PF_TRY(launch_boundary(m, s, st));
+    }
+    k_piece_begin<<<B, 256, (size_t)n * sizeof(int), st>>>(m->dev, s->dev, dev_ids, ld, i0, n, p0, boundary ? 0 : 1,
+                                                           pf.x);
+    PF_TRY(cudaGetLastError());
+    const int HD = md.H * md.D;
+    for (int l = 0; l < md.n_layers; ++l) {
+        const LayerW &L = md.layers[l];
+        PF_TRY(tc_prep(pf.x, md.d, T, md.d, L.ln1, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
+        {
+            const MatW *mats[3] = {&L.q, &L.k, &L.v};
+            PieceQKV epi{m->dev, s->dev, l, n, p0, L.bq, L.bk, L.bv, pf.qc, pf.qf};
+            PF_TRY(tc_gemm(mats, 3, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st));
+        }
+        PF_TRY(prefill_attention(m, s, l, n, p0, st));
+        PF_TRY(tc_prep(pf.attn, HD, T, HD, nullptr, 0.f, pf.x16, pf.ldx16, pf.xscale, st));
+        {
+            const MatW *mats[1] = {&L.o};
+            TokResid epi{pf.x, md.d, md.d};
+            PF_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st));
+        }
+        PF_TRY(tc_prep(pf.x, md.d, T, md.d, L.ln2, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
+        {
+            const MatW *mats[1] = {&L.gu};
+            TokGateUp epi{pf.h, md.F};
+            PF_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st));
+        }
+        PF_TRY(tc_prep(pf.h, md.F, T, md.F, nullptr, 0.f, pf.x16, pf.ldx16, pf.xscale, st));
+        {
+            const MatW *mats[1] = {&L.down};
+            TokResid epi{pf.x, md.d, md.d};
+            PF_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st));
+        }
+    }
+    if (want_lm) {   // the last token of every sequence: rows (b n + n - 1) of x, stride n d
+        PF_TRY(launch_lm_head(m, s, pf.x + (size_t)(n - 1) * md.d, n * md.d, st));
+        PF_TRY(launch_argmax_only(m, s, st));
+    }
+    k_piece_finish<<<1, 256, 0, st>>>(s->dev, n, want_lm ? 1 : 0);
+    PF_TRY(cudaGetLastError());
+#undef PF_TRY
+    return cudaSuccess;
+}
+
+}  // namespace v3g

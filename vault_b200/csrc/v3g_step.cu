@@ -25,36 +25,6 @@ __device__ __forceinline__ float tile_elem(const MatW &w, int row, int k) {
     return tile_value(w.tiles, w.fmt, w.n_ktiles, w.wscale, row, k);
 }
 
-// ChatML system-prompt auto-pin state machine for one token (src/vault_v3_model.py:2224-2252)
-__device__ void auto_pin_update(const ModelDev &m, SeqCtl &q, int64_t pos, int tid) {
-    if (q.pin_locked || !q.auto_pin) return;
-    const int limit = min(min(m.max_sink, m.W), m.sink_cap);
-    if (pos == 0) {
-        if (tid == m.im_start_id && limit >= 2) q.saw_im_start = 1;
-        else q.pin_locked = 1;
-    } else if (pos == 1 && q.saw_im_start) {
-        if (tid != m.system_id) {
-            q.saw_im_start = 0;
-            q.pin_locked = 1;
-        }
-    } else if (q.saw_im_start && pos < limit) {
-        if (q.awaiting_sys_nl) {
-            const int cand = (tid == m.newline_id) ? (int)pos + 1 : (int)pos;
-            q.n_pin = max(q.n_pin, cand);
-            q.pin_locked = 1;
-            q.awaiting_sys_nl = 0;
-        } else if (tid == m.im_end_id) {
-            q.n_pin = max(q.n_pin, (int)pos + 1);
-            if (pos + 1 < limit) q.awaiting_sys_nl = 1;
-            else q.pin_locked = 1;
-        }
-    } else if (pos >= limit) {
-        if (q.saw_im_start && !q.awaiting_sys_nl) q.n_pin = max(q.n_pin, limit);
-        q.pin_locked = 1;
-        q.awaiting_sys_nl = 0;
-    }
-}
-
 __device__ __forceinline__ int read_token(const ModelDev &m, const StateDev &s, int b) {
     const StepCtl &sc = *s.step;
     int tok = sc.ids ? sc.ids[(int64_t)b * sc.ids_ld + sc.ids_idx] : s.tok_in[b];
@@ -997,6 +967,35 @@ cudaError_t launch_mega(const v3g_model *m, v3g_state *s, bool want_lm, cudaStre
     return cudaLaunchKernelEx(&cfg, reinterpret_cast<MkKernel>(s->mk_fn), mdv, sdv, phases, n, scale, mc);
 }
 
+// The boundary kernels check pos >= 2W on the device, so one captured graph serves every rollover.
+cudaError_t launch_boundary(const v3g_model *m, v3g_state *s, cudaStream_t st) {
+    const ModelDev &md = m->host;
+    const StateDev &sd = s->host;
+    const ModelDev *mdv = m->dev;
+    const StateDev *sdv = s->dev;
+    const int B = s->B;
+    const bool any_seg = md.seg_n_feat > 0 && s->seg_budget > 0;
+    const bool pdl = s->use_pdl != 0;
+    cudaError_t e = launch_k(false, k_pin, dim3(B), dim3(32), 0, st, mdv, sdv);
+    if (e != cudaSuccess) return e;
+    if (any_seg) {
+        const size_t smem = (size_t)(2 * md.W + 3 * (sd.seg_cap + md.W)) * 4;
+        if (smem > (size_t)GEMV_MAX_SMEM) return cudaErrorInvalidValue;
+        if ((e = launch_k(pdl, k_bank_merge, dim3(B), dim3(1024), smem, st, mdv, sdv)) != cudaSuccess) return e;
+        if ((e = launch_k(pdl, k_bank_gather, dim3(16, md.n_layers, B), dim3(256), 0, st, mdv, sdv)) != cudaSuccess)
+            return e;
+    }
+    return launch_k(pdl, k_prefix_rot, dim3(64, md.n_layers, B), dim3(256), 0, st, mdv, sdv);
+}
+
+cudaError_t launch_lm_head(const v3g_model *m, v3g_state *s, const float *x, int x_ld, cudaStream_t st) {
+    const ModelDev &md = m->host;
+    const MatW *mats[1] = {&md.embed};
+    GemvCall a = gemv_args(mats, 1, x, x_ld, md.d, PRO_RMSNORM, md.norm, md.rms_eps);
+    EpiStore epi{s->host.logits, md.vocab, md.vocab};
+    return run_gemv(m, a, epi, s->B, st, false);
+}
+
 // Kernel sequence of one decode step.  Every launch after the first carries programmatic stream serialization:
 // the next kernel's CTAs start streaming their weights while the previous kernel drains (griddep_wait in each
 // kernel orders all state accesses).
@@ -1014,15 +1013,7 @@ cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool wa
         if ((e = (x)) != cudaSuccess) return e; \
     } while (0)
     if (boundary) {
-        // the boundary kernels check pos >= 2W on the device, so one captured graph serves every rollover
-        V3G_TRY(launch_k(false, k_pin, dim3(B), dim3(32), 0, st, mdv, sdv));
-        if (any_seg) {
-            const size_t smem = (size_t)(2 * md.W + 3 * (sd.seg_cap + md.W)) * 4;
-            if (smem > (size_t)GEMV_MAX_SMEM) return cudaErrorInvalidValue;
-            V3G_TRY(launch_k(pdl, k_bank_merge, dim3(B), dim3(1024), smem, st, mdv, sdv));
-            V3G_TRY(launch_k(pdl, k_bank_gather, dim3(16, md.n_layers, B), dim3(256), 0, st, mdv, sdv));
-        }
-        V3G_TRY(launch_k(pdl, k_prefix_rot, dim3(64, md.n_layers, B), dim3(256), 0, st, mdv, sdv));
+        V3G_TRY(launch_boundary(m, s, st));
         V3G_TRY(launch_k(pdl, k_begin<false>, dim3(B), dim3(256), 0, st, mdv, sdv));
     } else {
         V3G_TRY(launch_k(false, k_begin<true>, dim3(B), dim3(256), 0, st, mdv, sdv));

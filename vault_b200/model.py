@@ -32,7 +32,7 @@ class VAULTv3State:
 
     def __init__(self, model: "VAULTv3ForCausalLM", batch: int = 1, seg_budget: Optional[int] = None,
                  per_sequence_memory: bool = False, auto_pin: bool = True, graphs: bool = True,
-                 persistent: bool = True):
+                 persistent: bool = True, chunked_prefill: bool = True):
         self.model = model
         self.batch = int(batch)
         cfg = model.cfg
@@ -47,7 +47,8 @@ class VAULTv3State:
         self.arena = torch.empty(int(size), dtype=torch.uint8, device=model.device)
         flags = (_lib.V3G_STATE_PER_SEQ_MEMORY if per_sequence_memory else 0) | \
                 (0 if auto_pin else _lib.V3G_STATE_NO_AUTOPIN) | (0 if graphs else _lib.V3G_STATE_NO_GRAPHS) | \
-                (0 if persistent else _lib.V3G_STATE_NO_PERSISTENT)
+                (0 if persistent else _lib.V3G_STATE_NO_PERSISTENT) | \
+                (0 if chunked_prefill else _lib.V3G_STATE_TOKEN_PREFILL)
         h = C.c_void_p()
         with torch.cuda.device(model.device):
             _lib.check(L.v3g_state_init(C.byref(h), model._h, C.c_void_p(self.arena.data_ptr()), int(size),
@@ -188,11 +189,12 @@ class VAULTv3ForCausalLM:
 
     @torch.no_grad()
     def prefill(self, input_ids: torch.Tensor, vault_on: bool = False,
-                seg_budget: Optional[int] = None) -> Tuple[torch.Tensor, VAULTv3State]:
-        """Stream a prompt from position 0; returns last-token logits [B, V] and the state."""
+                seg_budget: Optional[int] = None, **state_kw) -> Tuple[torch.Tensor, VAULTv3State]:
+        """Prefill a prompt from position 0 (window-aligned pieces through the tensor-core GEMMs, or token by token
+        with chunked_prefill=False); returns last-token logits [B, V] and the state."""
         _ = vault_on
         B, Lq = input_ids.shape
-        st = self.new_state(B, seg_budget=seg_budget)
+        st = self.new_state(B, seg_budget=seg_budget, **state_kw)
         ids = self._ids(input_ids)
         out = torch.empty(B, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
         _lib.check(_lib.lib().v3g_prefill(st._h, C.c_void_p(ids.data_ptr()), Lq, Lq, C.c_void_p(out.data_ptr()),
