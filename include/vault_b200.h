@@ -64,7 +64,8 @@ enum {
                                      runs those only at batch 1, src/vault_v3_model.py:1944,2222) */
     V3G_STATE_NO_AUTOPIN = 2,     /* keep n_pin = n_sink (runtime/vault3_host.c --no-autopin) */
     V3G_STATE_NO_GRAPHS = 4,      /* launch kernels directly instead of replaying captured CUDA graphs */
-    V3G_STATE_NO_PERSISTENT = 8,  /* run a step as one kernel per layer phase instead of the persistent kernel */
+    V3G_STATE_NO_PERSISTENT = 8,  /* run a step as one GEMV kernel per layer phase (8 batch rows per pass) instead of
+                                     the persistent kernel (batch <= 8) or the tensor-core GEMM step (batch > 8) */
     V3G_STATE_TOKEN_PREFILL = 16  /* v3g_prefill streams the prompt one decode step per token instead of the chunked
                                      tensor-core prefill */
 };

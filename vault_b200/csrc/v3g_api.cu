@@ -691,12 +691,17 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
         delete s;
         return fail(V3G_E_CUDA, "state descriptor setup failed");
     }
+    if (const cudaError_t ea = tc_init_attrs()) {
+        v3g_state_free(s);
+        return fail(V3G_E_CUDA, std::string("tensor-core kernel attributes: ") + cudaGetErrorString(ea));
+    }
     if (!(flags & V3G_STATE_NO_PERSISTENT)) {
         const cudaError_t em = build_mega(m, s);
         if (em != cudaSuccess) {
             v3g_state_free(s);
             return fail(V3G_E_CUDA, std::string("persistent kernel setup: ") + cudaGetErrorString(em));
         }
+        s->use_tc_step = !s->use_mega && (int)batch > GEMV_MB && step_tc_supported(m, s) ? 1 : 0;
     }
     int rc = v3g_state_reset(s, nullptr);
     if (rc != V3G_OK) {

@@ -66,6 +66,7 @@ struct v3g_state {
     size_t mk_smem = 0;
     PfBuf pf;
     int chunked_prefill = 1;         // v3g_prefill runs window-aligned pieces through the tensor-core GEMMs
+    int use_tc_step = 0;             // batch > 8: decode steps run their projections on the tensor-core GEMM
     std::string last_error;
 };
 
@@ -96,6 +97,12 @@ cudaError_t launch_boundary(const v3g_model *m, v3g_state *s, cudaStream_t st);
 // final RMSNorm + tied lm head of B rows (row b at x + b * x_ld) into the state's logits, and their argmax keys
 cudaError_t launch_lm_head(const v3g_model *m, v3g_state *s, const float *x, int x_ld, cudaStream_t st);
 cudaError_t launch_argmax_only(const v3g_model *m, v3g_state *s, cudaStream_t st);
+cudaError_t launch_step_begin(const v3g_model *m, v3g_state *s, bool boundary, cudaStream_t st);
+cudaError_t launch_scorer(const v3g_model *m, v3g_state *s, cudaStream_t st);
+// batched decode step (B > 8) with every projection on the tensor-core GEMM (v3g_prefill.cu)
+cudaError_t launch_step_tc(const v3g_model *m, v3g_state *s, bool boundary, bool want_lm, cudaStream_t st);
+bool step_tc_supported(const v3g_model *m, const v3g_state *s);
+cudaError_t tc_init_attrs();
 // chunked prefill (v3g_prefill.cu)
 bool piece_supported(const v3g_model *m, const v3g_state *s);
 cudaError_t launch_piece(const v3g_model *m, v3g_state *s, const int32_t *dev_ids, int64_t ld, int64_t i0, int n,

@@ -98,7 +98,8 @@ __global__ void k_piece_finish(const StateDev *sp, int n, int want_lm) {
 }
 
 // ------------------------------------------------------------------------------------------ GEMM epilogues
-// Token t of a piece = (sequence t / n, position p0 + t % n).
+// Token t of a piece = (sequence t / n, position p0 + t % n); p0 < 0: the batched decode step (n = 1), whose
+// position is read from the state on the device (so a captured step replays at any position).
 struct PieceQKV {   // bias + RoPE + KV / sink writes + both query rotations (the QKV epilogue of v3g_step.cu per token)
     const ModelDev *m;
     const StateDev *s;
@@ -109,7 +110,7 @@ struct PieceQKV {   // bias + RoPE + KV / sink writes + both query rotations (th
     __device__ void operator()(int seg, int rt, int g, int tok, float y0, float y1) const {
         const int D = s->D, W = s->W, hd = D / 2;
         const int b = tok / n;
-        const int64_t pos = p0 + (tok - b * n);
+        const int64_t pos = (p0 < 0 ? s->step->pos : p0) + (tok - b * n);
         const int c = (int)(pos % W), par = (int)((pos / W) & 1);
         const int head = rt / (D / TILE_ROWS), j = rt % (D / TILE_ROWS), i = 8 * j + g;
         const int r0 = head * D + i, r1 = r0 + hd;
@@ -160,6 +161,18 @@ struct TokResid {   // x[t, row] += y (identity row order)
         float *xr = x + (size_t)tok * ld;
         if (r < rows) xr[r] += y0;
         if (r + 8 < rows) xr[r + 8] += y1;
+    }
+};
+
+struct TokStore {   // y[t, row] = value (identity row order): logits of the batched lm head
+    float *y;
+    int64_t ld;
+    int rows;
+    __device__ void operator()(int, int rt, int g, int tok, float y0, float y1) const {
+        const int r = TILE_ROWS * rt + g;
+        float *yr = y + (size_t)tok * ld;
+        if (r < rows) yr[r] = y0;
+        if (r + 8 < rows) yr[r + 8] = y1;
     }
 };
 
@@ -348,13 +361,7 @@ __global__ void __launch_bounds__(256) k_prefill_attn(const StateDev *sp, int la
 template <int D>
 static cudaError_t launch_prefill_attn(const v3g_model *m, v3g_state *s, int layer, int n, int64_t p0,
                                        cudaStream_t st) {
-    static bool attr = false;
-    const size_t smem = (size_t)4 * 64 * (D + 8) * sizeof(kv_t);
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_prefill_attn<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    const size_t smem = (size_t)4 * 64 * (D + 8) * sizeof(kv_t);   // attribute set by tc_init_attrs
     const PfBuf &pf = s->pf;
     dim3 grid((n + 15) / 16, m->host.G, s->B);
     k_prefill_attn<D><<<grid, 32 * (m->host.H / m->host.G), smem, st>>>(s->dev, layer, (float)(1.0 / sqrt((double)D)), n, p0,
@@ -373,6 +380,34 @@ static cudaError_t prefill_attention(const v3g_model *m, v3g_state *s, int layer
 }
 
 // ------------------------------------------------------------------------------------------ host orchestration
+// Large dynamic shared memory for every tensor-core kernel instantiation this file launches; called at state set-up
+// (never inside a stream capture).
+template <class Epi>
+static cudaError_t tc_attrs_for() {
+    cudaError_t e = cudaSuccess;
+    auto set = [&](const void *f) {
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    };
+    set((const void *)k_gemm_tc<FMT_Q8, FMT_Q8, Epi>);
+    set((const void *)k_gemm_tc<FMT_Q4, FMT_Q8, Epi>);
+    set((const void *)k_gemm_tc<FMT_Q4, FMT_Q4, Epi>);
+    set((const void *)k_gemm_tc<FMT_BF16, FMT_BF16, Epi>);
+    set((const void *)k_gemm_tc<FMT_F16, FMT_F16, Epi>);
+    return e;
+}
+
+cudaError_t tc_init_attrs() {
+    cudaError_t e = tc_attrs_for<PieceQKV>();
+    if (e == cudaSuccess) e = tc_attrs_for<TokResid>();
+    if (e == cudaSuccess) e = tc_attrs_for<TokGateUp>();
+    if (e == cudaSuccess) e = tc_attrs_for<TokStore>();
+    const int D[4] = {16, 32, 64, 128};
+    const void *fn[4] = {(const void *)k_prefill_attn<16>, (const void *)k_prefill_attn<32>,
+                         (const void *)k_prefill_attn<64>, (const void *)k_prefill_attn<128>};
+    for (int i = 0; i < 4 && e == cudaSuccess; ++i)
+        e = cudaFuncSetAttribute(fn[i], cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * 64 * (D[i] + 8) * 2);
+    return e;
+}
 bool piece_supported(const v3g_model *m, const v3g_state *s) {
     const ModelDev &md = m->host;
     if (!s->pf.x || s->pf.cap < 1) return false;
@@ -445,6 +480,78 @@ cudaError_t launch_piece(const v3g_model *m, v3g_state *s, const int32_t *dev_id
     PF_TRY(cudaGetLastError());
 #undef PF_TRY
     return cudaSuccess;
+}
+
+// One decode step of a batch of B > 8 sequences with every projection on the tensor-core GEMM (N = B tokens, so
+// each weight byte is read once per step): the step kernels of v3g_step.cu for the token bookkeeping, chunk
+// boundary, split-KV attention, segment scorer and argmax, the GEMMs for QKV (fused bias / RoPE / KV writes), O,
+// gate/up and down, and the tied lm head.  Positions come from the device state: the sequence can be captured.
+cudaError_t launch_step_tc(const v3g_model *m, v3g_state *s, bool boundary, bool want_lm, cudaStream_t st) {
+    const ModelDev &md = m->host;
+    const StateDev &sd = s->host;
+    const PfBuf &pf = s->pf;
+    const int B = s->B, HD = md.H * md.D;
+    const bool any_seg = md.seg_n_feat > 0 && s->seg_budget > 0;
+    int *status = &sd.step->status;
+    cudaError_t e;
+#define TS_TRY(x)                               \
+    do {                                        \
+        if ((e = (x)) != cudaSuccess) return e; \
+    } while (0)
+    TS_TRY(launch_step_begin(m, s, boundary, st));
+    for (int l = 0; l < md.n_layers; ++l) {
+        const LayerW &L = md.layers[l];
+        for (int fi = 0; fi < md.seg_n_feat && any_seg; ++fi)
+            if (md.seg_layers[fi] == l)   // scorer features: residual stream entering this layer
+                TS_TRY(cudaMemcpy2DAsync(sd.feat + (size_t)fi * md.d, (size_t)sd.feat_dim * 4, sd.x, (size_t)md.d * 4,
+                                         (size_t)md.d * 4, (size_t)B, cudaMemcpyDeviceToDevice, st));
+        TS_TRY(tc_prep(sd.x, md.d, B, md.d, L.ln1, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
+        {
+            const MatW *mats[3] = {&L.q, &L.k, &L.v};
+            PieceQKV epi{m->dev, s->dev, l, 1, -1, L.bq, L.bk, L.bv, sd.q_cur, sd.q_far};
+            TS_TRY(tc_gemm(mats, 3, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st));
+        }
+        TS_TRY(launch_attention(m, s, l, false, st));
+        TS_TRY(tc_prep(sd.attn, HD, B, HD, nullptr, 0.f, pf.x16, pf.ldx16, pf.xscale, st));
+        {
+            const MatW *mats[1] = {&L.o};
+            TokResid epi{sd.x, md.d, md.d};
+            TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st));
+        }
+        TS_TRY(tc_prep(sd.x, md.d, B, md.d, L.ln2, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
+        {
+            const MatW *mats[1] = {&L.gu};
+            TokGateUp epi{sd.hbuf, md.F};
+            TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st));
+        }
+        TS_TRY(tc_prep(sd.hbuf, md.F, B, md.F, nullptr, 0.f, pf.x16, pf.ldx16, pf.xscale, st));
+        {
+            const MatW *mats[1] = {&L.down};
+            TokResid epi{sd.x, md.d, md.d};
+            TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st));
+        }
+    }
+    if (any_seg) TS_TRY(launch_scorer(m, s, st));
+    if (want_lm) {
+        TS_TRY(tc_prep(sd.x, md.d, B, md.d, md.norm, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
+        const MatW *mats[1] = {&md.embed};
+        TokStore epi{sd.logits, md.vocab, md.vocab};
+        TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st));
+    }
+    TS_TRY(launch_argmax_finish(m, s, want_lm, false, st));
+#undef TS_TRY
+    return cudaSuccess;
+}
+
+bool step_tc_supported(const v3g_model *m, const v3g_state *s) {
+    const ModelDev &md = m->host;
+    auto ok = [](const MatW &w) { return w.fmt == FMT_Q8 || w.fmt == FMT_Q4 || w.fmt == FMT_BF16 || w.fmt == FMT_F16; };
+    if (!s->pf.x16 || s->pf.cap < s->B || !ok(md.embed)) return false;
+    for (int l = 0; l < md.n_layers; ++l) {
+        const LayerW &L = md.layers[l];
+        if (!ok(L.q) || !ok(L.k) || !ok(L.v) || !ok(L.o) || !ok(L.gu) || !ok(L.down)) return false;
+    }
+    return true;
 }
 
 }  // namespace v3g

@@ -996,6 +996,28 @@ cudaError_t launch_lm_head(const v3g_model *m, v3g_state *s, const float *x, int
     return run_gemv(m, a, epi, s->B, st, false);
 }
 
+// token bookkeeping, segment ids and embedding of a step (after the chunk-boundary kernels at a window boundary)
+cudaError_t launch_step_begin(const v3g_model *m, v3g_state *s, bool boundary, cudaStream_t st) {
+    const ModelDev *mdv = m->dev;
+    const StateDev *sdv = s->dev;
+    if (boundary) {
+        cudaError_t e = launch_boundary(m, s, st);
+        if (e != cudaSuccess) return e;
+        return launch_k(s->use_pdl != 0, k_begin<false>, dim3(s->B), dim3(256), 0, st, mdv, sdv);
+    }
+    return launch_k(false, k_begin<true>, dim3(s->B), dim3(256), 0, st, mdv, sdv);
+}
+
+// SegmentScorer v2 + habituation + spoof check of the step's token, per sequence
+cudaError_t launch_scorer(const v3g_model *m, v3g_state *s, cudaStream_t st) {
+    const ModelDev &md = m->host;
+    const bool pdl = s->use_pdl != 0;
+    cudaError_t e = launch_k(pdl, k_scorer_fc1, dim3((md.seg_hidden + 7) / 8, s->B), dim3(256), 0, st,
+                             (const ModelDev *)m->dev, (const StateDev *)s->dev);
+    if (e != cudaSuccess) return e;
+    return launch_k(pdl, k_scorer_out, dim3(s->B), dim3(256), 0, st, (const ModelDev *)m->dev, (const StateDev *)s->dev);
+}
+
 // Kernel sequence of one decode step.  Every launch after the first carries programmatic stream serialization:
 // the next kernel's CTAs start streaming their weights while the previous kernel drains (griddep_wait in each
 // kernel orders all state accesses).
@@ -1012,12 +1034,8 @@ cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool wa
     do {                                    \
         if ((e = (x)) != cudaSuccess) return e; \
     } while (0)
-    if (boundary) {
-        V3G_TRY(launch_boundary(m, s, st));
-        V3G_TRY(launch_k(pdl, k_begin<false>, dim3(B), dim3(256), 0, st, mdv, sdv));
-    } else {
-        V3G_TRY(launch_k(false, k_begin<true>, dim3(B), dim3(256), 0, st, mdv, sdv));
-    }
+    if (!s->use_mega && s->use_tc_step) return launch_step_tc(m, s, boundary, want_lm, st);
+    V3G_TRY(launch_step_begin(m, s, boundary, st));
     if (s->use_mega) {   // all layers + lm head in one persistent launch
         V3G_TRY(launch_mega(m, s, want_lm, st));
         if (any_seg) {
@@ -1060,10 +1078,7 @@ cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool wa
             V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
         }
     }
-    if (any_seg) {
-        V3G_TRY(launch_k(pdl, k_scorer_fc1, dim3((md.seg_hidden + 7) / 8, B), dim3(256), 0, st, mdv, sdv));
-        V3G_TRY(launch_k(pdl, k_scorer_out, dim3(B), dim3(256), 0, st, mdv, sdv));
-    }
+    if (any_seg) V3G_TRY(launch_scorer(m, s, st));
     if (want_lm) {
         const MatW *mats[1] = {&md.embed};
         GemvCall a = gemv_args(mats, 1, sd.x, md.d, md.d, PRO_RMSNORM, md.norm, md.rms_eps);
