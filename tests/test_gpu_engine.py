@@ -183,7 +183,10 @@ def test_out_of_range_token_becomes_pad(case_files):
 
 
 @pytest.mark.parametrize("name,seg_budget", [("b2_swa_q8_0", None), ("mini_gqa_q8_0", 0), ("mini_gqa_q4_0", 0),
-                                             ("mini_gqa_bf16", 0), ("deep_hybrid_q4_0", 0), ("tiny_seg_q8_0", 0)])
+                                             ("mini_gqa_bf16", 0), ("deep_hybrid_q4_0", 0), ("tiny_seg_q8_0", 0),
+                                             ("tiny_seg_q8_0", None), ("tiny_seg_q4_0", None), ("tiny_seg_bf16", None),
+                                             ("chat_pin_q8_0", None), ("chat_spoof_q8_0", None),
+                                             ("mini_gqa_q8_0", None), ("deep_hybrid_q4_0", None)])
 def test_chunked_prefill_matches_token_prefill(name, seg_budget, case_files):
     """The chunked prefill (tensor-core GEMMs + block-window attention per window-aligned piece) leaves the same
     state as streaming the prompt one decode step per token: the last-token logits and every later step agree
@@ -196,10 +199,15 @@ def test_chunked_prefill_matches_token_prefill(name, seg_budget, case_files):
     for sp in sorted({3, W - 1, W, W + 5, 2 * W + 3, ids.shape[1] - 4}):
         if not 0 < sp < ids.shape[1]:
             continue
-        outs = []
+        outs, banks = [], []
         for chunked in (True, False):
             lg, st = m.prefill(ids[:, :sp], seg_budget=seg_budget, chunked_prefill=chunked)
+            si, mem_pos, _ = st.info(0, with_bank=True)
+            banks.append((si.n_pin, mem_pos.tolist()))
             got = [lg.cpu().numpy()] + [m.step(ids[:, t], st).cpu().numpy() for t in range(sp, ids.shape[1])]
             st.check()
+            si, mem_pos, _ = st.info(0, with_bank=True)
+            banks.append((si.n_pin, mem_pos.tolist()))
             outs.append(np.stack(got, axis=1))
         assert np.abs(outs[0] - outs[1]).max() <= _tol(name), (sp, np.abs(outs[0] - outs[1]).max())
+        assert banks[0] == banks[2] and banks[1] == banks[3], (sp, banks)   # pins and bank after prefill / stream

@@ -539,7 +539,8 @@ struct Layout {
         off_mem_tok, off_mem_seg, off_mem_src, off_ema, off_feat, off_x, off_attn, off_h, off_qc, off_qf, off_part,
         off_cnt, off_logits, off_amax, off_scz, off_bar;
     // chunked-prefill workspace: pf_cap tokens
-    uint64_t off_pf_x, off_pf_qc, off_pf_qf, off_pf_attn, off_pf_h, off_pf_x16, off_pf_xs;
+    uint64_t off_pf_x, off_pf_qc, off_pf_qf, off_pf_attn, off_pf_h, off_pf_x16, off_pf_xs, off_pf_feat, off_pf_hin,
+        off_pf_z;
     int pf_cap, pf_ldx16;
     uint64_t total;
     int max_splits, seg_cap, feat_dim;
@@ -602,6 +603,10 @@ Layout make_layout(const ModelDev &md, int B, int seg_cap) {
     L.off_pf_h = take(T * md.F * 4);
     L.off_pf_x16 = take(T * L.pf_ldx16 * 2);
     L.off_pf_xs = take(T * 4);
+    const uint64_t fdim = seg_cap > 0 ? (uint64_t)L.feat_dim : 1;   // scorer buffers only with segment memory
+    L.off_pf_feat = take(T * fdim * 4);
+    L.off_pf_hin = take(T * fdim * 4);
+    L.off_pf_z = take(T * 2 * std::max(1, md.seg_hidden) * 4);
     L.total = cur;
     return L;
 }
@@ -684,6 +689,9 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
     s->pf.x16 = reinterpret_cast<__half *>(A + L.off_pf_x16);
     s->pf.ldx16 = L.pf_ldx16;
     s->pf.xscale = reinterpret_cast<float *>(A + L.off_pf_xs);
+    s->pf.feat = reinterpret_cast<float *>(A + L.off_pf_feat);
+    s->pf.hin = reinterpret_cast<float *>(A + L.off_pf_hin);
+    s->pf.z = reinterpret_cast<float *>(A + L.off_pf_z);
     if (cudaSetDevice(m->device) != cudaSuccess || cudaMalloc(&s->dev, sizeof(StateDev)) != cudaSuccess ||
         cudaMemcpy(s->dev, &sd, sizeof(StateDev), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaStreamCreateWithFlags(&s->cap_stream, cudaStreamNonBlocking) != cudaSuccess) {

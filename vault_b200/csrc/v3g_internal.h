@@ -36,6 +36,9 @@ struct PfBuf {
     __half *x16 = nullptr;   // [cap][ldx16] fp16 GEMM operand
     int ldx16 = 0;
     float *xscale = nullptr; // [cap] per-token operand scale
+    float *feat = nullptr;   // [cap][feat_dim] segment-scorer features of every token
+    float *hin = nullptr;    // [cap][feat_dim] habituated scorer inputs
+    float *z = nullptr;      // [cap][2][seg_hidden] scorer fc1 outputs (raw, habituated)
 };
 
 struct v3g_state {

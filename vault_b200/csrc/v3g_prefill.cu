@@ -17,6 +17,7 @@
 #include "v3g_attn.cuh"
 #include "v3g_gemm.cuh"
 #include "v3g_internal.h"
+#include "v3g_scorer.cuh"
 
 namespace v3g {
 
@@ -82,19 +83,78 @@ __global__ void __launch_bounds__(256) k_piece_begin(const ModelDev *mp, const S
     }
 }
 
-// end of a piece: position, prefill id cursor and (with the lm head) each sequence's greedy next token
+// end of a piece: position, prefill id cursor, the scorer's EMA flag and (with the lm head) each sequence's greedy
+// next token
 __global__ void k_piece_finish(const StateDev *sp, int n, int want_lm) {
     const StateDev &s = *sp;
     StepCtl &sc = *s.step;
-    for (int b = threadIdx.x; b < s.B && want_lm; b += blockDim.x) {
-        const unsigned long long key = __ldcg(&s.amax[b]);
-        s.tok_in[b] = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu)) : 0;
+    for (int b = threadIdx.x; b < s.B; b += blockDim.x) {
+        if (want_lm) {
+            const unsigned long long key = __ldcg(&s.amax[b]);
+            s.tok_in[b] = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu)) : 0;
+        }
+        SeqCtl &q = s.seq[b];
+        if (q.seg_on && q.seg_budget > 0 && n > 0) q.ema_ready = 1;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         sc.pos += n;
         if (sc.ids) sc.ids_idx += n;
     }
+}
+
+// ------------------------------------------------------------------------------------------ segment scorer
+// Habituation inputs of a piece, hin[t] = f[t] - 0.65 ema(before t), and the EMA carried to the piece's end:
+// sequential over the piece's tokens, parallel over features (the step's EMA update, token after token).
+__global__ void k_piece_scan(const StateDev *sp, int n, const float *feat, float *hin) {
+    const StateDev &s = *sp;
+    const int b = blockIdx.y, fd = s.feat_dim;
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    const SeqCtl &q = s.seq[b];
+    if (k >= fd || !(q.seg_on && q.seg_budget > 0)) return;
+    bool ready = q.ema_ready != 0;
+    float e = s.ema[(size_t)b * fd + k];
+    for (int j = 0; j < n; ++j) {
+        const size_t t = (size_t)b * n + j;
+        const float f = feat[t * fd + k];
+        if (ready) {
+            hin[t * fd + k] = sc_hab_in(f, e);
+            e = sc_ema_next(e, f);
+        } else {   // the stream's first token: no habituated score, the EMA starts at f
+            hin[t * fd + k] = f;
+            e = f;
+            ready = true;
+        }
+    }
+    s.ema[(size_t)b * fd + k] = e;
+}
+
+// fc1 of both LayerNorm inputs for every token of the piece (grid: hidden / 8 unit blocks x tokens)
+__global__ void __launch_bounds__(SCORER_THREADS) k_piece_fc1(const ModelDev *mp, const StateDev *sp, int n,
+                                                              const float *feat, const float *hin, float *z) {
+    const ModelDev &m = *mp;
+    const StateDev &s = *sp;
+    const int t = blockIdx.y, b = t / n, fd = s.feat_dim;
+    const SeqCtl &q = s.seq[b];
+    if (!(q.seg_on && q.seg_budget > 0)) return;
+    const float *f = feat + (size_t)t * fd, *h = hin + (size_t)t * fd;
+    scorer_fc1_block(m, fd, [=](int k) { return f[k]; }, [=](int k) { return h[k]; }, blockIdx.x * (SCORER_THREADS / 32),
+                     z + (size_t)t * 2 * m.seg_hidden, z + ((size_t)t * 2 + 1) * m.seg_hidden);
+}
+
+// score of every token of the piece into the score ring (one CTA per token)
+__global__ void __launch_bounds__(SCORER_THREADS) k_piece_score(const ModelDev *mp, const StateDev *sp, int n,
+                                                                int64_t p0, const float *z) {
+    const ModelDev &m = *mp;
+    const StateDev &s = *sp;
+    const int t = blockIdx.x, b = t / n, j = t - b * n;
+    const SeqCtl &q = s.seq[b];
+    if (!(q.seg_on && q.seg_budget > 0)) return;
+    const int64_t pos = p0 + j;
+    const bool ready = q.ema_ready != 0 || j > 0;
+    const float sc = scorer_score_block(m, s, b, q, z + (size_t)t * 2 * m.seg_hidden,
+                                        z + ((size_t)t * 2 + 1) * m.seg_hidden, ready, pos);
+    if (threadIdx.x == 0) s.sc_ring[((size_t)b * 2 + ((pos / m.W) & 1)) * m.W + (int)(pos % m.W)] = sc;
 }
 
 // ------------------------------------------------------------------------------------------ GEMM epilogues
@@ -411,7 +471,6 @@ cudaError_t tc_init_attrs() {
 bool piece_supported(const v3g_model *m, const v3g_state *s) {
     const ModelDev &md = m->host;
     if (!s->pf.x || s->pf.cap < 1) return false;
-    if (md.seg_n_feat > 0 && s->seg_budget > 0) return false;   // segment memory: token path (scorer per token)
     auto ok = [](const MatW &w) { return w.fmt == FMT_Q8 || w.fmt == FMT_Q4 || w.fmt == FMT_BF16 || w.fmt == FMT_F16; };
     for (int l = 0; l < md.n_layers; ++l) {
         const LayerW &L = md.layers[l];
@@ -444,8 +503,13 @@ cudaError_t launch_piece(const v3g_model *m, v3g_state *s, const int32_t *dev_id
                                                            pf.x);
     PF_TRY(cudaGetLastError());
     const int HD = md.H * md.D;
+    const bool any_seg = md.seg_n_feat > 0 && s->seg_budget > 0;
     for (int l = 0; l < md.n_layers; ++l) {
         const LayerW &L = md.layers[l];
+        for (int fi = 0; fi < md.seg_n_feat && any_seg; ++fi)
+            if (md.seg_layers[fi] == l)   // scorer features: residual stream entering this layer, every token
+                PF_TRY(cudaMemcpy2DAsync(pf.feat + (size_t)fi * md.d, (size_t)sd.feat_dim * 4, pf.x, (size_t)md.d * 4,
+                                         (size_t)md.d * 4, (size_t)T, cudaMemcpyDeviceToDevice, st));
         PF_TRY(tc_prep(pf.x, md.d, T, md.d, L.ln1, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
         {
             const MatW *mats[3] = {&L.q, &L.k, &L.v};
@@ -471,6 +535,13 @@ cudaError_t launch_piece(const v3g_model *m, v3g_state *s, const int32_t *dev_id
             TokResid epi{pf.x, md.d, md.d};
             PF_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st));
         }
+    }
+    if (any_seg) {
+        k_piece_scan<<<dim3((sd.feat_dim + 255) / 256, B), 256, 0, st>>>(s->dev, n, pf.feat, pf.hin);
+        k_piece_fc1<<<dim3((md.seg_hidden + 7) / 8, T), SCORER_THREADS, 0, st>>>(m->dev, s->dev, n, pf.feat, pf.hin,
+                                                                                pf.z);
+        k_piece_score<<<T, SCORER_THREADS, 0, st>>>(m->dev, s->dev, n, p0, pf.z);
+        PF_TRY(cudaGetLastError());
     }
     if (want_lm) {   // the last token of every sequence: rows (b n + n - 1) of x, stride n d
         PF_TRY(launch_lm_head(m, s, pf.x + (size_t)(n - 1) * md.d, n * md.d, st));

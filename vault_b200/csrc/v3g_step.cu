@@ -9,6 +9,7 @@
 #include <math.h>
 
 #include "v3g_internal.h"
+#include "v3g_scorer.cuh"
 
 namespace v3g {
 
@@ -397,97 +398,24 @@ __global__ void k_prefix_rot(const ModelDev *mp, const StateDev *sp) {
 }
 
 // ------------------------------------------------------------------------------------------ segment scorer
-// fc1 of SegmentScorer on LayerNorm(f) and LayerNorm(f - 0.65 ema) (src/vault_v3_model.py:879-883, :2294-2305)
-__global__ void k_scorer_fc1(const ModelDev *mp, const StateDev *sp) {
+// fc1 of SegmentScorer on LayerNorm(f) and LayerNorm(f - 0.65 ema) for the step's token (v3g_scorer.cuh)
+__global__ void __launch_bounds__(SCORER_THREADS) k_scorer_fc1(const ModelDev *mp, const StateDev *sp) {
     griddep_wait();
     griddep_launch();
     const ModelDev &m = *mp;
     const StateDev &s = *sp;
     const int b = blockIdx.y;
     if (!seg_active(s.seq[b])) return;
-    const int fd = s.feat_dim, tid = threadIdx.x, nt = blockDim.x;
+    const int fd = s.feat_dim;
     const float *f = s.feat + (size_t)b * fd;
     const float *e = s.ema + (size_t)b * fd;
-    __shared__ float red[4][32];
-    __shared__ float st[4];
-    float a0 = 0.f, a1 = 0.f;
-    for (int k = tid; k < fd; k += nt) {
-        a0 += f[k];
-        a1 += f[k] - 0.65f * e[k];
-    }
-    a0 = warp_sum(a0);
-    a1 = warp_sum(a1);
-    if ((tid & 31) == 0) {
-        red[0][tid >> 5] = a0;
-        red[1][tid >> 5] = a1;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        float x0 = 0.f, x1 = 0.f;
-        for (int w = 0; w < nt / 32; ++w) {
-            x0 += red[0][w];
-            x1 += red[1][w];
-        }
-        st[0] = x0 / fd;
-        st[1] = x1 / fd;
-    }
-    __syncthreads();
-    const float mu0 = st[0], mu1 = st[1];
-    float v0 = 0.f, v1 = 0.f;
-    for (int k = tid; k < fd; k += nt) {
-        const float d0 = f[k] - mu0, d1 = (f[k] - 0.65f * e[k]) - mu1;
-        v0 = fmaf(d0, d0, v0);
-        v1 = fmaf(d1, d1, v1);
-    }
-    v0 = warp_sum(v0);
-    v1 = warp_sum(v1);
-    if ((tid & 31) == 0) {
-        red[2][tid >> 5] = v0;
-        red[3][tid >> 5] = v1;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        float x0 = 0.f, x1 = 0.f;
-        for (int w = 0; w < nt / 32; ++w) {
-            x0 += red[2][w];
-            x1 += red[3][w];
-        }
-        st[2] = 1.0f / sqrtf(x0 / fd + 1e-5f);
-        st[3] = 1.0f / sqrtf(x1 / fd + 1e-5f);
-    }
-    __syncthreads();
-    const float i0 = st[2], i1 = st[3];
-    const int warp = tid >> 5, lane = tid & 31;
-    const int u = blockIdx.x * (nt / 32) + warp;
-    if (u >= m.seg_hidden) return;
-    const float *w1 = m.sc_w1 + (size_t)u * fd;
-    float z0 = 0.f, z1 = 0.f;
-    for (int k = lane; k < fd; k += 32) {
-        const float lw = m.sc_ln_w[k], lb = m.sc_ln_b[k], wk = w1[k];
-        const float h0 = (f[k] - mu0) * i0 * lw + lb;
-        const float h1 = ((f[k] - 0.65f * e[k]) - mu1) * i1 * lw + lb;
-        z0 = fmaf(wk, h0, z0);
-        z1 = fmaf(wk, h1, z1);
-    }
-    z0 = warp_sum(z0);
-    z1 = warp_sum(z1);
-    if (lane == 0) {
-        s.sc_z[((size_t)b * 2 + 0) * m.seg_hidden + u] = z0 + m.sc_b1[u];
-        s.sc_z[((size_t)b * 2 + 1) * m.seg_hidden + u] = z1 + m.sc_b1[u];
-    }
+    scorer_fc1_block(m, fd, [=](int k) { return f[k]; },
+                     [=](int k) { return sc_hab_in(f[k], e[k]); }, blockIdx.x * (SCORER_THREADS / 32),
+                     s.sc_z + ((size_t)b * 2 + 0) * m.seg_hidden, s.sc_z + ((size_t)b * 2 + 1) * m.seg_hidden);
 }
 
-__device__ bool contains(const uint8_t *buf, int n, const char *lit, int ln) {
-    for (int i = 0; i + ln <= n; ++i) {
-        int k = 0;
-        while (k < ln && buf[i + k] == (uint8_t)lit[k]) ++k;
-        if (k == ln) return true;
-    }
-    return false;
-}
-
-// GELU + fc2, habituated score, EMA update, spoof quarantine (src/vault_v3_model.py:2294-2308, :1795-1817)
-__global__ void k_scorer_out(const ModelDev *mp, const StateDev *sp) {
+// GELU + fc2, habituated score, spoof quarantine, then the EMA update of the step's token
+__global__ void __launch_bounds__(SCORER_THREADS) k_scorer_out(const ModelDev *mp, const StateDev *sp) {
     griddep_wait();
     griddep_launch();
     const ModelDev &m = *mp;
@@ -495,63 +423,17 @@ __global__ void k_scorer_out(const ModelDev *mp, const StateDev *sp) {
     const int b = blockIdx.x;
     SeqCtl &q = s.seq[b];
     if (!seg_active(q)) return;
-    const int tid = threadIdx.x, nt = blockDim.x, hd = m.seg_hidden, fd = s.feat_dim;
-    __shared__ float red[2][32];
-    __shared__ uint8_t buf[4096];
+    const int fd = s.feat_dim;
     const bool ready = q.ema_ready;   // read by every thread before thread 0 updates it below
-    float r0 = 0.f, r1 = 0.f;
-    for (int u = tid; u < hd; u += nt) {
-        const float z0 = s.sc_z[((size_t)b * 2 + 0) * hd + u], z1 = s.sc_z[((size_t)b * 2 + 1) * hd + u];
-        const float g0 = 0.5f * z0 * (1.0f + erff(z0 * 0.70710678118654752f));
-        const float g1 = 0.5f * z1 * (1.0f + erff(z1 * 0.70710678118654752f));
-        r0 = fmaf(m.sc_w2[u], g0, r0);
-        r1 = fmaf(m.sc_w2[u], g1, r1);
-    }
-    r0 = warp_sum(r0);
-    r1 = warp_sum(r1);
-    if ((tid & 31) == 0) {
-        red[0][tid >> 5] = r0;
-        red[1][tid >> 5] = r1;
-    }
-    __syncthreads();
+    const int64_t pos = s.step->pos;
+    const float sc = scorer_score_block(m, s, b, q, s.sc_z + ((size_t)b * 2 + 0) * m.seg_hidden,
+                                        s.sc_z + ((size_t)b * 2 + 1) * m.seg_hidden, ready, pos);
     float *e = s.ema + (size_t)b * fd;
     const float *f = s.feat + (size_t)b * fd;
-    for (int k = tid; k < fd; k += nt) e[k] = ready ? 0.985f * e[k] + 0.015f * f[k] : f[k];
-    if (tid == 0) {
-        float raw = 0.f, hab = 0.f;
-        for (int w = 0; w < nt / 32; ++w) {
-            raw += red[0][w];
-            hab += red[1][w];
-        }
-        raw += m.sc_b2[0];
-        hab += m.sc_b2[0];
-        float sc = raw;
-        if (ready && hab > raw) sc = raw + 0.35f * (hab - raw);
+    for (int k = threadIdx.x; k < fd; k += blockDim.x) e[k] = ready ? sc_ema_next(e[k], f[k]) : f[k];
+    if (threadIdx.x == 0) {
         q.ema_ready = 1;
-        const int64_t pos = s.step->pos;
-        const int W = m.W, c = (int)(pos % W), par = ring_par(pos, W);
-        // authority-spoof quarantine over the last <= 24 tokens
-        if (q.n_pin > m.n_sink && pos >= q.n_pin) {
-            int lb = (int)min((int64_t)24, pos - q.n_pin + 1);
-            const int avail_cur = c + 1;
-            lb = min(lb, pos >= W ? W + avail_cur : avail_cur);
-            const int need_prev = avail_cur < lb ? lb - avail_cur : 0;
-            const int cur_start = avail_cur > lb ? avail_cur - lb : 0;
-            int n = 0;
-            for (int k = 0; k < need_prev + (c + 1 - cur_start); ++k) {
-                const int tk = k < need_prev ? s.tok_ring[((size_t)b * 2 + (par ^ 1)) * W + (W - need_prev + k)]
-                                             : s.tok_ring[((size_t)b * 2 + par) * W + cur_start + (k - need_prev)];
-                const uint32_t off = m.tok_off[tk];
-                const int len = m.tok_len[tk];
-                for (int i = 0; i < len && n < 4096; ++i) {
-                    uint8_t ch = m.tok_pool[off + i];
-                    buf[n++] = (ch >= 0x41 && ch <= 0x5A) ? (uint8_t)(ch + 32) : ch;
-                }
-            }
-            if (contains(buf, n, "opi_signed_directive", 20) || contains(buf, n, "urgent opi delegation", 21))
-                sc = -1.0e30f;
-        }
-        s.sc_ring[((size_t)b * 2 + par) * W + c] = sc;
+        s.sc_ring[((size_t)b * 2 + ring_par(pos, m.W)) * m.W + (int)(pos % m.W)] = sc;
     }
 }
 
@@ -1012,10 +894,11 @@ cudaError_t launch_step_begin(const v3g_model *m, v3g_state *s, bool boundary, c
 cudaError_t launch_scorer(const v3g_model *m, v3g_state *s, cudaStream_t st) {
     const ModelDev &md = m->host;
     const bool pdl = s->use_pdl != 0;
-    cudaError_t e = launch_k(pdl, k_scorer_fc1, dim3((md.seg_hidden + 7) / 8, s->B), dim3(256), 0, st,
+    cudaError_t e = launch_k(pdl, k_scorer_fc1, dim3((md.seg_hidden + 7) / 8, s->B), dim3(SCORER_THREADS), 0, st,
                              (const ModelDev *)m->dev, (const StateDev *)s->dev);
     if (e != cudaSuccess) return e;
-    return launch_k(pdl, k_scorer_out, dim3(s->B), dim3(256), 0, st, (const ModelDev *)m->dev, (const StateDev *)s->dev);
+    return launch_k(pdl, k_scorer_out, dim3(s->B), dim3(SCORER_THREADS), 0, st, (const ModelDev *)m->dev,
+                    (const StateDev *)s->dev);
 }
 
 // Kernel sequence of one decode step.  Every launch after the first carries programmatic stream serialization:
@@ -1038,10 +921,7 @@ cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool wa
     V3G_TRY(launch_step_begin(m, s, boundary, st));
     if (s->use_mega) {   // all layers + lm head in one persistent launch
         V3G_TRY(launch_mega(m, s, want_lm, st));
-        if (any_seg) {
-            V3G_TRY(launch_k(pdl, k_scorer_fc1, dim3((md.seg_hidden + 7) / 8, B), dim3(256), 0, st, mdv, sdv));
-            V3G_TRY(launch_k(pdl, k_scorer_out, dim3(B), dim3(256), 0, st, mdv, sdv));
-        }
+        if (any_seg) V3G_TRY(launch_scorer(m, s, st));
         V3G_TRY(launch_argmax_finish(m, s, want_lm, pdl, st));
         return cudaSuccess;
     }
