@@ -153,6 +153,11 @@ V3G_API int v3g_gemv(const v3g_model *m, uint32_t tensor_id, const float *dev_x,
 V3G_API size_t v3g_gemm_work_size(const v3g_model *m, uint32_t tensor_id, uint32_t n_tok);
 V3G_API int v3g_gemm(const v3g_model *m, uint32_t tensor_id, const float *dev_x, uint32_t n_tok, float *dev_y,
                      void *dev_work, size_t work_bytes, void *stream);
+/* One launch of the decode attention of `layer` (the kernel the state's step uses) for every sequence at the state's
+ * current position (the
+ * keys of src/vault_v3_model.py:1072-1139 / runtime/vault3.c:1967-2032: sinks, bank, previous and current chunk),
+ * reading the queries the last step left in the state: for timing the kernel alone (kernel sweep). */
+V3G_API int v3g_attention(v3g_state *s, uint32_t layer, void *stream);
 /* One launch of the persistent decode kernel (every layer of the current position, plus the lm head when want_lm)
  * on a state whose steps use it, without the step's token bookkeeping: for timing the kernel alone.  It rewrites
  * the current position's activations and KV rows, so reset the state before decoding again. */

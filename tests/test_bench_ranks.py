@@ -50,3 +50,20 @@ def test_whole_job_rate_counts_every_rank():
 
 def test_rank_max_without_a_process_group_is_the_identity():
     assert bench.rank_max([3.0, 1.5], "cpu") == [3.0, 1.5]
+
+
+def test_config3_sequences_shard_without_overlap():
+    """BASELINE config 3 shards its 64 sequences evenly: every sequence is served by exactly one rank."""
+    for world in (1, 2, 4, 8):
+        served = [s for r in range(world) for s in bench.shard(64, r, world)]
+        assert sorted(served) == list(range(64))
+        assert all(len(bench.shard(64, r, world)) == 64 // world for r in range(world))
+
+
+def test_chat_prompt_pins_its_system_prefix():
+    """The config 3 / 4 prompts: a ChatML system prefix closing at exactly n_pin tokens, then break tokens."""
+    ids = bench.chat_prompt(5, 512, 4608)
+    assert len(ids) == 4608 and ids[0] == 151644 and ids[1] == 8948 and ids[510] == 151645 and ids[511] == 198
+    body = ids[512:]
+    gaps = [i for i, t in enumerate(body) if t == 198]
+    assert len(gaps) > 4096 // 49

@@ -540,7 +540,7 @@ struct Layout {
         off_cnt, off_logits, off_amax, off_scz, off_bar;
     // chunked-prefill workspace: pf_cap tokens
     uint64_t off_pf_x, off_pf_qc, off_pf_qf, off_pf_attn, off_pf_h, off_pf_x16, off_pf_xs, off_pf_feat, off_pf_hin,
-        off_pf_z;
+        off_pf_z, off_pf_skws;
     int pf_cap, pf_ldx16;
     uint64_t total;
     int max_splits, seg_cap, feat_dim;
@@ -607,6 +607,7 @@ Layout make_layout(const ModelDev &md, int B, int seg_cap) {
     L.off_pf_feat = take(T * fdim * 4);
     L.off_pf_hin = take(T * fdim * 4);
     L.off_pf_z = take(T * 2 * std::max(1, md.seg_hidden) * 4);
+    L.off_pf_skws = take(TC_SPLITK_WS_BYTES);
     L.total = cur;
     return L;
 }
@@ -692,6 +693,8 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
     s->pf.feat = reinterpret_cast<float *>(A + L.off_pf_feat);
     s->pf.hin = reinterpret_cast<float *>(A + L.off_pf_hin);
     s->pf.z = reinterpret_cast<float *>(A + L.off_pf_z);
+    s->pf.sk.ws = reinterpret_cast<float *>(A + L.off_pf_skws);
+    s->pf.sk.ws_bytes = TC_SPLITK_WS_BYTES;
     if (cudaSetDevice(m->device) != cudaSuccess || cudaMalloc(&s->dev, sizeof(StateDev)) != cudaSuccess ||
         cudaMemcpy(s->dev, &sd, sizeof(StateDev), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaStreamCreateWithFlags(&s->cap_stream, cudaStreamNonBlocking) != cudaSuccess) {
@@ -950,6 +953,12 @@ extern "C" int v3g_decode_pass(v3g_state *s, int want_lm, void *stream) {
     cudaStream_t st = (cudaStream_t)stream;
     CUDA_TRY(cudaMemsetAsync(s->host.bar, 0, sizeof(unsigned int), st));   // grid-barrier counter, as k_begin does
     CUDA_TRY(launch_mega(s->m, s, want_lm != 0, st));
+    return V3G_OK;
+}
+
+extern "C" int v3g_attention(v3g_state *s, uint32_t layer, void *stream) {
+    if (!s || layer >= (uint32_t)s->m->host.n_layers) return fail(V3G_E_ARG, "null state or layer out of range");
+    CUDA_TRY(launch_step_attention(s->m, s, (int)layer, (cudaStream_t)stream));
     return V3G_OK;
 }
 

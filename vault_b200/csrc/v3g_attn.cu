@@ -7,16 +7,17 @@
 
 namespace v3g {
 
+// one work item per CTA: `tps` 64-key tiles of (sequence blockIdx.z, KV head blockIdx.y), split blockIdx.x
 template <int D>
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(const ModelDev *mp, const StateDev *sp, int layer,
-                                                           float scale) {
-    __shared__ __align__(16) AttnSmem<D> sm;
+                                                           float scale, int tps) {
+    __shared__ __align__(16) AttnSmemSpan<D> sm;
     griddep_wait();
     griddep_launch();
     const int64_t pos = __ldcg(&sp->step->pos);
     (void)mp;
     const KeySpan ks = key_span(*sp, blockIdx.z, pos);
-    attn_item<D>(*sp, ks, layer, scale, blockIdx.x, blockIdx.y, blockIdx.z, pos, sm, blockDim.x);
+    attn_span<D>(*sp, ks, layer, scale, blockIdx.x, tps, blockIdx.y, blockIdx.z, pos, sm, blockDim.x);
 }
 
 // greedy next token = first index of the largest logit (v3_argmax, runtime/vault3.c:3198-3202; torch.argmax):
@@ -72,11 +73,16 @@ __global__ void k_finish(const StateDev *sp, int want_lm) {
     }
 }
 
+// tiles per split: enough splits to give the SMs about four items each at the state's longest key span, at most
+// 16 tiles (1,024 keys) per item
 template <int D>
 static cudaError_t launch_attention_d(const v3g_model *m, v3g_state *s, int layer, bool pdl, cudaStream_t st) {
-    dim3 grid(s->host.max_splits, m->host.G, s->B);
+    const int64_t work = (int64_t)s->host.max_splits * m->host.G * s->B;   // 64-key tiles at the longest span
+    int tps = (int)(work / (4 * (int64_t)m->n_sm));
+    tps = tps < 1 ? 1 : (tps > 16 ? 16 : tps);
+    dim3 grid((s->host.max_splits + tps - 1) / tps, m->host.G, s->B);
     return launch_k(pdl, k_attention<D>, grid, dim3(ATT_THREADS), 0, st, (const ModelDev *)m->dev,
-                    (const StateDev *)s->dev, layer, (float)(1.0 / sqrt((double)D)));
+                    (const StateDev *)s->dev, layer, (float)(1.0 / sqrt((double)D)), tps);
 }
 
 cudaError_t launch_attention(const v3g_model *m, v3g_state *s, int layer, bool pdl, cudaStream_t st) {

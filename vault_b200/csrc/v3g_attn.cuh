@@ -272,4 +272,178 @@ __device__ bool attn_item(const StateDev &s, const KeySpan &ks, int layer, float
     return true;
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Long splits for the per-phase decode path: one work item covers `tps` consecutive 64-key tiles of one (sequence,
+// KV head) with an online softmax across them, so a batch over thousands of keys leaves a few partials per head
+// (few items to merge) instead of one per 64 keys.  Tile arithmetic as in attn_item (queries and probabilities as
+// high + low fp16 parts on the tensor cores, fp16 K / V); the running maximum rescales the partial output and sum.
+template <int D>
+struct AttnSmemSpan {
+    AttnSmem<D> t;
+    float alpha[ATT_GRP_MAX];   // rescale of the running output when a tile raises a head's maximum
+};
+
+template <int D>
+__device__ bool attn_span(const StateDev &s, const KeySpan &ks, int layer, float scale, int split, int tps, int g, int b,
+                          int64_t pos, AttnSmemSpan<D> &ss, int nt) {
+    constexpr int KP = D + 8, CH = D / 8, PS = att_part_stride(D), NBW = (D / 8 + 3) / 4;
+    AttnSmem<D> &sm = ss.t;
+    const int H = s.H, G = s.G, grp = H / G;
+    const int span = ATT_KPC * tps;
+    const int n_splits = (ks.total + span - 1) / span;
+    if (split >= n_splits) return false;
+    const int jb = split * span, nkeys = min(span, ks.total - jb);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarp = nt >> 5;
+    const int gq = lane >> 2, t = lane & 3;
+    float o[NBW][4];   // this warp's output blocks nb = warp, warp + nwarp, ...
+#pragma unroll
+    for (int i = 0; i < NBW; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    for (int idx = tid; idx < 2 * ATT_GRP_MAX * D / 4; idx += nt) {   // queries, four dims per item
+        const int w = idx / (ATT_GRP_MAX * D / 4), r = idx - w * (ATT_GRP_MAX * D / 4);
+        const int hr = r / (D / 4), dd = 4 * (r - hr * (D / 4));
+        float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (hr < grp && (w == 1 || pos >= s.W)) {
+            const size_t qo = ((size_t)b * H + g * grp + hr) * D + dd;
+            q = __ldcg(reinterpret_cast<const float4 *>((w ? s.q_cur : s.q_far) + qo));
+        }
+        const float qv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) split_half(qv[e], sm.qa[w][0][hr][dd + e], sm.qa[w][1][hr][dd + e]);
+    }
+    if (tid < ATT_GRP_MAX) {
+        sm.m[tid] = -INFINITY;
+        sm.l[tid] = 0.f;
+    }
+    for (int j0 = jb; j0 < jb + nkeys; j0 += ATT_KPC) {
+        const int nk = min(ATT_KPC, jb + nkeys - j0);
+        const int nfar = ks.n_sk + ks.n_seg + ks.n_prev - j0;   // keys j < nfar are scored with the far query
+        for (int c = tid; c < ATT_KPC * CH; c += nt) {
+            const int j = c / CH, part = c - j * CH;
+            if (j < nk) {
+                bool far;
+                cp_async16(&sm.k[j * KP + part * 8], kv_row(s, layer, b, g, ks, j0 + j, false, far) + part * 8);
+                cp_async16(&sm.v[j * KP + part * 8], kv_row(s, layer, b, g, ks, j0 + j, true, far) + part * 8);
+            } else {
+                *reinterpret_cast<uint4 *>(&sm.v[j * KP + part * 8]) = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        sync_threads(nt);
+        for (int kb = warp; kb * 8 < nk; kb += nwarp) {
+            const int key0 = kb * 8;
+            const bool any_far = key0 < nfar, any_cur = key0 + 8 > nfar;
+            float cf[4] = {0.f, 0.f, 0.f, 0.f}, cc[4] = {0.f, 0.f, 0.f, 0.f};
+            const kv_t *krow = &sm.k[(key0 + gq) * KP + 2 * t];
+#pragma unroll
+            for (int k16 = 0; k16 < D / 16; ++k16) {
+                const uint32_t b0 = ld_h2(krow + 16 * k16), b1 = ld_h2(krow + 16 * k16 + 8);
+                const int qc = 16 * k16 + 2 * t;
+                if (any_far)
+                    mma16816(cf, ld_h2(&sm.qa[0][0][gq][qc]), ld_h2(&sm.qa[0][1][gq][qc]), ld_h2(&sm.qa[0][0][gq][qc + 8]),
+                             ld_h2(&sm.qa[0][1][gq][qc + 8]), b0, b1);
+                if (any_cur)
+                    mma16816(cc, ld_h2(&sm.qa[1][0][gq][qc]), ld_h2(&sm.qa[1][1][gq][qc]), ld_h2(&sm.qa[1][0][gq][qc + 8]),
+                             ld_h2(&sm.qa[1][1][gq][qc + 8]), b0, b1);
+            }
+            if (gq < grp) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int j = key0 + 2 * t + e;
+                    const float sc = (j < nfar ? cf[e] + cf[2 + e] : cc[e] + cc[2 + e]) * scale;
+                    sm.p[gq][j] = j < nk ? sc : -INFINITY;
+                }
+            }
+        }
+        sync_threads(nt);
+        // online softmax, one warp per head: the tile's maximum updates the running one
+        for (int hr = warp; hr < ATT_GRP_MAX; hr += nwarp) {
+            if (hr < grp) {
+                float mx = -INFINITY;
+                for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sm.p[hr][j]);
+                mx = warp_max(mx);
+                const float m_old = sm.m[hr], m_new = fmaxf(m_old, mx);
+                float l = 0.f;
+                for (int j = lane; j < ATT_KPC; j += 32) {
+                    const float p = j < nk ? expf(sm.p[hr][j] - m_new) : 0.f;
+                    split_half(p, sm.pa[0][hr][j], sm.pa[1][hr][j]);
+                    l += p;
+                }
+                l = warp_sum(l);
+                if (lane == 0) {
+                    const float al = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+                    ss.alpha[hr] = al;
+                    sm.l[hr] = sm.l[hr] * al + l;
+                    sm.m[hr] = m_new;
+                }
+            } else {
+                for (int j = lane; j < ATT_KPC; j += 32) sm.pa[0][hr][j] = sm.pa[1][hr][j] = __float2half_rn(0.f);
+                if (lane == 0) ss.alpha[hr] = 0.f;
+            }
+        }
+        sync_threads(nt);
+        const int nk16 = (nk + 15) / 16;
+        const float al = gq < grp ? ss.alpha[gq] : 0.f;
+#pragma unroll
+        for (int i = 0; i < NBW; ++i) {
+            const int nb = warp + i * nwarp;
+            if (nb >= D / 8) continue;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[i][e] *= al;
+            for (int k16 = 0; k16 < nk16; ++k16) {
+                uint32_t b0, b1;
+                ldsm_x2_trans(b0, b1, &sm.v[(16 * k16 + (lane & 15)) * KP + 8 * nb]);
+                const int pc = 16 * k16 + 2 * t;
+                mma16816(o[i], ld_h2(&sm.pa[0][gq][pc]), ld_h2(&sm.pa[1][gq][pc]), ld_h2(&sm.pa[0][gq][pc + 8]),
+                         ld_h2(&sm.pa[1][gq][pc + 8]), b0, b1);
+            }
+        }
+        sync_threads(nt);   // the tile buffers are refilled next
+    }
+    // write the split's result: direct when one split covers the span, else a partial merged by the last CTA
+    float *part = n_splits == 1 ? nullptr : s.att_part + ((((size_t)b * G + g) * s.max_splits + split) * grp) * PS;
+#pragma unroll
+    for (int i = 0; i < NBW; ++i) {
+        const int nb = warp + i * nwarp;
+        if (nb >= D / 8 || gq >= grp) continue;
+        const int dd = 8 * nb + 2 * t;
+        const float o0 = o[i][0] + o[i][2], o1 = o[i][1] + o[i][3];
+        if (!part) {
+            const float inv = 1.f / sm.l[gq];
+            *reinterpret_cast<float2 *>(&s.attn[((size_t)b * H + g * grp + gq) * D + dd]) = make_float2(o0 * inv, o1 * inv);
+        } else {
+            *reinterpret_cast<float2 *>(&part[gq * PS + dd]) = make_float2(o0, o1);
+        }
+    }
+    if (!part) {
+        sync_threads(nt);
+        return true;
+    }
+    if (tid < grp) *reinterpret_cast<float2 *>(&part[tid * PS + D]) = make_float2(sm.m[tid], sm.l[tid]);
+    __threadfence();
+    sync_threads(nt);
+    if (tid == 0) sm.last = atomicAdd(&s.att_cnt[b * G + g], 1u) == (uint32_t)(n_splits - 1);
+    sync_threads(nt);
+    if (sm.last) {
+        __threadfence();
+        const float *p0 = s.att_part + (((size_t)b * G + g) * s.max_splits) * grp * PS;
+        for (int idx = tid; idx < grp * D; idx += nt) {
+            const int hr = idx / D, dd = idx - hr * D;
+            float M = -INFINITY;
+            for (int sp2 = 0; sp2 < n_splits; ++sp2) M = fmaxf(M, __ldcg(&p0[((size_t)sp2 * grp + hr) * PS + D]));
+            float L = 0.f, O = 0.f;
+            for (int sp2 = 0; sp2 < n_splits; ++sp2) {
+                const float *pp = p0 + ((size_t)sp2 * grp + hr) * PS;
+                const float w = expf(__ldcg(&pp[D]) - M);
+                L = fmaf(__ldcg(&pp[D + 1]), w, L);
+                O = fmaf(__ldcg(&pp[dd]), w, O);
+            }
+            s.attn[((size_t)b * H + g * grp + hr) * D + dd] = O / L;
+        }
+        if (tid == 0) s.att_cnt[b * G + g] = 0u;
+    }
+    sync_threads(nt);
+    return true;
+}
+
 }  // namespace v3g

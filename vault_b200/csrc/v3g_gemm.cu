@@ -2,6 +2,7 @@
 // the kernel-level entry point v3g_gemm used by the tests and the kernel sweep.
 #include <string.h>
 
+#include <algorithm>
 #include <cmath>
 
 #include <mutex>
@@ -93,7 +94,7 @@ static cudaError_t make_xmap(CUtensorMap *map, const __half *x, int rows, int K,
 
 // ------------------------------------------------------------------------------------------------ launch plan
 cudaError_t tc_setup(TcLaunch &L, const MatW *const *mats, int n, const __half *x16, int ldx, const float *xscale,
-                     int n_tok, int *status, int n_sm) {
+                     int n_tok, int *status, int n_sm, const TcSplitWs *sk) {
     memset(&L, 0, sizeof(L));
     TcArgs &a = L.a;
     if (n < 1 || n > 3 || n_tok < 1) return cudaErrorInvalidValue;
@@ -147,8 +148,21 @@ cudaError_t tc_setup(TcLaunch &L, const MatW *const *mats, int n, const __half *
     a.x_off = a.stages * a.stage_a;
     a.raw_off = a.x_off + a.stages * a.stage_x;
     a.bar_off = a.raw_off + a.stages * a.stage_raw;
-    L.smem = (size_t)a.bar_off + 8 * (3 * a.stages + 4) + 16 + 1024;   // + slack for the 1024-byte alignment
-    const int work = a.m_tiles * a.n_tiles;
+    L.smem = (size_t)a.bar_off + 8 * (3 * a.stages + 4) + 16 + 1024;   // + TMEM address, flag, alignment slack
+    // split K when the output tiles cannot cover the GPU (small batches): up to 16 splits of >= 4 stages each,
+    // bounded by the workspace
+    const int tiles = a.m_tiles * a.n_tiles;
+    a.splits = 1;
+    if (sk && sk->ws && tiles < n_sm) {
+        int sp = n_sm / tiles;
+        sp = std::min(sp, std::min(16, a.kstages / 4));
+        while (sp > 1 && (size_t)tiles * sp * a.bn * TC_BM * 4 > sk->ws_bytes) --sp;
+        if (sp > 1) {
+            a.splits = sp;
+            a.ws = sk->ws;
+        }
+    }
+    const int work = tiles * a.splits;
     L.grid = work < n_sm ? work : n_sm;
     return make_xmap(&L.xmap, x16, n_tok, a.K, ldx, a.bn);
 }
@@ -182,7 +196,8 @@ extern "C" size_t v3g_gemm_work_size(const v3g_model *m, uint32_t tensor_id, uin
     const MatW *w = m ? tc_find_mat(m, tensor_id) : nullptr;
     if (!w || n_tok == 0) return 0;
     const size_t ldx = (size_t)(w->cols + 63) / 64 * 64;
-    return ((size_t)n_tok * ldx * 2 + 255) / 256 * 256 + ((size_t)n_tok * 4 + 255) / 256 * 256 + 256;
+    return ((size_t)n_tok * ldx * 2 + 255) / 256 * 256 + ((size_t)n_tok * 4 + 255) / 256 * 256 + 256 +
+           TC_SPLITK_WS_BYTES;
 }
 
 extern "C" int v3g_gemm(const v3g_model *m, uint32_t tensor_id, const float *dev_x, uint32_t n_tok, float *dev_y,
@@ -198,12 +213,15 @@ extern "C" int v3g_gemm(const v3g_model *m, uint32_t tensor_id, const float *dev
     __half *x16 = reinterpret_cast<__half *>(wp);
     float *xs = reinterpret_cast<float *>(wp + ((size_t)n_tok * ldx * 2 + 255) / 256 * 256);
     int *status = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(xs) + ((size_t)n_tok * 4 + 255) / 256 * 256);
+    TcSplitWs sk;
+    sk.ws = reinterpret_cast<float *>(status + 64);
+    sk.ws_bytes = TC_SPLITK_WS_BYTES;
     cudaError_t e = cudaMemsetAsync(status, 0, 4, st);
     if (e == cudaSuccess) e = tc_prep(dev_x, w->cols, (int)n_tok, w->cols, nullptr, 0.f, x16, ldx, xs, st);
     const MatW *mats[1] = {w};
     const int src_rows = w->rowmap == ROWS_GATE_UP ? w->rows / 2 : w->rows;
     TcEpiStore epi{dev_y, (int64_t)w->rows, w->rowmap, m->host.D, src_rows};
-    if (e == cudaSuccess) e = tc_gemm(mats, 1, x16, ldx, xs, (int)n_tok, status, m->n_sm, epi, st);
+    if (e == cudaSuccess) e = tc_gemm(mats, 1, x16, ldx, xs, (int)n_tok, status, m->n_sm, epi, st, &sk);
     if (e == cudaErrorNotSupported) return v3g_fail(V3G_E_UNSUPPORTED, "matrix format has no tensor-core path (F32)");
     if (e != cudaSuccess) return v3g_fail(V3G_E_CUDA, std::string("v3g_gemm: ") + cudaGetErrorString(e));
     return V3G_OK;

@@ -9,20 +9,22 @@
 // CTA tile), the tokens its B operand (N = bn tokens, 16..256), the fp32 accumulator lives in tensor memory.
 //
 // One persistent CTA per SM walks the (128-row, bn-token) output tiles with warp-specialised roles:
-//   warp 0      producer: for every 64-wide k stage, bulk-copies the 8 row tiles' stored weight bytes (their
-//               k tiles are contiguous in HBM) and loads the bn x 64 activation box with the tensor map (TMA,
-//               128-byte swizzle), all completing on the stage's `full` mbarrier;
-//   warps 2-5   converters: dequantize the stage's weight bytes into the A operand (fp16, K-major, 128-byte
+//   warp 0      producer: for every 64-wide k stage, lanes 0-7 bulk-copy the 8 row tiles' stored weight bytes (their
+//               k tiles are contiguous in HBM) and lane 8 loads the bn x 64 activation box with the tensor map
+//               (TMA, 128-byte swizzle), all completing on the stage's `full` mbarrier;
+//   warps 2-9   converters (one per row tile): dequantize the stage's weight bytes into the A operand (fp16, K-major, 128-byte
 //               swizzle) -- Q8_0 codes and Q4_0 nibbles times their fp16 block scale (times a per-matrix power of two
 //               that keeps small scales out of the fp16 subnormal range), 16-bit tiles copied -- then fence the
 //               writes to the async proxy and arrive on `conv`;
 //   warp 1      allocates 512 TMEM columns (two accumulator buffers) and issues, from one thread, the four
 //               tcgen05.mma (K = 16 each) of every stage, committing the stage's `empty` barrier (its buffers may be
 //               refilled) and, after a tile's last stage, the buffer's `acc_full` barrier;
-//   warps 6-9   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32 (w % 4) ..), scale each token's
+//   warps 10-13 epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32 (w % 4) ..), scale each token's
 //               column by its activation scale and the matrix's weight scale, and hand (row g, row g+8) pairs of a
 //               16-row tile to the fused epilogue -- the partners of the RoPE / gate-up row order sit 8 lanes apart;
 //               then release the accumulator buffer (`acc_empty`).
+// Few output tiles (small batches) split K over up to 16 CTAs per tile: each split writes an fp32 partial, and a
+// second kernel over all (row pair, token) outputs adds the splits in order (deterministic) and runs the epilogue.
 // Every wait is bounded: a wait that runs out records status bit 4 (timeout) and its role stops.
 #pragma once
 #include <cuda.h>
@@ -35,11 +37,13 @@ namespace v3g {
 
 constexpr int TC_BM = 128;            // weight rows per CTA tile (8 row tiles)
 constexpr int TC_BK = 64;             // k per stage (one 128-byte swizzled row)
-constexpr int TC_THREADS = 320;       // 10 warps
-constexpr int TC_CONV_WARPS = 4;
+constexpr int TC_CONV_WARPS = 8;      // one per row tile of the CTA tile
+constexpr int TC_THREADS = 32 * (2 + TC_CONV_WARPS + 4);   // producer, MMA, converters, 4 epilogue warps
 constexpr int TC_RAW_ROW = 2048;      // stored weight bytes of one row tile per stage (16-bit tiles: 4 x 512)
 constexpr int TC_MAX_STAGES = 4;
 constexpr int TC_TMEM_COLS = 512;
+// split-K workspace of a state: tiles x splits <= SMs, so 256 SMs x 256 tokens x 128 rows of fp32 always suffice
+constexpr size_t TC_SPLITK_WS_BYTES = (size_t)256 * 256 * 128 * 4;
 
 struct TcSeg {
     const uint8_t *tiles;
@@ -57,6 +61,9 @@ struct TcArgs {
     int n_tok, bn, n_tiles;
     int stages;
     int seg_base;          // segment index the epilogue receives for seg[0]
+    int splits;            // k splits per output tile (1: no split)
+    float *ws;             // split-K partials [tile][split][bn][128] (splits > 1)
+
     const float *xscale;   // [n_tok] multiplier undoing each token's activation scale
     int *status;           // sticky error word (bit 4: a bounded wait ran out)
     // shared-memory layout (bytes from the 1024-aligned base)
@@ -178,6 +185,16 @@ __device__ __forceinline__ void tc_convert_row_tile(const TcArgs &a, uint8_t *A,
 }
 
 // --------------------------------------------------------------------------------------------------- the kernel
+// work item w -> output tile (mt, nt) and k-split sp (k stages [ks0, ks1))
+__device__ __forceinline__ void tc_work(const TcArgs &a, int w, int &mt, int &nt, int &sp, int &ks0, int &ks1) {
+    const int tile = w / a.splits;
+    sp = w - tile * a.splits;
+    mt = tile / a.n_tiles;
+    nt = tile - mt * a.n_tiles;
+    ks0 = (int)((int64_t)sp * a.kstages / a.splits);
+    ks1 = (int)((int64_t)(sp + 1) * a.kstages / a.splits);
+}
+
 template <int FA, int FB, class Epi>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ TcArgs a,
                                                           const __grid_constant__ CUtensorMap xmap, Epi epi) {
@@ -187,7 +204,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = a.stages;
     const uint32_t bars = tc::smem_addr(smem + a.bar_off);
-    // barrier slots: full[S], conv[S], empty[S], acc_full[2], acc_empty[2]; then the TMEM address
+    // barrier slots: full[S], conv[S], empty[S], acc_full[2], acc_empty[2]; then the TMEM address and a flag word
     auto FULL = [&](int s) { return bars + 8u * s; };
     auto CONV = [&](int s) { return bars + 8u * (S + s); };
     auto EMPTY = [&](int s) { return bars + 8u * (2 * S + s); };
@@ -211,55 +228,58 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int n_work = a.m_tiles * a.n_tiles;
+    const int n_work = a.m_tiles * a.n_tiles * a.splits;
+    const int total_rt = a.rbase[a.n_seg];
 
     if (warp == 0) {   // ------------------------------------------------------------------------- producer
-        if (lane == 0) {
-            tc::prefetch_tmap(&xmap);
-            const uint64_t pol = tc::l2_evict_first_policy();
-            int it = 0;
-            bool ok = true;
-            for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
-                const int mt = w / a.n_tiles, nt = w - mt * a.n_tiles;
-                for (int ks = 0; ks < a.kstages; ++ks, ++it) {
-                    const int s = it % S;
-                    if (it >= S && !tc::mbar_wait(EMPTY(s), ((it / S) - 1) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    uint32_t bytes = (uint32_t)a.bn * TC_BK * 2;
-                    const uint8_t *src[8];
-                    uint32_t nb[8];
-                    for (int r = 0; r < 8; ++r) {
-                        const int R = mt * 8 + r;
-                        src[r] = nullptr;
-                        nb[r] = 0;
-                        if (R >= a.rbase[a.n_seg]) continue;
-                        int rt;
-                        const int si = tc_seg_of(a, R, rt);
-                        const TcSeg &sg = a.seg[si];
-                        const int tk = tile_k(sg.fmt), per = TC_BK / tk, kt0 = ks * per;
-                        const int n = min(per, sg.n_ktiles - kt0);
-                        if (n <= 0) continue;
-                        src[r] = sg.tiles + ((size_t)rt * sg.n_ktiles + kt0) * tile_bytes(sg.fmt);
-                        nb[r] = (uint32_t)(n * tile_bytes(sg.fmt));
-                        bytes += nb[r];
-                    }
-                    tc::mbar_expect_tx(FULL(s), bytes);
-                    const uint32_t raw = tc::smem_addr(smem + a.raw_off + s * a.stage_raw);
-                    for (int r = 0; r < 8; ++r)
-                        if (src[r]) tc::bulk_g2s(raw + r * TC_RAW_ROW, src[r], nb[r], FULL(s), pol);
+        // lane r < 8 streams row tile r of the CTA tile (its stored k tiles are contiguous); lane 8 the activations
+        if (lane == 0) tc::prefetch_tmap(&xmap);
+        const uint64_t pol = tc::l2_evict_first_policy();
+        int it = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
+            int mt, nt, sp, ks0, ks1;
+            tc_work(a, w, mt, nt, sp, ks0, ks1);
+            const uint8_t *base = nullptr;
+            int tb = 0, nkt = 0, per = 0;
+            const int R = mt * 8 + lane;
+            if (lane < 8 && R < total_rt) {
+                int rt;
+                const TcSeg &sg = a.seg[tc_seg_of(a, R, rt)];
+                tb = tile_bytes(sg.fmt);
+                nkt = sg.n_ktiles;
+                per = TC_BK / tile_k(sg.fmt);
+                base = sg.tiles + (size_t)rt * nkt * tb;
+            }
+            for (int ks = ks0; ks < ks1; ++ks, ++it) {
+                const int s = it % S;
+                if (it >= S && !tc::mbar_wait(EMPTY(s), ((it / S) - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                const int kt0 = ks * per;
+                const int n = base ? max(0, min(per, nkt - kt0)) : 0;
+                int bytes = n * tb;
+#pragma unroll
+                for (int o = 4; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);   // lanes 0..7
+                if (lane == 0) tc::mbar_expect_tx(FULL(s), (uint32_t)(bytes + a.bn * TC_BK * 2));
+                __syncwarp();
+                if (n > 0)
+                    tc::bulk_g2s(tc::smem_addr(smem + a.raw_off + s * a.stage_raw + lane * TC_RAW_ROW),
+                                 base + (size_t)kt0 * tb, (uint32_t)(n * tb), FULL(s), pol);
+                if (lane == 8)
                     tc::tma_load_2d(tc::smem_addr(smem + a.x_off + s * a.stage_x), &xmap, ks * TC_BK, nt * a.bn,
                                     FULL(s));
-                }
             }
-            if (!ok) atomicOr(a.status, 4);
         }
+        if (!ok && lane == 0) atomicOr(a.status, 4);
     } else if (warp == 1) {   // ------------------------------------------------------------------ MMA issuer
         const uint32_t idesc = tc::idesc_f16(TC_BM, a.bn);
         int it = 0, tcount = 0;
         bool ok = true;
         for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x, ++tcount) {
+            int mt, nt, sp, ks0, ks1;
+            tc_work(a, w, mt, nt, sp, ks0, ks1);
             const int buf = tcount & 1;
             if (tcount >= 2 && !tc::mbar_wait(ACCE(buf), ((tcount >> 1) - 1) & 1)) {
                 ok = false;
@@ -267,7 +287,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             }
             tc::tc_fence_after();
             const uint32_t d = tmem + (uint32_t)(buf * a.bn);
-            for (int ks = 0; ks < a.kstages; ++ks, ++it) {
+            for (int ks = ks0; ks < ks1; ++ks, ++it) {
                 const int s = it % S;
                 if (!tc::mbar_wait(CONV(s), (it / S) & 1)) {
                     ok = false;
@@ -280,7 +300,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
 #pragma unroll
                     for (int k16 = 0; k16 < TC_BK / 16; ++k16)
                         tc::mma_f16(d, tc::sw128_desc(sa + 32 * k16), tc::sw128_desc(sx + 32 * k16), idesc,
-                                    (ks | k16) != 0 ? 1u : 0u);
+                                    (ks > ks0 || k16 > 0) ? 1u : 0u);
                     tc::mma_commit(EMPTY(s));
                 }
                 __syncwarp();
@@ -291,23 +311,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         }
         if (!ok && lane == 0) atomicOr(a.status, 4);
     } else if (warp < 2 + TC_CONV_WARPS) {   // ---------------------------------------------------- converters
-        const int cw = warp - 2;
+        const int rl = warp - 2;              // the row tile this warp converts
         int it = 0;
         bool ok = true;
         for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
-            const int mt = w / a.n_tiles;
-            for (int ks = 0; ks < a.kstages; ++ks, ++it) {
+            int mt, nt, sp, ks0, ks1;
+            tc_work(a, w, mt, nt, sp, ks0, ks1);
+            const int R = mt * 8 + rl;
+            for (int ks = ks0; ks < ks1; ++ks, ++it) {
                 const int s = it % S;
                 if (!tc::mbar_wait(FULL(s), (it / S) & 1)) {
                     ok = false;
                     break;
                 }
-                uint8_t *A = smem + a.a_off + s * a.stage_a;
-                const uint8_t *raw = smem + a.raw_off + s * a.stage_raw;
-                for (int rl = 2 * cw; rl < 2 * cw + 2; ++rl) {
-                    const int R = mt * 8 + rl;
-                    if (R < a.rbase[a.n_seg]) tc_convert_row_tile<FA, FB>(a, A, raw + rl * TC_RAW_ROW, R, rl, ks, lane);
-                }
+                if (R < total_rt)
+                    tc_convert_row_tile<FA, FB>(a, smem + a.a_off + s * a.stage_a,
+                                                smem + a.raw_off + s * a.stage_raw + rl * TC_RAW_ROW, R, rl, ks, lane);
                 tc::fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(CONV(s));
@@ -320,7 +339,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         int tcount = 0;
         bool ok = true;
         for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x, ++tcount) {
-            const int mt = w / a.n_tiles, nt = w - mt * a.n_tiles;
+            int mt, nt, sp, ks0, ks1;
+            tc_work(a, w, mt, nt, sp, ks0, ks1);
             const int buf = tcount & 1;
             if (!tc::mbar_wait(ACCF(buf), (tcount >> 1) & 1)) {
                 ok = false;
@@ -328,28 +348,48 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             }
             tc::tc_fence_after();
             const int R = mt * 8 + (row >> 4), tr = row & 15;
-            const bool live = R < a.rbase[a.n_seg] && tr < 8;
+            const bool live = R < total_rt && tr < 8;
             int rt = 0, si = 0;
-            if (R < a.rbase[a.n_seg]) si = tc_seg_of(a, R, rt);
+            if (R < total_rt) si = tc_seg_of(a, R, rt);
             const float ws = a.seg[si].wscale;
+            const int tile = mt * a.n_tiles + nt;
+            if (a.splits == 1) {
+                for (int c0 = 0; c0 < a.bn; c0 += 16) {
+                    uint32_t v[16];
+                    tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * a.bn + c0), v);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float y = __uint_as_float(v[j]);
+                        const float yp = __shfl_xor_sync(0xffffffffu, y, 8);
+                        const int tok = nt * a.bn + c0 + j;
+                        if (live && tok < a.n_tok) {
+                            const float sc = __ldg(a.xscale + tok) * ws;
+                            epi(si + a.seg_base, rt, tr, tok, y * sc, yp * sc);
+                        }
+                    }
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(ACCE(buf));
+                continue;
+            }
+            // split-K: this split's fp32 partial goes to the workspace ([tile][split][128 rows][bn columns]); the
+            // reduction kernel (k_tc_splitk_reduce) adds the splits in order and runs the epilogue
+            float *part = a.ws + (((size_t)tile * a.splits + sp) * TC_BM + row) * a.bn;
             for (int c0 = 0; c0 < a.bn; c0 += 16) {
                 uint32_t v[16];
                 tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * a.bn + c0), v);
                 tc::tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const float y = __uint_as_float(v[j]);
-                    const float yp = __shfl_xor_sync(0xffffffffu, y, 8);
-                    const int tok = nt * a.bn + c0 + j;
-                    if (live && tok < a.n_tok) {
-                        const float sc = __ldg(a.xscale + tok) * ws;
-                        epi(si + a.seg_base, rt, tr, tok, y * sc, yp * sc);
-                    }
-                }
+                for (int j = 0; j < 16; j += 4)
+                    __stcg(reinterpret_cast<float4 *>(part + c0 + j),
+                           make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                       __uint_as_float(v[j + 3])));
             }
             tc::tc_fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(ACCE(buf));
+            if (lane == 0) tc::mbar_arrive(ACCE(buf));   // the accumulator buffer is free again
         }
         if (!ok && lane == 0) atomicOr(a.status, 4);
     }
@@ -359,6 +399,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, TC_TMEM_COLS);
     }
+}
+
+// split-K reduction: one thread per (output tile, row pair (g, g+8) of a 16-row tile, token column): the splits'
+// partials summed in split order, then the fused epilogue of the pair
+template <class Epi>
+__global__ void __launch_bounds__(256) k_tc_splitk_reduce(const __grid_constant__ TcArgs a, Epi epi) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t n = (int64_t)a.m_tiles * a.n_tiles * 64 * a.bn;
+    if (idx >= n) return;
+    const int c = (int)(idx % a.bn);
+    const int pair = (int)((idx / a.bn) % 64);
+    const int tile = (int)(idx / ((int64_t)a.bn * 64));
+    const int mt = tile / a.n_tiles, nt = tile - mt * a.n_tiles;
+    const int rl = pair >> 3, g = pair & 7;
+    const int R = mt * 8 + rl, tok = nt * a.bn + c;
+    if (R >= a.rbase[a.n_seg] || tok >= a.n_tok) return;
+    const int r0 = 16 * rl + g;
+    const float *p = a.ws + (size_t)tile * a.splits * TC_BM * a.bn + c;
+    float y0 = 0.f, y1 = 0.f;
+    for (int k = 0; k < a.splits; ++k) {
+        y0 += __ldcg(p + ((size_t)k * TC_BM + r0) * a.bn);
+        y1 += __ldcg(p + ((size_t)k * TC_BM + r0 + 8) * a.bn);
+    }
+    int rt;
+    const int si = tc_seg_of(a, R, rt);
+    const float sc = __ldg(a.xscale + tok) * a.seg[si].wscale;
+    epi(si + a.seg_base, rt, g, tok, y0 * sc, y1 * sc);
 }
 
 // ------------------------------------------------------------------------------------------------ host launch
@@ -374,8 +441,12 @@ struct TcLaunch {
 // Fill `L` for the stacked matrices mats[0..n) (all of one K) against n_tok fp16 activation rows x16 (row stride
 // ldx elements, ldx >= K, 16-byte aligned rows).  Returns cudaErrorNotSupported when a matrix is not in a
 // tensor-core format (F32 tiles) or the formats do not form one kernel's pair (the caller then splits by matrix).
+struct TcSplitWs {
+    float *ws = nullptr;     // split-K partials
+    size_t ws_bytes = 0;
+};
 cudaError_t tc_setup(TcLaunch &L, const MatW *const *mats, int n, const __half *x16, int ldx, const float *xscale,
-                     int n_tok, int *status, int n_sm);
+                     int n_tok, int *status, int n_sm, const TcSplitWs *sk = nullptr);
 
 template <int FA, int FB, class Epi>
 cudaError_t tc_launch_t(const TcLaunch &L, const Epi &epi, cudaStream_t st) {
@@ -387,6 +458,10 @@ cudaError_t tc_launch_t(const TcLaunch &L, const Epi &epi, cudaStream_t st) {
         attr_set = true;
     }
     k_gemm_tc<FA, FB, Epi><<<L.grid, TC_THREADS, L.smem, st>>>(L.a, L.xmap, epi);
+    if (L.a.splits > 1) {
+        const int64_t n = (int64_t)L.a.m_tiles * L.a.n_tiles * 64 * L.a.bn;
+        k_tc_splitk_reduce<Epi><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(L.a, epi);
+    }
     return cudaGetLastError();
 }
 
@@ -404,13 +479,13 @@ cudaError_t tc_launch(const TcLaunch &L, const Epi &epi, cudaStream_t st) {
 // per matrix (the epilogue still receives the matrix index as its segment).
 template <class Epi>
 cudaError_t tc_gemm(const MatW *const *mats, int n, const __half *x16, int ldx, const float *xscale, int n_tok,
-                    int *status, int n_sm, const Epi &epi, cudaStream_t st) {
+                    int *status, int n_sm, const Epi &epi, cudaStream_t st, const TcSplitWs *sk = nullptr) {
     TcLaunch L;
-    cudaError_t e = tc_setup(L, mats, n, x16, ldx, xscale, n_tok, status, n_sm);
+    cudaError_t e = tc_setup(L, mats, n, x16, ldx, xscale, n_tok, status, n_sm, sk);
     if (e == cudaSuccess) return tc_launch(L, epi, st);
     if (e != cudaErrorNotSupported || n == 1) return e;
     for (int i = 0; i < n; ++i) {
-        e = tc_setup(L, mats + i, 1, x16, ldx, xscale, n_tok, status, n_sm);
+        e = tc_setup(L, mats + i, 1, x16, ldx, xscale, n_tok, status, n_sm, sk);
         if (e != cudaSuccess) return e;
         L.a.seg_base = i;
         e = tc_launch(L, epi, st);

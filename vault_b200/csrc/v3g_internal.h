@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "v3g.cuh"
+#include "v3g_gemm.cuh"
 #include "v3g_gemv.cuh"
 
 struct v3g_model {
@@ -39,6 +40,7 @@ struct PfBuf {
     float *feat = nullptr;   // [cap][feat_dim] segment-scorer features of every token
     float *hin = nullptr;    // [cap][feat_dim] habituated scorer inputs
     float *z = nullptr;      // [cap][2][seg_hidden] scorer fc1 outputs (raw, habituated)
+    v3g::TcSplitWs sk;       // split-K partials and tickets of the tensor-core GEMM
 };
 
 struct v3g_state {
@@ -105,6 +107,7 @@ cudaError_t launch_scorer(const v3g_model *m, v3g_state *s, cudaStream_t st);
 // batched decode step (B > 8) with every projection on the tensor-core GEMM (v3g_prefill.cu)
 cudaError_t launch_step_tc(const v3g_model *m, v3g_state *s, bool boundary, bool want_lm, cudaStream_t st);
 bool step_tc_supported(const v3g_model *m, const v3g_state *s);
+cudaError_t launch_step_attention(const v3g_model *m, v3g_state *s, int layer, cudaStream_t st);
 cudaError_t tc_init_attrs();
 // chunked prefill (v3g_prefill.cu)
 bool piece_supported(const v3g_model *m, const v3g_state *s);

@@ -251,10 +251,11 @@ struct TokGateUp {   // h[t, f] = silu(gate_f) * up_f  (src/vault_v3_model.py:11
 // (GQA).  Scores and P V run on the tensor cores (mma.sync m16n8k16): queries and probabilities enter as high + low
 // fp16 parts (about 22 significant bits), keys and values are the fp16 cache; online softmax in fp32.  Phase 1
 // scores the prefix (sinks, bank, previous chunk) with the queries rotated at W + c, phase 2 the current chunk's
-// keys 0..c with the queries rotated at c.
+// keys 0..c with the queries rotated at c.  p0 < 0: the batched decode step (n = 1), position read from the state.
 template <int D>
 __global__ void __launch_bounds__(256) k_prefill_attn(const StateDev *sp, int layer, float scale, int n, int64_t p0,
                                                       const float *Qc, const float *Qf, float *out) {
+    if (p0 < 0) p0 = __ldcg(&sp->step->pos);
     constexpr int KP = D + 8, NS = D / 16, NB = D / 8, TK = 64;
     extern __shared__ __align__(16) uint8_t smraw[];
     kv_t *Ks = reinterpret_cast<kv_t *>(smraw);   // [2][TK][KP]
@@ -420,21 +421,28 @@ __global__ void __launch_bounds__(256) k_prefill_attn(const StateDev *sp, int la
 
 template <int D>
 static cudaError_t launch_prefill_attn(const v3g_model *m, v3g_state *s, int layer, int n, int64_t p0,
-                                       cudaStream_t st) {
+                                       const float *qc, const float *qf, float *out, cudaStream_t st) {
     const size_t smem = (size_t)4 * 64 * (D + 8) * sizeof(kv_t);   // attribute set by tc_init_attrs
-    const PfBuf &pf = s->pf;
     dim3 grid((n + 15) / 16, m->host.G, s->B);
     k_prefill_attn<D><<<grid, 32 * (m->host.H / m->host.G), smem, st>>>(s->dev, layer, (float)(1.0 / sqrt((double)D)), n, p0,
-                                                                        pf.qc, pf.qf, pf.attn);
+                                                                        qc, qf, out);
     return cudaGetLastError();
 }
 
-static cudaError_t prefill_attention(const v3g_model *m, v3g_state *s, int layer, int n, int64_t p0, cudaStream_t st) {
+// n queries per sequence at positions p0.. (p0 < 0: one query at the state's position); queries and outputs default
+// to the prefill workspace
+static cudaError_t prefill_attention(const v3g_model *m, v3g_state *s, int layer, int n, int64_t p0, cudaStream_t st,
+                                     const float *qc = nullptr, const float *qf = nullptr, float *out = nullptr) {
+    if (!qc) {
+        qc = s->pf.qc;
+        qf = s->pf.qf;
+        out = s->pf.attn;
+    }
     switch (m->host.D) {
-        case 16: return launch_prefill_attn<16>(m, s, layer, n, p0, st);
-        case 32: return launch_prefill_attn<32>(m, s, layer, n, p0, st);
-        case 64: return launch_prefill_attn<64>(m, s, layer, n, p0, st);
-        case 128: return launch_prefill_attn<128>(m, s, layer, n, p0, st);
+        case 16: return launch_prefill_attn<16>(m, s, layer, n, p0, qc, qf, out, st);
+        case 32: return launch_prefill_attn<32>(m, s, layer, n, p0, qc, qf, out, st);
+        case 64: return launch_prefill_attn<64>(m, s, layer, n, p0, qc, qf, out, st);
+        case 128: return launch_prefill_attn<128>(m, s, layer, n, p0, qc, qf, out, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -514,26 +522,26 @@ cudaError_t launch_piece(const v3g_model *m, v3g_state *s, const int32_t *dev_id
         {
             const MatW *mats[3] = {&L.q, &L.k, &L.v};
             PieceQKV epi{m->dev, s->dev, l, n, p0, L.bq, L.bk, L.bv, pf.qc, pf.qf};
-            PF_TRY(tc_gemm(mats, 3, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st));
+            PF_TRY(tc_gemm(mats, 3, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st, &pf.sk));
         }
         PF_TRY(prefill_attention(m, s, l, n, p0, st));
         PF_TRY(tc_prep(pf.attn, HD, T, HD, nullptr, 0.f, pf.x16, pf.ldx16, pf.xscale, st));
         {
             const MatW *mats[1] = {&L.o};
             TokResid epi{pf.x, md.d, md.d};
-            PF_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st));
+            PF_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st, &pf.sk));
         }
         PF_TRY(tc_prep(pf.x, md.d, T, md.d, L.ln2, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
         {
             const MatW *mats[1] = {&L.gu};
             TokGateUp epi{pf.h, md.F};
-            PF_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st));
+            PF_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st, &pf.sk));
         }
         PF_TRY(tc_prep(pf.h, md.F, T, md.F, nullptr, 0.f, pf.x16, pf.ldx16, pf.xscale, st));
         {
             const MatW *mats[1] = {&L.down};
             TokResid epi{pf.x, md.d, md.d};
-            PF_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st));
+            PF_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st, &pf.sk));
         }
     }
     if (any_seg) {
@@ -580,26 +588,26 @@ cudaError_t launch_step_tc(const v3g_model *m, v3g_state *s, bool boundary, bool
         {
             const MatW *mats[3] = {&L.q, &L.k, &L.v};
             PieceQKV epi{m->dev, s->dev, l, 1, -1, L.bq, L.bk, L.bv, sd.q_cur, sd.q_far};
-            TS_TRY(tc_gemm(mats, 3, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st));
+            TS_TRY(tc_gemm(mats, 3, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st, &pf.sk));
         }
         TS_TRY(launch_attention(m, s, l, false, st));
         TS_TRY(tc_prep(sd.attn, HD, B, HD, nullptr, 0.f, pf.x16, pf.ldx16, pf.xscale, st));
         {
             const MatW *mats[1] = {&L.o};
             TokResid epi{sd.x, md.d, md.d};
-            TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st));
+            TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st, &pf.sk));
         }
         TS_TRY(tc_prep(sd.x, md.d, B, md.d, L.ln2, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
         {
             const MatW *mats[1] = {&L.gu};
             TokGateUp epi{sd.hbuf, md.F};
-            TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st));
+            TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st, &pf.sk));
         }
         TS_TRY(tc_prep(sd.hbuf, md.F, B, md.F, nullptr, 0.f, pf.x16, pf.ldx16, pf.xscale, st));
         {
             const MatW *mats[1] = {&L.down};
             TokResid epi{sd.x, md.d, md.d};
-            TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st));
+            TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st, &pf.sk));
         }
     }
     if (any_seg) TS_TRY(launch_scorer(m, s, st));
@@ -607,11 +615,16 @@ cudaError_t launch_step_tc(const v3g_model *m, v3g_state *s, bool boundary, bool
         TS_TRY(tc_prep(sd.x, md.d, B, md.d, md.norm, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
         const MatW *mats[1] = {&md.embed};
         TokStore epi{sd.logits, md.vocab, md.vocab};
-        TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st));
+        TS_TRY(tc_gemm(mats, 1, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st, &pf.sk));
     }
     TS_TRY(launch_argmax_finish(m, s, want_lm, false, st));
 #undef TS_TRY
     return cudaSuccess;
+}
+
+// the decode attention of `layer` as the state's step runs it (kernel-level timing entry v3g_attention)
+cudaError_t launch_step_attention(const v3g_model *m, v3g_state *s, int layer, cudaStream_t st) {
+    return launch_attention(m, s, layer, false, st);
 }
 
 bool step_tc_supported(const v3g_model *m, const v3g_state *s) {
