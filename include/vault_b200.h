@@ -66,8 +66,10 @@ enum {
     V3G_STATE_NO_GRAPHS = 4,      /* launch kernels directly instead of replaying captured CUDA graphs */
     V3G_STATE_NO_PERSISTENT = 8,  /* run a step as one GEMV kernel per layer phase (8 batch rows per pass) instead of
                                      the persistent kernel (batch <= 8) or the tensor-core GEMM step (batch > 8) */
-    V3G_STATE_TOKEN_PREFILL = 16  /* v3g_prefill streams the prompt one decode step per token instead of the chunked
+    V3G_STATE_TOKEN_PREFILL = 16, /* v3g_prefill streams the prompt one decode step per token instead of the chunked
                                      tensor-core prefill */
+    V3G_STATE_FP16_ACTIVATIONS = 32 /* decode GEMVs take each activation as one fp16 part (11 bits) instead of a high
+                                       and a low part (about 22 bits) at batch <= 4: faster, less precise */
 };
 
 typedef struct v3g_model v3g_model;

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(HERE, "libvault_b200.so")
 V3G_OK = 0
 V3G_STATE_PER_SEQ_MEMORY, V3G_STATE_NO_AUTOPIN, V3G_STATE_NO_GRAPHS, V3G_STATE_NO_PERSISTENT = 1, 2, 4, 8
 V3G_STATE_TOKEN_PREFILL = 16
+V3G_STATE_FP16_ACTIVATIONS = 32
 V3G_STATUS_RESONANCE, V3G_STATUS_BOUNDS, V3G_STATUS_TIMEOUT = 1, 2, 4
 # codes -1..-12 are the file-validation codes of runtime/vault3.h:35-49
 FILE_ERRORS = set(range(-12, 0)) - {-8}

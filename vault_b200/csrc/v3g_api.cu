@@ -646,6 +646,7 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
     s->seg_budget = batch_mode_ref ? 0 : budget;
     s->use_graphs = (flags & V3G_STATE_NO_GRAPHS) ? 0 : 1;
     s->chunked_prefill = (flags & V3G_STATE_TOKEN_PREFILL) ? 0 : 1;
+    s->act_single = (flags & V3G_STATE_FP16_ACTIVATIONS) ? 1 : 0;
     StateDev &sd = s->host;
     memset(&sd, 0, sizeof(sd));
     uint8_t *A = s->arena;

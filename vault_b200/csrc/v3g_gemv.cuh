@@ -34,6 +34,7 @@ struct GemvArgs {
     int kpx;          // padded K + 8 (kept for the host plan; the converted activations use nblk 32-blocks)
     int nblk;         // 32-wide blocks of the padded K (block sums)
     int B;            // batch rows in this pass (<= GEMV_MB)
+    int lo;           // tensor-core column of the first low activation part (gemv_lo), 0: one fp16 part per row
     int b0;           // first batch row of this pass
     int wk;           // warps per row tile
     const float *x;   // fp32 activations, row b at x + (b0 + b) * x_ld
@@ -50,20 +51,19 @@ __host__ __device__ constexpr bool fmt_int(int fmt) { return fmt == FMT_Q8 || fm
 // Activation precision.  A batch of B <= 4 rows leaves tensor-core columns free, so every activation row enters as
 // two fp16 parts -- high part x_h = fp16(x), low part x_l = fp16(x - x_h), about 22 significant bits together --
 // in columns b (high) and P + b (low), P = 1, 2 or 4; the two columns are added after the tensor core.  Larger
-// batches keep one fp16 part per row (11 bits).  gemv_lo(B) = P (0: no low parts), gemv_xrows(B) = record rows.
+// batches keep one fp16 part per row (11 bits); a state may also ask for one part at any batch (GemvArgs::lo = 0).
+// gemv_lo(B) = P (0: no low parts), gemv_xrows(B, P) = record rows.
 __host__ __device__ constexpr int gemv_lo(int B) { return B == 1 ? 1 : (B == 2 ? 2 : (B <= 4 ? 4 : 0)); }
-__host__ __device__ constexpr int gemv_xrows(int B) { return gemv_lo(B) ? 2 * gemv_lo(B) : B; }
+__host__ __device__ constexpr int gemv_xrows(int B, int P) { return P ? 2 * P : B; }
 // record row read by the lanes of tensor-core column g: its own row when it holds data, else row 0 (the columns of
 // absent rows are computed and never read)
-__device__ __forceinline__ int gemv_rec_row(int B, int g) {
-    const int P = gemv_lo(B);
+__device__ __forceinline__ int gemv_rec_row(int B, int P, int g) {
     if (P) return (g < 2 * P && (g & (P - 1)) < B) ? g : 0;
     return g < B ? g : 0;
 }
 // add the low-part columns into the high-part columns of a lane's accumulators (rows g, g+8 x columns 2t, 2t+1);
 // every lane of the warp must call it together
-__device__ __forceinline__ void gemv_fold_lo(int B, float (&acc)[4]) {
-    const int P = gemv_lo(B);
+__device__ __forceinline__ void gemv_fold_lo(int P, float (&acc)[4]) {
     if (P == 1) {
         acc[0] += acc[1];
         acc[2] += acc[3];
@@ -247,7 +247,7 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
     const bool norm = a.prologue == PRO_RMSNORM;
     const bool vec = (a.K & 31) == 0 && (a.x_ld & 3) == 0;
     const int nb = (a.K + 31) >> 5, nq = 4 * nb, items = a.B * nq;
-    const int xr = gemv_xrows(a.B), lo = gemv_lo(a.B);
+    const int xr = gemv_xrows(a.B, a.lo), lo = a.lo;
     const float *nwp = nw_s ? nw_s : a.norm_w;
     const float inv_k = 1.0f / (float)a.K;
     float ss[GEMV_MB], mx[GEMV_MB];
@@ -462,7 +462,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     if (active) {
         const int g = lane >> 2;
-        const XFrag xf{reinterpret_cast<const uint4 *>(xs) + gemv_rec_row(a.B, g) * 4 + (lane & 3), 4 * gemv_xrows(a.B)};
+        const XFrag xf{reinterpret_cast<const uint4 *>(xs) + gemv_rec_row(a.B, a.lo, g) * 4 + (lane & 3),
+                       4 * gemv_xrows(a.B, a.lo)};
         if (si == 0) stream_tiles<FA>(pre, tp, k0, nkt, xf, bsum, lane, acc);
         else stream_tiles<FB>(pre, tp, k0, nkt, xf, bsum, lane, acc);
     }
@@ -481,7 +482,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
         }
     }
     if (active && kw == 0) {
-        gemv_fold_lo(a.B, acc);
+        gemv_fold_lo(a.lo, acc);
         const int g = lane >> 2, t = lane & 3;
         const int sg = si + a.seg_base;
         const float ws = a.seg[si].wscale;
@@ -498,7 +499,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, Epi epi)
 
 inline size_t gemv_smem_bytes(const GemvArgs &a, bool bsum) {
     return (136 + GEMV_MB + 8 * 32 * 4 + (bsum ? a.nblk * GEMV_MB : 0)) * sizeof(float) +
-           (size_t)gemv_xrows(a.B) * a.nblk * 64;
+           (size_t)gemv_xrows(a.B, a.lo) * a.nblk * 64;
 }
 
 // Host helper: choose the k split so the launch covers the GPU, fill the launch parameters.

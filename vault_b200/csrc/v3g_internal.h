@@ -72,6 +72,7 @@ struct v3g_state {
     PfBuf pf;
     int chunked_prefill = 1;         // v3g_prefill runs window-aligned pieces through the tensor-core GEMMs
     int use_tc_step = 0;             // batch > 8: decode steps run their projections on the tensor-core GEMM
+    int act_single = 0;              // GEMV activations as one fp16 part (V3G_STATE_FP16_ACTIVATIONS)
     std::string last_error;
 };
 

@@ -488,7 +488,7 @@ __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkR
                                            int n_phases, int p, int cta, int G, int wi, const uint4 *xq,
                                            const float *bq, const float *s_scale, MkPart &part, int *status,
                                            int lane) {
-    const int t = lane & 3, B = P.a.B, xbs = 4 * gemv_xrows(B);
+    const int t = lane & 3, B = P.a.B, xbs = 4 * gemv_xrows(B, P.a.lo);
     const float sc0 = 2 * t < B ? s_scale[2 * t] : 0.f, sc1 = 2 * t + 1 < B ? s_scale[2 * t + 1] : 0.f;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     int cur_si = -1, cur_r = -1;
@@ -497,7 +497,7 @@ __device__ __forceinline__ void mk_consume(const MkPhase &P, const Epi &epi, MkR
     mk_range(lite[p], wi, t0w, t1w);
     if (lane == 0) part.head_row[wi] = t0w < t1w ? -1 : -2;
     auto flush = [&]() {   // the finished piece of row tile (cur_si, cur_r)
-        gemv_fold_lo(B, acc);
+        gemv_fold_lo(P.a.lo, acc);
         const float ws = P.a.seg[cur_si].wscale, s0 = sc0 * ws, s1 = sc1 * ws;
         const float y0 = acc[0] * s0, y1 = acc[1] * s1, y2 = acc[2] * s0, y3 = acc[3] * s1;
         const int KT = P.a.seg[cur_si].n_ktiles;
@@ -836,7 +836,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
                 asm volatile("cp.async.commit_group;" ::: "memory");
             }
             const int g = lane >> 2, t = lane & 3;
-            const uint4 *xq = reinterpret_cast<const uint4 *>(xs) + gemv_rec_row(P.a.B, g) * 4 + t;
+            const uint4 *xq = reinterpret_cast<const uint4 *>(xs) + gemv_rec_row(P.a.B, P.a.lo, g) * 4 + t;
             mk_consume_epi<FA, FB>(P, mp, misc, R, lite, n_phases, p, c, G, warp, xq, bsum + 2 * t, s_scale, part,
                                    status, lane);
         }

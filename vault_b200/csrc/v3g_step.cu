@@ -484,6 +484,7 @@ static cudaError_t launch_gemv_t(const v3g_model *m, GemvCall c, const Epi &epi,
     for (int b0 = 0; b0 < Btot; b0 += GEMV_MB) {
         c.a.b0 = b0;
         c.a.B = Btot - b0 < GEMV_MB ? Btot - b0 : GEMV_MB;
+        c.a.lo = c.a.lo == 0 ? 0 : -1;   // one part stays one part; otherwise re-planned for this pass
         int grid;
         size_t smem;
         gemv_plan(c.a, c.fmts, m->n_sm, grid, smem);
@@ -538,6 +539,7 @@ static GemvCall gemv_args(const MatW *const *mats, int n, const float *x, int x_
         c.fmts[i] = mats[i]->fmt;
     }
     c.a.K = K;
+    c.a.lo = -1;   // gemv_plan picks the activation split for the pass's batch
     c.a.x = x;
     c.a.x_ld = x_ld;
     c.a.prologue = prologue;
@@ -655,6 +657,7 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
         GemvCall c = gemv_args(mats, n, x, x_ld, K, prologue, norm_w, md.rms_eps);
         c.a.B = s->B;
         c.a.b0 = 0;
+        if (s->act_single) c.a.lo = 0;
         int grid;
         size_t smem;
         gemv_plan(c.a, c.fmts, m->n_sm, grid, smem);
@@ -674,7 +677,7 @@ cudaError_t build_mega(const v3g_model *m, v3g_state *s) {
         ok = ok && tb < (int64_t)1 << 30;
         p.tbase[n] = (int)tb;
         max_rt = rb > max_rt ? rb : max_rt;
-        const size_t need = (size_t)(144 + (bs ? c.a.nblk * GEMV_MB : 0)) * 4 + (size_t)gemv_xrows(s->B) * c.a.nblk * 64;
+        const size_t need = (size_t)(144 + (bs ? c.a.nblk * GEMV_MB : 0)) * 4 + (size_t)gemv_xrows(s->B, c.a.lo) * c.a.nblk * 64;
         xr = need > xr ? need : xr;
         p.kind = MK_GEMV;
         p.epi = epi;
@@ -936,6 +939,7 @@ cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool wa
                     a.a.feat_ld = sd.feat_dim;
                 }
             EpiQKV epi{mdv, sdv, l, L.bq, L.bk, L.bv};
+            if (s->act_single) a.a.lo = 0;
             V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
         }
         V3G_TRY(launch_attention(m, s, l, pdl, st));
@@ -943,18 +947,21 @@ cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool wa
             const MatW *mats[1] = {&L.o};
             GemvCall a = gemv_args(mats, 1, sd.attn, md.H * md.D, md.H * md.D, PRO_PLAIN, nullptr, 0.f);
             EpiResid epi{sd.x, md.d, md.d};
+            if (s->act_single) a.a.lo = 0;
             V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
         }
         {
             const MatW *mats[1] = {&L.gu};
             GemvCall a = gemv_args(mats, 1, sd.x, md.d, md.d, PRO_RMSNORM, L.ln2, md.rms_eps);
             EpiGateUp epi{sd.hbuf, md.F};
+            if (s->act_single) a.a.lo = 0;
             V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
         }
         {
             const MatW *mats[1] = {&L.down};
             GemvCall a = gemv_args(mats, 1, sd.hbuf, md.F, md.F, PRO_PLAIN, nullptr, 0.f);
             EpiResid epi{sd.x, md.d, md.d};
+            if (s->act_single) a.a.lo = 0;
             V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
         }
     }
@@ -963,6 +970,7 @@ cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool wa
         const MatW *mats[1] = {&md.embed};
         GemvCall a = gemv_args(mats, 1, sd.x, md.d, md.d, PRO_RMSNORM, md.norm, md.rms_eps);
         EpiStore epi{sd.logits, md.vocab, md.vocab};
+        if (s->act_single) a.a.lo = 0;
         V3G_TRY(run_gemv(m, a, epi, B, st, pdl));
     }
     V3G_TRY(launch_argmax_finish(m, s, want_lm, pdl, st));

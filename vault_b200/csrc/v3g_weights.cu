@@ -267,6 +267,7 @@ int dequant_matrix(const MatW &w, int head_dim, float *out, cudaStream_t st) {
 }
 
 void gemv_plan(GemvArgs &a, const int *fmts, int n_sm, int &grid, size_t &smem) {
+    if (a.lo < 0) a.lo = gemv_lo(a.B);   // default: two fp16 parts per activation when the batch leaves columns free
     int maxk = 0, kpad = 0;
     bool bsum = false;
     a.total_rtiles = 0;

@@ -32,7 +32,7 @@ class VAULTv3State:
 
     def __init__(self, model: "VAULTv3ForCausalLM", batch: int = 1, seg_budget: Optional[int] = None,
                  per_sequence_memory: bool = False, auto_pin: bool = True, graphs: bool = True,
-                 persistent: bool = True, chunked_prefill: bool = True):
+                 persistent: bool = True, chunked_prefill: bool = True, fp16_activations: bool = False):
         self.model = model
         self.batch = int(batch)
         cfg = model.cfg
@@ -48,7 +48,8 @@ class VAULTv3State:
         flags = (_lib.V3G_STATE_PER_SEQ_MEMORY if per_sequence_memory else 0) | \
                 (0 if auto_pin else _lib.V3G_STATE_NO_AUTOPIN) | (0 if graphs else _lib.V3G_STATE_NO_GRAPHS) | \
                 (0 if persistent else _lib.V3G_STATE_NO_PERSISTENT) | \
-                (0 if chunked_prefill else _lib.V3G_STATE_TOKEN_PREFILL)
+                (0 if chunked_prefill else _lib.V3G_STATE_TOKEN_PREFILL) | \
+                (_lib.V3G_STATE_FP16_ACTIVATIONS if fp16_activations else 0)
         h = C.c_void_p()
         with torch.cuda.device(model.device):
             _lib.check(L.v3g_state_init(C.byref(h), model._h, C.c_void_p(self.arena.data_ptr()), int(size),
