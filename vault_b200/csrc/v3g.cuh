@@ -149,6 +149,10 @@ struct StateDev {
     unsigned int *bar;           // grid-barrier counter of the persistent decode kernel (zeroed every step)
 };
 
+constexpr int KIND_KROT = 0, KIND_KRAW = 1, KIND_V = 2;   // ring kinds
+constexpr int SINK_KRAW = 0, SINK_KROT = 1, SINK_V = 2;   // sink kinds
+constexpr int BANK_KRAW = 0, BANK_V = 1;                  // bank kinds
+
 __device__ __forceinline__ uint64_t ring_off(const StateDev &s, int par, int kind, int g, int t) {
     return s.off_ring + (uint64_t)par * s.ring_par_stride + (uint64_t)kind * s.ring_kind_stride +
            ((uint64_t)g * s.W + t) * s.D * 2ull;

@@ -540,7 +540,7 @@ struct Layout {
         off_cnt, off_logits, off_amax, off_scz, off_bar;
     // chunked-prefill workspace: pf_cap tokens
     uint64_t off_pf_x, off_pf_qc, off_pf_qf, off_pf_attn, off_pf_h, off_pf_x16, off_pf_xs, off_pf_feat, off_pf_hin,
-        off_pf_z, off_pf_skws;
+        off_pf_z, off_pf_stat, off_pf_skws;
     int pf_cap, pf_ldx16;
     uint64_t total;
     int max_splits, seg_cap, feat_dim;
@@ -607,6 +607,7 @@ Layout make_layout(const ModelDev &md, int B, int seg_cap) {
     L.off_pf_feat = take(T * fdim * 4);
     L.off_pf_hin = take(T * fdim * 4);
     L.off_pf_z = take(T * 2 * std::max(1, md.seg_hidden) * 4);
+    L.off_pf_stat = take(T * 16);
     L.off_pf_skws = take(TC_SPLITK_WS_BYTES);
     L.total = cur;
     return L;
@@ -694,6 +695,7 @@ extern "C" int v3g_state_init(v3g_state **out, const v3g_model *m, void *dev_are
     s->pf.feat = reinterpret_cast<float *>(A + L.off_pf_feat);
     s->pf.hin = reinterpret_cast<float *>(A + L.off_pf_hin);
     s->pf.z = reinterpret_cast<float *>(A + L.off_pf_z);
+    s->pf.stat = reinterpret_cast<float4 *>(A + L.off_pf_stat);
     s->pf.sk.ws = reinterpret_cast<float *>(A + L.off_pf_skws);
     s->pf.sk.ws_bytes = TC_SPLITK_WS_BYTES;
     if (cudaSetDevice(m->device) != cudaSuccess || cudaMalloc(&s->dev, sizeof(StateDev)) != cudaSuccess ||

@@ -51,10 +51,80 @@ __global__ void __launch_bounds__(256) k_tc_prep(const float *x, int64_t ld_x, i
     if (tid == 0) xscale[r] = __int_as_float((127 + e) << 23);
 }
 
+// The same operand for K a multiple of 4 and at most 1024 NV: the row is read once with 16-byte loads and held in
+// registers (NV float4 per thread) for both the statistics and the conversion; 8-byte fp16 stores.
+template <int NV>
+__global__ void __launch_bounds__(256) k_tc_prep_v(const float *x, int64_t ld_x, int K, const float *norm_w,
+                                                   float eps, __half *out, int ldo, float *xscale) {
+    const int r = blockIdx.x, tid = threadIdx.x, K4 = K >> 2;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)r * ld_x);
+    const float4 *wr = reinterpret_cast<const float4 *>(norm_w);
+    __shared__ float red[2][8];
+    float4 v[NV];
+    float ss = 0.f, mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int q = tid + 256 * i;
+        v[i] = q < K4 ? xr[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (norm_w && q < K4) {
+            const float4 w = __ldg(wr + q);
+            ss = fmaf(v[i].x, v[i].x, ss);
+            ss = fmaf(v[i].y, v[i].y, ss);
+            ss = fmaf(v[i].z, v[i].z, ss);
+            ss = fmaf(v[i].w, v[i].w, ss);
+            v[i].x *= w.x;
+            v[i].y *= w.y;
+            v[i].z *= w.z;
+            v[i].w *= w.w;
+        }
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
+    ss = warp_sum(ss);
+    mx = warp_max(mx);
+    if ((tid & 31) == 0) {
+        red[0][tid >> 5] = ss;
+        red[1][tid >> 5] = mx;
+    }
+    __syncthreads();
+    float S = 0.f, M = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        S += red[0][w];
+        M = fmaxf(M, red[1][w]);
+    }
+    const float inv = norm_w ? rsqrtf(S / (float)K + eps) : 1.f;
+    const int be = (__float_as_int(M * inv) >> 23) & 0xff;
+    int e = be > 0 ? be - 140 : 0;
+    e = e < -126 ? -126 : (e > 126 ? 126 : e);
+    const float mul = inv * __int_as_float((127 - e) << 23);
+    uint2 *o = reinterpret_cast<uint2 *>(out + (int64_t)r * ldo);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int q = tid + 256 * i;
+        if (q < K4) {
+            const __half2 lo = __floats2half2_rn(v[i].x * mul, v[i].y * mul);
+            const __half2 hi = __floats2half2_rn(v[i].z * mul, v[i].w * mul);
+            o[q] = make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+        }
+    }
+    for (int q = K4 + tid; q < (ldo >> 2); q += 256) o[q] = make_uint2(0u, 0u);   // zero padding up to ldo
+    if (tid == 0) xscale[r] = __int_as_float((127 + e) << 23);
+}
+
 cudaError_t tc_prep(const float *x, int64_t ld_x, int n, int K, const float *norm_w, float eps, __half *out, int ldo,
                     float *xscale, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    k_tc_prep<<<n, 256, 0, st>>>(x, ld_x, K, norm_w, eps, out, ldo, xscale);
+    const bool vec = K % 4 == 0 && ld_x % 4 == 0 && ldo % 4 == 0 && ((uintptr_t)x & 15) == 0 &&
+                     ((uintptr_t)norm_w & 15) == 0 && ((uintptr_t)out & 7) == 0;
+    const int nv = (K / 4 + 255) / 256;
+    if (vec && nv <= 2)
+        k_tc_prep_v<2><<<n, 256, 0, st>>>(x, ld_x, K, norm_w, eps, out, ldo, xscale);
+    else if (vec && nv <= 4)
+        k_tc_prep_v<4><<<n, 256, 0, st>>>(x, ld_x, K, norm_w, eps, out, ldo, xscale);
+    else if (vec && nv <= 9)
+        k_tc_prep_v<9><<<n, 256, 0, st>>>(x, ld_x, K, norm_w, eps, out, ldo, xscale);
+    else
+        k_tc_prep<<<n, 256, 0, st>>>(x, ld_x, K, norm_w, eps, out, ldo, xscale);
     return cudaGetLastError();
 }
 
@@ -179,6 +249,12 @@ struct TcEpiStore {
             y[tok * ld + src * src_rows + row] = y0;
         if (map_tile_row(rowmap, head_dim, src_rows, TILE_ROWS * rt + g + 8, src, row))
             y[tok * ld + src * src_rows + row] = y1;
+    }
+    template <int N>
+    __device__ void chunk(int seg, int rt, int g, int tok0, int nv, const float (&y0)[N], const float (&y1)[N]) const {
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if (j < nv) (*this)(seg, rt, g, tok0 + j, y0[j], y1[j]);
     }
 };
 

@@ -23,6 +23,11 @@
 //               column by its activation scale and the matrix's weight scale, and hand (row g, row g+8) pairs of a
 //               16-row tile to the fused epilogue -- the partners of the RoPE / gate-up row order sit 8 lanes apart;
 //               then release the accumulator buffer (`acc_empty`).
+// An epilogue functor provides
+//   chunk(seg, rt, g, tok0, nv, y0[8], y1[8])     tokens tok0 .. tok0 + nv - 1 of rows (g, g + 8) of row tile rt
+//   operator()(seg, rt, g, tok, y0, y1)           one token (the split-K reduction)
+// chunk() issues its global reads for all nv tokens before its first write: the reads cannot be reordered across
+// the writes by the compiler (they may alias), so a per-token loop would pay one L2 round trip per token.
 // Few output tiles (small batches) split K over up to 16 CTAs per tile: each split writes an fp32 partial, and a
 // second kernel over all (row pair, token) outputs adds the splits in order (deterministic) and runs the epilogue.
 // Every wait is bounded: a wait that runs out records status bit 4 (timeout) and its role stops.
@@ -39,6 +44,7 @@ constexpr int TC_BM = 128;            // weight rows per CTA tile (8 row tiles)
 constexpr int TC_BK = 64;             // k per stage (one 128-byte swizzled row)
 constexpr int TC_CONV_WARPS = 8;      // one per row tile of the CTA tile
 constexpr int TC_THREADS = 32 * (2 + TC_CONV_WARPS + 4);   // producer, MMA, converters, 4 epilogue warps
+constexpr int TC_EPI_CHUNK = 8;   // tokens per epilogue chunk() call
 constexpr int TC_RAW_ROW = 2048;      // stored weight bytes of one row tile per stage (16-bit tiles: 4 x 512)
 constexpr int TC_MAX_STAGES = 4;
 constexpr int TC_TMEM_COLS = 512;
@@ -348,44 +354,49 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             }
             tc::tc_fence_after();
             const int R = mt * 8 + (row >> 4), tr = row & 15;
-            const bool live = R < total_rt && tr < 8;
+            const int g = tr & 7, hi = tr >> 3;   // lanes g and g + 8 hold the row pair (g, g + 8)
+            const bool live = R < total_rt;
             int rt = 0, si = 0;
-            if (R < total_rt) si = tc_seg_of(a, R, rt);
+            if (live) si = tc_seg_of(a, R, rt);
             const float ws = a.seg[si].wscale;
             const int tile = mt * a.n_tiles + nt;
             if (a.splits == 1) {
+                // per 16 token columns, lane g takes tokens 0-7 and lane g + 8 tokens 8-15 of the row pair
+                // (g, g + 8): each swaps the other half with its partner, and the epilogue gets 8 tokens at once,
+                // so that it can issue all of its global reads before its first write
                 for (int c0 = 0; c0 < a.bn; c0 += 16) {
                     uint32_t v[16];
                     tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * a.bn + c0), v);
                     tc::tmem_ld_wait();
+                    const int tok0 = nt * a.bn + c0 + 8 * hi;
+                    const int nv = min(TC_EPI_CHUNK, a.n_tok - tok0);
+                    float y0[TC_EPI_CHUNK], y1[TC_EPI_CHUNK];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float y = __uint_as_float(v[j]);
-                        const float yp = __shfl_xor_sync(0xffffffffu, y, 8);
-                        const int tok = nt * a.bn + c0 + j;
-                        if (live && tok < a.n_tok) {
-                            const float sc = __ldg(a.xscale + tok) * ws;
-                            epi(si + a.seg_base, rt, tr, tok, y * sc, yp * sc);
-                        }
+                    for (int j = 0; j < TC_EPI_CHUNK; ++j) {
+                        const float lo_v = __uint_as_float(v[j]), hi_v = __uint_as_float(v[j + 8]);
+                        const float keep = hi ? hi_v : lo_v;
+                        const float recv = __shfl_xor_sync(0xffffffffu, hi ? lo_v : hi_v, 8);
+                        const float sc = j < nv ? __ldg(a.xscale + tok0 + j) * ws : 0.f;
+                        y0[j] = (hi ? recv : keep) * sc;
+                        y1[j] = (hi ? keep : recv) * sc;
                     }
+                    if (live && nv > 0) epi.chunk(si + a.seg_base, rt, g, tok0, nv, y0, y1);
                 }
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(ACCE(buf));
                 continue;
             }
-            // split-K: this split's fp32 partial goes to the workspace ([tile][split][128 rows][bn columns]); the
-            // reduction kernel (k_tc_splitk_reduce) adds the splits in order and runs the epilogue
-            float *part = a.ws + (((size_t)tile * a.splits + sp) * TC_BM + row) * a.bn;
+            // split-K: this split's fp32 partial goes to the workspace ([tile][split][bn columns][128 rows], so a
+            // warp writes 128 contiguous bytes per column); k_tc_splitk_reduce adds the splits in order and runs
+            // the epilogue
+            float *part = a.ws + ((size_t)tile * a.splits + sp) * TC_BM * a.bn + row;
             for (int c0 = 0; c0 < a.bn; c0 += 16) {
                 uint32_t v[16];
                 tc::tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * a.bn + c0), v);
                 tc::tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 16; j += 4)
-                    __stcg(reinterpret_cast<float4 *>(part + c0 + j),
-                           make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
-                                       __uint_as_float(v[j + 3])));
+                for (int j = 0; j < 16; ++j) __stcg(part + (size_t)(c0 + j) * TC_BM, __uint_as_float(v[j]));
             }
             tc::tc_fence_before();
             __syncwarp();
@@ -401,26 +412,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     }
 }
 
-// split-K reduction: one thread per (output tile, row pair (g, g+8) of a 16-row tile, token column): the splits'
-// partials summed in split order, then the fused epilogue of the pair
+// split-K reduction: one thread per (output tile, token column, row pair (g, g+8) of a 16-row tile), the row pairs
+// fastest so that a warp reads and writes contiguous rows: the splits' partials summed in split order (deterministic),
+// then the fused epilogue of the pair
 template <class Epi>
 __global__ void __launch_bounds__(256) k_tc_splitk_reduce(const __grid_constant__ TcArgs a, Epi epi) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t n = (int64_t)a.m_tiles * a.n_tiles * 64 * a.bn;
     if (idx >= n) return;
-    const int c = (int)(idx % a.bn);
-    const int pair = (int)((idx / a.bn) % 64);
+    const int pair = (int)(idx & 63);
+    const int c = (int)((idx >> 6) % a.bn);
     const int tile = (int)(idx / ((int64_t)a.bn * 64));
     const int mt = tile / a.n_tiles, nt = tile - mt * a.n_tiles;
     const int rl = pair >> 3, g = pair & 7;
     const int R = mt * 8 + rl, tok = nt * a.bn + c;
     if (R >= a.rbase[a.n_seg] || tok >= a.n_tok) return;
     const int r0 = 16 * rl + g;
-    const float *p = a.ws + (size_t)tile * a.splits * TC_BM * a.bn + c;
+    const float *p = a.ws + (size_t)tile * a.splits * TC_BM * a.bn + (size_t)c * TC_BM + r0;
+    const size_t split_stride = (size_t)TC_BM * a.bn;
     float y0 = 0.f, y1 = 0.f;
     for (int k = 0; k < a.splits; ++k) {
-        y0 += __ldcg(p + ((size_t)k * TC_BM + r0) * a.bn);
-        y1 += __ldcg(p + ((size_t)k * TC_BM + r0 + 8) * a.bn);
+        y0 += __ldcg(p + k * split_stride);
+        y1 += __ldcg(p + k * split_stride + 8);
     }
     int rt;
     const int si = tc_seg_of(a, R, rt);

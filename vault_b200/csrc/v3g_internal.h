@@ -40,6 +40,7 @@ struct PfBuf {
     float *feat = nullptr;   // [cap][feat_dim] segment-scorer features of every token
     float *hin = nullptr;    // [cap][feat_dim] habituated scorer inputs
     float *z = nullptr;      // [cap][2][seg_hidden] scorer fc1 outputs (raw, habituated)
+    float4 *stat = nullptr;  // [cap] scorer LayerNorm statistics (means raw / habituated, inverse deviations)
     v3g::TcSplitWs sk;       // split-K partials and tickets of the tensor-core GEMM
 };
 

@@ -29,6 +29,27 @@
 
 namespace v3g {
 
+// Optional timeline of the persistent kernel (compile with -DV3G_MK_TRACE): per phase and CTA, %globaltimer at the
+// phase start, after the activation prologue, after the phase's work and after the grid barrier; plus the time the
+// producer issued its first copy of the phase.  Read back with v3g_mk_trace_read.
+#ifdef V3G_MK_TRACE
+constexpr int MK_TRACE_PH = 512, MK_TRACE_CTA = 160;
+__device__ unsigned long long g_mk_trace[MK_TRACE_PH][MK_TRACE_CTA][5];
+__device__ __forceinline__ unsigned long long mk_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+#define MK_TRACE(p, ev)                                                                    \
+    do {                                                                                   \
+        if ((p) < MK_TRACE_PH && blockIdx.x < MK_TRACE_CTA) g_mk_trace[p][blockIdx.x][ev] = mk_now(); \
+    } while (0)
+#else
+#define MK_TRACE(p, ev) \
+    do {                \
+    } while (0)
+#endif
+
 enum : int { MK_GEMV = 0, MK_ATTN = 1 };
 enum : int { MK_EPI_QKV = 0, MK_EPI_RESID = 1, MK_EPI_GATEUP = 2, MK_EPI_STORE = 3 };
 constexpr int MK_WARPS = GEMV_THREADS / 32;            // consumer warps
@@ -651,6 +672,9 @@ __device__ __forceinline__ void mk_produce(const MkLite *lite, int n_phases, int
     mk_enter(lite, n_phases, lane, cur, 0);
     uint32_t slot = 0, round = 0, idle = 0;
     const uint64_t pol = l2_evict_first();
+#ifdef V3G_MK_TRACE
+    int traced = -1;
+#endif
     while (cur.p < n_phases) {
         if (round > 0 && !mbar_test(empty + slot * 8, (round - 1) & 1u)) {   // slot still in use
             if (++idle > MK_WAIT_LIMIT) {
@@ -667,6 +691,12 @@ __device__ __forceinline__ void mk_produce(const MkLite *lite, int n_phases, int
             continue;
         }
         hush = 0;
+#ifdef V3G_MK_TRACE
+        if (lane == 0 && cur.p != traced) {
+            traced = cur.p;
+            MK_TRACE(cur.p, 4);
+        }
+#endif
         const int n = mk_chunk_n(cur);
         const int tb = tile_bytes(cur.fmt);
         bulk_load(buf + slot * MK_SLOT_BYTES, cur.tiles + (size_t)cur.tl * tb, (uint32_t)(n * tb), full + slot * 8, pol);
@@ -801,6 +831,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
     float *bsum = s_scale + GEMV_MB;
     for (int p = 0; p < n_phases; ++p) {
         const MkPhase &P = ph_s[p & 1];
+        if (threadIdx.x == 0) MK_TRACE(p, 0);
         if (P.kind == MK_ATTN) {
             const int n_items = Bst * n_kv * ms;
             for (int i = c; i < n_items; i += G) {
@@ -835,15 +866,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
                 for (int i = threadIdx.x; i < P.next_k / 4; i += MK_CT) cp_async16(nw_s + 4 * i, P.next_norm + 4 * i);
                 asm volatile("cp.async.commit_group;" ::: "memory");
             }
+            if (threadIdx.x == 0) MK_TRACE(p, 1);
             const int g = lane >> 2, t = lane & 3;
             const uint4 *xq = reinterpret_cast<const uint4 *>(xs) + gemv_rec_row(P.a.B, P.a.lo, g) * 4 + t;
             mk_consume_epi<FA, FB>(P, mp, misc, R, lite, n_phases, p, c, G, warp, xq, bsum + 2 * t, s_scale, part,
                                    status, lane);
         }
+        if (threadIdx.x == 0) MK_TRACE(p, 2);
         if (p + 1 < n_phases) {
             asm volatile("cp.async.wait_all;" ::: "memory");   // descriptor p + 1 is in place after the barrier
             if (threadIdx.x == 0 && lite[p + 1].kind == MK_GEMV) misc.quiet = 1;
             mk_grid_sync(gbar, (unsigned int)(p + 1) * (unsigned int)G, status, lite, n_phases, warp, R.cons);
+            if (threadIdx.x == 0) MK_TRACE(p, 3);
             mk_fetch_phase(phases, p + 2, n_phases, ph_s + (p & 1));   // slot of phase p, now unused
         }
     }

@@ -22,36 +22,58 @@
 namespace v3g {
 
 // ------------------------------------------------------------------------------------------ per-piece control
-// token bookkeeping of a piece (the sequential part of src/vault_v3_model.py:2224-2268 / :1952-2022 for every
-// token), then the embedding rows of all its tokens.  pin_first = 0 when a boundary piece's first token was
-// already auto-pinned before the eviction (k_pin).
+// Token bookkeeping of a piece (the sequential part of src/vault_v3_model.py:2224-2268 / :1952-2022 for every
+// token) and the embedding rows of all its tokens.  Grid (sequence, token slice): every CTA gathers the embedding
+// rows of its slice; CTA 0 of a sequence also runs the bookkeeping, with the piece's token ids and tiers staged in
+// shared memory and the sequence's control block held in registers (one thread: the segmentation is a recurrence
+// over the tokens), then writes the token and segment rings in parallel.  pin_first = 0 when a boundary piece's
+// first token was already auto-pinned before the eviction (k_pin).  A piece never crosses a window boundary.
 __global__ void __launch_bounds__(256) k_piece_begin(const ModelDev *mp, const StateDev *sp, const int32_t *ids,
                                                      int64_t ld, int64_t i0, int n, int64_t p0, int pin_first,
                                                      float *X) {
     const ModelDev &m = *mp;
     const StateDev &s = *sp;
     const int b = blockIdx.x;
-    extern __shared__ int s_tok[];   // [n]
-    const int W = m.W;
+    const int W = m.W, d = m.d;
+    const int c0 = (int)(p0 % W), par = (int)((p0 / W) & 1);
+    extern __shared__ int s_tok[];   // [n] token ids, [n] tiers, [n] segment ids
+    int *s_tier = s_tok + n, *s_seg = s_tok + 2 * n;
+    const int j0 = (int)((int64_t)n * blockIdx.y / gridDim.y), j1 = (int)((int64_t)n * (blockIdx.y + 1) / gridDim.y);
+    const bool ctl = blockIdx.y == 0;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        if (!ctl && (j < j0 || j >= j1)) continue;
+        int tok = ids[(int64_t)b * ld + i0 + j];
+        if (tok < 0 || tok >= m.vocab) tok = m.pad_id;   // runtime/vault3.c:2041
+        s_tok[j] = tok;
+        if (ctl) s_tier[j] = m.tier[tok];
+    }
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < (int64_t)(j1 - j0) * d; i += blockDim.x) {
+        const int j = j0 + (int)(i / d), k = (int)(i % d);
+        X[((int64_t)b * n + j) * d + k] = tile_value(m.embed.tiles, m.embed.fmt, m.embed.n_ktiles, m.embed.wscale,
+                                                     s_tok[j], k);
+    }
+    if (!ctl) return;
+    int32_t *tok_ring = s.tok_ring + ((size_t)b * 2 + par) * W;
+    const int32_t *tok_prev = s.tok_ring + ((size_t)b * 2 + (par ^ 1)) * W;
     if (threadIdx.x == 0) {
-        SeqCtl &q = s.seq[b];
+        SeqCtl q = s.seq[b];
         const bool seg = q.seg_on && q.seg_budget > 0;
+        const bool res = p0 >= 2 * W && q.mem_cnt > 0 && q.n_uniq_segs > 2;   // resonance trigger (see k_begin)
         const int t2 = max(m.seg_min, (m.seg_max * 2) / 3);
         const int t3 = max(m.seg_min, m.seg_max > 8 ? m.seg_max - 8 : m.seg_min);
+        bool flagged = false;
         for (int j = 0; j < n; ++j) {
             const int64_t pos = p0 + j;
-            const int c = (int)(pos % W), par = (int)((pos / W) & 1);
-            int tok = ids[(int64_t)b * ld + i0 + j];
-            if (tok < 0 || tok >= m.vocab) tok = m.pad_id;   // runtime/vault3.c:2041
+            const int c = c0 + j, tok = s_tok[j];
             if (j > 0 || pin_first) auto_pin_update(m, q, pos, tok);
             if (c == 0) {
                 q.cur_seg_id = 0;
                 q.seg_len = 0;
             }
-            s.tok_ring[((size_t)b * 2 + par) * W + c] = tok;
             if (seg) {
-                const int tr = m.tier[tok];
-                s.seg_ring[((size_t)b * 2 + par) * W + c] = q.cur_seg_id;
+                const int tr = s_tier[j];
+                s_seg[j] = q.cur_seg_id;
                 q.seg_len += 1;
                 const bool brk = (tr == 1 && q.seg_len >= m.seg_min) || (tr == 2 && q.seg_len >= t2) ||
                                  (tr == 3 && q.seg_len >= t3);
@@ -59,27 +81,28 @@ __global__ void __launch_bounds__(256) k_piece_begin(const ModelDev *mp, const S
                     q.cur_seg_id += 1;
                     q.seg_len = 0;
                 }
-                if (pos >= 2 * W && q.mem_cnt > 0 && q.n_uniq_segs > 2) {   // resonance trigger (see k_begin)
+                if (res && !flagged) {   // the latest <|im_end|> within 37 tokens, in the window up to this token
                     const int hi = W + c;
                     for (int p = hi; p >= max(0, hi - 37); --p) {
-                        const int tk = p < W ? s.tok_ring[((size_t)b * 2 + (par ^ 1)) * W + p]
-                                             : s.tok_ring[((size_t)b * 2 + par) * W + (p - W)];
+                        const int cp = p - W;   // slot in the current chunk (< 0: the previous chunk)
+                        const int tk = cp < 0 ? tok_prev[p] : (cp >= c0 ? s_tok[cp - c0] : tok_ring[cp]);
                         if (tk == m.im_end_id) {
-                            if (p > 0 && pos - (hi - p) >= q.n_pin) atomicOr(&s.step->status, STATUS_RESONANCE);
+                            if (p > 0 && pos - (hi - p) >= q.n_pin) flagged = true;
                             break;
                         }
                     }
                 }
             }
-            s_tok[j] = tok;
         }
+        if (flagged) atomicOr(&s.step->status, STATUS_RESONANCE);
+        s.seq[b] = q;
         s.amax[b] = 0ull;
     }
     __syncthreads();
-    for (int64_t i = threadIdx.x; i < (int64_t)n * m.d; i += blockDim.x) {
-        const int j = (int)(i / m.d), k = (int)(i - (int64_t)j * m.d);
-        X[((int64_t)b * n + j) * m.d + k] = tile_value(m.embed.tiles, m.embed.fmt, m.embed.n_ktiles, m.embed.wscale,
-                                                       s_tok[j], k);
+    const bool seg = s.seq[b].seg_on && s.seq[b].seg_budget > 0;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        tok_ring[c0 + j] = s_tok[j];
+        if (seg) s.seg_ring[((size_t)b * 2 + par) * W + c0 + j] = s_seg[j];
     }
 }
 
@@ -129,17 +152,80 @@ __global__ void k_piece_scan(const StateDev *sp, int n, const float *feat, float
     s.ema[(size_t)b * fd + k] = e;
 }
 
-// fc1 of both LayerNorm inputs for every token of the piece (grid: hidden / 8 unit blocks x tokens)
-__global__ void __launch_bounds__(SCORER_THREADS) k_piece_fc1(const ModelDev *mp, const StateDev *sp, int n,
-                                                              const float *feat, const float *hin, float *z) {
-    const ModelDev &m = *mp;
+// LayerNorm statistics {mean raw, mean habituated, 1/std raw, 1/std habituated} of every token of the piece (one
+// CTA per token; the reduction order of the decode step's scorer)
+__global__ void __launch_bounds__(SCORER_THREADS) k_piece_lnstat(const StateDev *sp, int n, const float *feat,
+                                                                 const float *hin, float4 *stat) {
     const StateDev &s = *sp;
-    const int t = blockIdx.y, b = t / n, fd = s.feat_dim;
+    const int t = blockIdx.x, b = t / n, fd = s.feat_dim;
     const SeqCtl &q = s.seq[b];
-    if (!(q.seg_on && q.seg_budget > 0)) return;
+    if (!(q.seg_on && q.seg_budget > 0)) {
+        if (threadIdx.x == 0) stat[t] = make_float4(0.f, 0.f, 1.f, 1.f);   // unused: keeps k_piece_fc1's input finite
+        return;
+    }
     const float *f = feat + (size_t)t * fd, *h = hin + (size_t)t * fd;
-    scorer_fc1_block(m, fd, [=](int k) { return f[k]; }, [=](int k) { return h[k]; }, blockIdx.x * (SCORER_THREADS / 32),
-                     z + (size_t)t * 2 * m.seg_hidden, z + ((size_t)t * 2 + 1) * m.seg_hidden);
+    float st[4];
+    scorer_ln_stats_block(fd, [=](int k) { return f[k]; }, [=](int k) { return h[k]; }, st);
+    if (threadIdx.x == 0) stat[t] = make_float4(st[0], st[1], st[2], st[3]);
+}
+
+constexpr int PF_FC1_TOK = 16;    // tokens per CTA
+constexpr int PF_FC1_KC = 128;    // features per shared-memory chunk
+
+// fc1 of both LayerNorm inputs for 16 tokens x 8 hidden units per CTA (one warp per unit): the normalised inputs of
+// a 128-feature chunk are staged in shared memory once per CTA and every W1 element is read once per 16 tokens.
+// Each lane keeps the per-lane order of scorer_fc1_block (k = lane, lane + 32, ... increasing, then the butterfly),
+// so every output equals the decode step's bit for bit.
+__global__ void __launch_bounds__(SCORER_THREADS) k_piece_fc1(const ModelDev *mp, const StateDev *sp, int T,
+                                                              const float *feat, const float *hin, const float4 *stat,
+                                                              float *z) {
+    const ModelDev &m = *mp;
+    const int fd = sp->feat_dim, hdn = m.seg_hidden;
+    const int t0 = blockIdx.y * PF_FC1_TOK, nt = min(PF_FC1_TOK, T - t0);
+    __shared__ float ln0[PF_FC1_TOK][PF_FC1_KC], ln1[PF_FC1_TOK][PF_FC1_KC];
+    __shared__ float4 st[PF_FC1_TOK];
+    if (threadIdx.x < PF_FC1_TOK)
+        st[threadIdx.x] = (int)threadIdx.x < nt ? stat[t0 + threadIdx.x] : make_float4(0.f, 0.f, 1.f, 1.f);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int u = blockIdx.x * (SCORER_THREADS / 32) + warp;
+    const float *w1 = m.sc_w1 + (size_t)min(u, hdn - 1) * fd;
+    float s0[PF_FC1_TOK], s1[PF_FC1_TOK];
+#pragma unroll
+    for (int j = 0; j < PF_FC1_TOK; ++j) s0[j] = s1[j] = 0.f;
+    for (int kc = 0; kc < fd; kc += PF_FC1_KC) {
+        __syncthreads();   // the previous chunk is consumed (first pass: st is written)
+        for (int i = threadIdx.x; i < PF_FC1_TOK * PF_FC1_KC; i += SCORER_THREADS) {
+            const int tt = i / PF_FC1_KC, kk = i - tt * PF_FC1_KC, k = kc + kk;
+            float v0 = 0.f, v1 = 0.f;
+            if (tt < nt && k < fd) {
+                const float lw = m.sc_ln_w[k], lb = m.sc_ln_b[k];
+                const float4 q = st[tt];
+                v0 = sc_ln(feat[(size_t)(t0 + tt) * fd + k], q.x, q.z, lw, lb);
+                v1 = sc_ln(hin[(size_t)(t0 + tt) * fd + k], q.y, q.w, lw, lb);
+            }
+            ln0[tt][kk] = v0;
+            ln1[tt][kk] = v1;
+        }
+        __syncthreads();
+        for (int kk = lane; kk < PF_FC1_KC && kc + kk < fd; kk += 32) {
+            const float wk = w1[kc + kk];
+#pragma unroll
+            for (int j = 0; j < PF_FC1_TOK; ++j) {
+                s0[j] = sc_fc1_term(s0[j], wk, ln0[j][kk]);
+                s1[j] = sc_fc1_term(s1[j], wk, ln1[j][kk]);
+            }
+        }
+    }
+    if (u >= hdn) return;
+    const float bias = m.sc_b1[u];
+#pragma unroll
+    for (int j = 0; j < PF_FC1_TOK; ++j) {
+        const float a0 = warp_sum(s0[j]), a1 = warp_sum(s1[j]);
+        if (lane == 0 && j < nt) {
+            z[((size_t)(t0 + j) * 2) * hdn + u] = __fadd_rn(a0, bias);
+            z[((size_t)(t0 + j) * 2 + 1) * hdn + u] = __fadd_rn(a1, bias);
+        }
+    }
 }
 
 // score of every token of the piece into the score ring (one CTA per token)
@@ -161,61 +247,138 @@ __global__ void __launch_bounds__(SCORER_THREADS) k_piece_score(const ModelDev *
 // Token t of a piece = (sequence t / n, position p0 + t % n); p0 < 0: the batched decode step (n = 1), whose
 // position is read from the state on the device (so a captured step replays at any position).
 struct PieceQKV {   // bias + RoPE + KV / sink writes + both query rotations (the QKV epilogue of v3g_step.cu per token)
-    const ModelDev *m;
-    const StateDev *s;
+    StateDev sd;           // the state descriptor by value (its scalars and base pointers stay in registers)
+    const float *rope;     // model RoPE table, rows from position rope_pos0
+    int rope_pos0;
     int layer, n;
     int64_t p0;
     const float *bq, *bk, *bv;
     float *qc, *qf;   // [tokens][H][D]
-    __device__ void operator()(int seg, int rt, int g, int tok, float y0, float y1) const {
-        const int D = s->D, W = s->W, hd = D / 2;
-        const int b = tok / n;
-        const int64_t pos = (p0 < 0 ? s->step->pos : p0) + (tok - b * n);
-        const int c = (int)(pos % W), par = (int)((pos / W) & 1);
-        const int head = rt / (D / TILE_ROWS), j = rt % (D / TILE_ROWS), i = 8 * j + g;
-        const int r0 = head * D + i, r1 = r0 + hd;
-        const float *rc = rope_row(*m, c);
-        const float cs = rc[i], sn = rc[hd + i];
-        const float *bsrc = seg == 0 ? bq : (seg == 1 ? bk : bv);
-        const float a = y0 + bsrc[r0], bb = y1 + bsrc[r1];
-        if (seg == 0) {
-            float *q = qc + ((size_t)tok * s->H + head) * D;
-            q[i] = a * cs - bb * sn;
-            q[i + hd] = bb * cs + a * sn;
-            if (pos >= W) {
-                const float *rf = rope_row(*m, W + c);
-                float *qq = qf + ((size_t)tok * s->H + head) * D;
-                qq[i] = a * rf[i] - bb * rf[hd + i];
-                qq[i + hd] = bb * rf[i] + a * rf[hd + i];
-            }
-        } else if (seg == 1) {
-            kv_t *kr = kvp(*s, layer, b, ring_off(*s, par, 1, head, c));
-            kv_t *ko = kvp(*s, layer, b, ring_off(*s, par, 0, head, c));
-            kr[i] = f2kv(a);
-            kr[i + hd] = f2kv(bb);
-            ko[i] = f2kv(a * cs - bb * sn);
-            ko[i + hd] = f2kv(bb * cs + a * sn);
-            if (pos < s->sink_cap) {
-                kv_t *sk = kvp(*s, layer, b, sink_off(*s, 0, head, (int)pos));
-                sk[i] = f2kv(a);
-                sk[i + hd] = f2kv(bb);
-            }
+
+    // position bookkeeping of consecutive tokens: sequence b, position pos, window slot c, ring parity par
+    struct Cursor {
+        int b, jn, c, par;
+        int64_t pos;
+    };
+    __device__ Cursor start(int tok0, int64_t base) const {
+        Cursor u;
+        u.b = tok0 / n;
+        u.jn = tok0 - u.b * n;
+        u.pos = base + u.jn;
+        u.c = (int)(u.pos % sd.W);
+        u.par = (int)((u.pos / sd.W) & 1);
+        return u;
+    }
+    __device__ void advance(Cursor &u, int64_t base) const {
+        if (++u.jn == n) {   // next sequence: back to the piece's first position
+            u.jn = 0;
+            ++u.b;
+            u.pos = base;
+            u.c = (int)(base % sd.W);
+            u.par = (int)((base / sd.W) & 1);
         } else {
-            kv_t *vv = kvp(*s, layer, b, ring_off(*s, par, 2, head, c));
-            vv[i] = f2kv(a);
-            vv[i + hd] = f2kv(bb);
-            if (pos < s->sink_cap) {
-                kv_t *sv = kvp(*s, layer, b, sink_off(*s, 2, head, (int)pos));
-                sv[i] = f2kv(a);
-                sv[i + hd] = f2kv(bb);
+            ++u.pos;
+            if (++u.c == sd.W) {
+                u.c = 0;
+                u.par ^= 1;
             }
         }
+    }
+    __device__ const float *rope_at(int64_t p) const { return rope + (p - rope_pos0) * (int64_t)sd.D; }
+
+    template <int N>
+    __device__ void chunk(int seg, int rt, int g, int tok0, int nv, const float (&y0)[N], const float (&y1)[N]) const {
+        const int D = sd.D, W = sd.W, hd = D / 2;
+        const int head = rt / (D / TILE_ROWS), i = 8 * (rt % (D / TILE_ROWS)) + g;
+        const int r0 = head * D + i, r1 = r0 + hd;
+        const float *bsrc = seg == 0 ? bq : (seg == 1 ? bk : bv);
+        const float b0 = __ldg(bsrc + r0), b1 = __ldg(bsrc + r1);
+        const int64_t base = p0 < 0 ? __ldcg(&sd.step->pos) : p0;
+        // reads: the RoPE factors of every token (rotations at c and, for queries past the first window, W + c)
+        float cs[N], sn[N], fc[N], fs[N];
+        Cursor u = start(tok0, base);
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            cs[j] = sn[j] = fc[j] = fs[j] = 0.f;
+            if (j < nv) {
+                const float *rc = rope_at(u.c);
+                cs[j] = __ldg(rc + i);
+                sn[j] = __ldg(rc + hd + i);
+                if (seg == 0 && u.pos >= W) {
+                    const float *rf = rope_at(W + u.c);
+                    fc[j] = __ldg(rf + i);
+                    fs[j] = __ldg(rf + hd + i);
+                }
+                advance(u, base);
+            }
+        }
+        // writes
+        u = start(tok0, base);
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            if (j >= nv) break;
+            const int tok = tok0 + j;
+            const float a = y0[j] + b0, bb = y1[j] + b1;
+            if (seg == 0) {
+                float *q = qc + ((size_t)tok * sd.H + head) * D;
+                q[i] = a * cs[j] - bb * sn[j];
+                q[i + hd] = bb * cs[j] + a * sn[j];
+                if (u.pos >= W) {
+                    float *qq = qf + ((size_t)tok * sd.H + head) * D;
+                    qq[i] = a * fc[j] - bb * fs[j];
+                    qq[i + hd] = bb * fc[j] + a * fs[j];
+                }
+            } else if (seg == 1) {
+                kv_t *kr = kvp(sd, layer, u.b, ring_off(sd, u.par, KIND_KRAW, head, u.c));
+                kv_t *ko = kvp(sd, layer, u.b, ring_off(sd, u.par, KIND_KROT, head, u.c));
+                kr[i] = f2kv(a);
+                kr[i + hd] = f2kv(bb);
+                ko[i] = f2kv(a * cs[j] - bb * sn[j]);
+                ko[i + hd] = f2kv(bb * cs[j] + a * sn[j]);
+                if (u.pos < sd.sink_cap) {
+                    kv_t *sk = kvp(sd, layer, u.b, sink_off(sd, SINK_KRAW, head, (int)u.pos));
+                    sk[i] = f2kv(a);
+                    sk[i + hd] = f2kv(bb);
+                }
+            } else {
+                kv_t *vv = kvp(sd, layer, u.b, ring_off(sd, u.par, KIND_V, head, u.c));
+                vv[i] = f2kv(a);
+                vv[i + hd] = f2kv(bb);
+                if (u.pos < sd.sink_cap) {
+                    kv_t *sv = kvp(sd, layer, u.b, sink_off(sd, SINK_V, head, (int)u.pos));
+                    sv[i] = f2kv(a);
+                    sv[i + hd] = f2kv(bb);
+                }
+            }
+            advance(u, base);
+        }
+    }
+    __device__ void operator()(int seg, int rt, int g, int tok, float y0, float y1) const {
+        const float a0[1] = {y0}, a1[1] = {y1};
+        chunk<1>(seg, rt, g, tok, 1, a0, a1);
     }
 };
 
 struct TokResid {   // x[t, row] += y (identity row order)
     float *x;
     int ld, rows;
+    template <int N>
+    __device__ void chunk(int, int rt, int g, int tok0, int nv, const float (&y0)[N], const float (&y1)[N]) const {
+        const int r = TILE_ROWS * rt + g;
+        float *xr = x + (size_t)tok0 * ld + r;
+        float x0[N], x1[N];
+#pragma unroll
+        for (int j = 0; j < N; ++j) {   // every read first ...
+            x0[j] = j < nv && r < rows ? __ldcg(xr + (size_t)j * ld) : 0.f;
+            x1[j] = j < nv && r + 8 < rows ? __ldcg(xr + (size_t)j * ld + 8) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < N; ++j) {   // ... then the writes
+            if (j >= nv) break;
+            if (r < rows) xr[(size_t)j * ld] = x0[j] + y0[j];
+            if (r + 8 < rows) xr[(size_t)j * ld + 8] = x1[j] + y1[j];
+        }
+    }
     __device__ void operator()(int, int rt, int g, int tok, float y0, float y1) const {
         const int r = TILE_ROWS * rt + g;
         float *xr = x + (size_t)tok * ld;
@@ -234,6 +397,12 @@ struct TokStore {   // y[t, row] = value (identity row order): logits of the bat
         if (r < rows) yr[r] = y0;
         if (r + 8 < rows) yr[r + 8] = y1;
     }
+    template <int N>
+    __device__ void chunk(int seg, int rt, int g, int tok0, int nv, const float (&y0)[N], const float (&y1)[N]) const {
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if (j < nv) (*this)(seg, rt, g, tok0 + j, y0[j], y1[j]);
+    }
 };
 
 struct TokGateUp {   // h[t, f] = silu(gate_f) * up_f  (src/vault_v3_model.py:1149-1150)
@@ -242,6 +411,12 @@ struct TokGateUp {   // h[t, f] = silu(gate_f) * up_f  (src/vault_v3_model.py:11
     __device__ void operator()(int, int rt, int g, int tok, float gt, float u) const {
         const int f = 8 * rt + g;
         if (f < F) h[(size_t)tok * F + f] = gt / (1.0f + expf(-gt)) * u;
+    }
+    template <int N>
+    __device__ void chunk(int seg, int rt, int g, int tok0, int nv, const float (&y0)[N], const float (&y1)[N]) const {
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if (j < nv) (*this)(seg, rt, g, tok0 + j, y0[j], y1[j]);
     }
 };
 
@@ -507,8 +682,9 @@ cudaError_t launch_piece(const v3g_model *m, v3g_state *s, const int32_t *dev_id
                                  (size_t)B, cudaMemcpyDeviceToDevice, st));
         PF_TRY(launch_boundary(m, s, st));
     }
-    k_piece_begin<<<B, 256, (size_t)n * sizeof(int), st>>>(m->dev, s->dev, dev_ids, ld, i0, n, p0, boundary ? 0 : 1,
-                                                           pf.x);
+    const int slices = std::max(1, std::min(32, (n * md.d) / (256 * 64)));   // about 64 embedding values a thread
+    k_piece_begin<<<dim3(B, slices), 256, (size_t)n * 3 * sizeof(int), st>>>(m->dev, s->dev, dev_ids, ld, i0, n, p0,
+                                                                               boundary ? 0 : 1, pf.x);
     PF_TRY(cudaGetLastError());
     const int HD = md.H * md.D;
     const bool any_seg = md.seg_n_feat > 0 && s->seg_budget > 0;
@@ -521,7 +697,7 @@ cudaError_t launch_piece(const v3g_model *m, v3g_state *s, const int32_t *dev_id
         PF_TRY(tc_prep(pf.x, md.d, T, md.d, L.ln1, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
         {
             const MatW *mats[3] = {&L.q, &L.k, &L.v};
-            PieceQKV epi{m->dev, s->dev, l, n, p0, L.bq, L.bk, L.bv, pf.qc, pf.qf};
+            PieceQKV epi{s->host, md.rope, md.rope_pos0, l, n, p0, L.bq, L.bk, L.bv, pf.qc, pf.qf};
             PF_TRY(tc_gemm(mats, 3, pf.x16, pf.ldx16, pf.xscale, T, status, m->n_sm, epi, st, &pf.sk));
         }
         PF_TRY(prefill_attention(m, s, l, n, p0, st));
@@ -546,8 +722,9 @@ cudaError_t launch_piece(const v3g_model *m, v3g_state *s, const int32_t *dev_id
     }
     if (any_seg) {
         k_piece_scan<<<dim3((sd.feat_dim + 255) / 256, B), 256, 0, st>>>(s->dev, n, pf.feat, pf.hin);
-        k_piece_fc1<<<dim3((md.seg_hidden + 7) / 8, T), SCORER_THREADS, 0, st>>>(m->dev, s->dev, n, pf.feat, pf.hin,
-                                                                                pf.z);
+        k_piece_lnstat<<<T, SCORER_THREADS, 0, st>>>(s->dev, n, pf.feat, pf.hin, pf.stat);
+        k_piece_fc1<<<dim3((md.seg_hidden + 7) / 8, (T + PF_FC1_TOK - 1) / PF_FC1_TOK), SCORER_THREADS, 0, st>>>(
+            m->dev, s->dev, T, pf.feat, pf.hin, pf.stat, pf.z);
         k_piece_score<<<T, SCORER_THREADS, 0, st>>>(m->dev, s->dev, n, p0, pf.z);
         PF_TRY(cudaGetLastError());
     }
@@ -587,7 +764,7 @@ cudaError_t launch_step_tc(const v3g_model *m, v3g_state *s, bool boundary, bool
         TS_TRY(tc_prep(sd.x, md.d, B, md.d, L.ln1, md.rms_eps, pf.x16, pf.ldx16, pf.xscale, st));
         {
             const MatW *mats[3] = {&L.q, &L.k, &L.v};
-            PieceQKV epi{m->dev, s->dev, l, 1, -1, L.bq, L.bk, L.bv, sd.q_cur, sd.q_far};
+            PieceQKV epi{s->host, md.rope, md.rope_pos0, l, 1, -1, L.bq, L.bk, L.bv, sd.q_cur, sd.q_far};
             TS_TRY(tc_gemm(mats, 3, pf.x16, pf.ldx16, pf.xscale, B, status, m->n_sm, epi, st, &pf.sk));
         }
         TS_TRY(launch_attention(m, s, l, false, st));

@@ -23,15 +23,14 @@ __device__ __forceinline__ float sc_ln(float v, float mu, float inv, float lw, f
     return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, mu), inv), lw), lb);
 }
 
-// fc1 pre-activations of the raw features (in0) and the habituated ones (in1) for hidden units [u0, u0 + 8): one
-// 256-thread CTA; LayerNorm statistics over fd features (eps 1e-5), one warp per unit.  z0[u], z1[u] receive fc1
-// outputs plus bias.  in0(k) / in1(k) return feature k.
+// LayerNorm statistics of the raw (in0) and habituated (in1) feature rows over fd features (eps 1e-5), one 256-thread
+// CTA: stat = {mean0, mean1, 1/std0, 1/std1} on every thread.  Thread tid sums features tid, tid + 256, ..., the warp
+// sums reduce by butterfly and thread 0 adds the 8 warp partials in warp order.
 template <class In0, class In1>
-__device__ void scorer_fc1_block(const ModelDev &m, int fd, const In0 &in0, const In1 &in1, int u0, float *z0,
-                                 float *z1) {
+__device__ void scorer_ln_stats_block(int fd, const In0 &in0, const In1 &in1, float (&stat)[4]) {
     const int tid = threadIdx.x, nt = SCORER_THREADS;
     __shared__ float red[4][32];
-    __shared__ float stat[4];
+    __shared__ float sh[4];
     float a0 = 0.f, a1 = 0.f;
     for (int k = tid; k < fd; k += nt) {
         a0 = __fadd_rn(a0, in0(k));
@@ -50,11 +49,11 @@ __device__ void scorer_fc1_block(const ModelDev &m, int fd, const In0 &in0, cons
             x0 = __fadd_rn(x0, red[0][w]);
             x1 = __fadd_rn(x1, red[1][w]);
         }
-        stat[0] = __fdiv_rn(x0, (float)fd);
-        stat[1] = __fdiv_rn(x1, (float)fd);
+        sh[0] = __fdiv_rn(x0, (float)fd);
+        sh[1] = __fdiv_rn(x1, (float)fd);
     }
     __syncthreads();
-    const float mu0 = stat[0], mu1 = stat[1];
+    const float mu0 = sh[0], mu1 = sh[1];
     float v0 = 0.f, v1 = 0.f;
     for (int k = tid; k < fd; k += nt) {
         const float d0 = __fsub_rn(in0(k), mu0), d1 = __fsub_rn(in1(k), mu1);
@@ -74,20 +73,37 @@ __device__ void scorer_fc1_block(const ModelDev &m, int fd, const In0 &in0, cons
             x0 = __fadd_rn(x0, red[2][w]);
             x1 = __fadd_rn(x1, red[3][w]);
         }
-        stat[2] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(x0, (float)fd), 1e-5f)));
-        stat[3] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(x1, (float)fd), 1e-5f)));
+        sh[2] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(x0, (float)fd), 1e-5f)));
+        sh[3] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(x1, (float)fd), 1e-5f)));
     }
     __syncthreads();
-    const float i0 = stat[2], i1 = stat[3];
-    const int warp = tid >> 5, lane = tid & 31;
+    stat[0] = mu0;
+    stat[1] = mu1;
+    stat[2] = sh[2];
+    stat[3] = sh[3];
+}
+
+// fc1 dot product of hidden unit u with one LayerNorm'd input row, as lane `lane` of a warp: the lane adds
+// w1[u][k] * ln(k) over k = lane, lane + 32, ... in increasing k, then the warp sums by butterfly.  Callers that
+// tile k or tokens keep this per-lane order, so every path gives the same bits.
+__device__ __forceinline__ float sc_fc1_term(float acc, float wk, float lnk) { return __fadd_rn(acc, __fmul_rn(wk, lnk)); }
+
+// fc1 pre-activations of the raw features (in0) and the habituated ones (in1) for hidden units [u0, u0 + 8): one
+// 256-thread CTA, one warp per unit.  z0[u], z1[u] receive fc1 outputs plus bias.  in0(k) / in1(k) return feature k.
+template <class In0, class In1>
+__device__ void scorer_fc1_block(const ModelDev &m, int fd, const In0 &in0, const In1 &in1, int u0, float *z0,
+                                 float *z1) {
+    float st[4];
+    scorer_ln_stats_block(fd, in0, in1, st);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int u = u0 + warp;
     if (u >= m.seg_hidden) return;
     const float *w1 = m.sc_w1 + (size_t)u * fd;
     float s0 = 0.f, s1 = 0.f;
     for (int k = lane; k < fd; k += 32) {
         const float lw = m.sc_ln_w[k], lb = m.sc_ln_b[k], wk = w1[k];
-        s0 = __fadd_rn(s0, __fmul_rn(wk, sc_ln(in0(k), mu0, i0, lw, lb)));
-        s1 = __fadd_rn(s1, __fmul_rn(wk, sc_ln(in1(k), mu1, i1, lw, lb)));
+        s0 = sc_fc1_term(s0, wk, sc_ln(in0(k), st[0], st[2], lw, lb));
+        s1 = sc_fc1_term(s1, wk, sc_ln(in1(k), st[1], st[3], lw, lb));
     }
     s0 = warp_sum(s0);
     s1 = warp_sum(s1);

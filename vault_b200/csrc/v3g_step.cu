@@ -13,10 +13,6 @@
 
 namespace v3g {
 
-constexpr int KIND_KROT = 0, KIND_KRAW = 1, KIND_V = 2;   // ring kinds
-constexpr int SINK_KRAW = 0, SINK_KROT = 1, SINK_V = 2;   // sink kinds
-constexpr int BANK_KRAW = 0, BANK_V = 1;                  // bank kinds
-
 __device__ __forceinline__ int ring_par(int64_t pos, int W) { return (int)((pos / W) & 1); }
 
 __device__ __forceinline__ bool seg_active(const SeqCtl &q) { return q.seg_on && q.seg_budget > 0; }
@@ -979,3 +975,11 @@ cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool wa
 }
 
 }  // namespace v3g
+
+#ifdef V3G_MK_TRACE
+#include "../../include/vault_b200.h"
+// timeline of the last persistent-kernel launch ([phase][cta][5] u64 nanoseconds; see v3g_mega.cuh)
+extern "C" V3G_API int v3g_mk_trace_read(void *dst, size_t bytes) {
+    return (int)cudaMemcpyFromSymbol(dst, v3g::g_mk_trace, bytes < sizeof(v3g::g_mk_trace) ? bytes : sizeof(v3g::g_mk_trace));
+}
+#endif
