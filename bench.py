@@ -82,6 +82,22 @@ def select_config(n: int) -> None:
     CONFIG, FMT, PROMPT, DECODE, METRIC, TRAFFIC = n, c["fmt"], c["prompt"], c["decode"], c["metric"], c["traffic"]
 
 
+def override_config(batch=None, prompt=None) -> None:
+    """A smaller instance of the selected config (profiling captures): the workload text records the change."""
+    global PROMPT, TRAFFIC
+    c = CONFIGS[CONFIG]
+    changes = []
+    if batch is not None and batch != c["batch"]:
+        c["batch"] = batch
+        changes.append(f"{batch} sequences")
+    if prompt is not None and prompt != c["prompt"]:
+        c["prompt"] = PROMPT = prompt
+        changes.append(f"{prompt}-token prompts")
+    if changes:
+        c["workload"] += " -- OVERRIDDEN to " + ", ".join(changes) + " (not the BASELINE size)"
+        c["traffic"] = TRAFFIC = None
+
+
 def model_path(fmt: str = "q8_0", model=None) -> str:
     from vault_b200 import synth
     return synth.full_model_file(fmt, seed=0, n_sink=0, **(model or {}))
@@ -675,8 +691,13 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the config's sequence count (a smaller case of the same path, e.g. for ncu "
+                         "captures; the JSON line then names the override)")
+    ap.add_argument("--prompt", type=int, default=None, help="override the config's prompt length (same use)")
     args = ap.parse_args()
     select_config(args.config)
+    override_config(args.batch, args.prompt)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

@@ -149,6 +149,28 @@ struct StateDev {
     unsigned int *bar;           // grid-barrier counter of the persistent decode kernel (zeroed every step)
 };
 
+// Optional timeline of the persistent decode kernel (compile with -DV3G_MK_TRACE): per phase and CTA, %globaltimer
+// at the phase start (0), after the activation prologue (1), after the phase's work (2), after the grid barrier (3),
+// the producer's first copy of the phase (4), and inside the prologue after the loads (5) and the block barrier (6).
+// Read back with v3g_mk_trace_read (the copy of v3g_step.cu, where the kernel lives).
+#ifdef V3G_MK_TRACE
+constexpr int MK_TRACE_PH = 512, MK_TRACE_CTA = 160, MK_TRACE_EV = 8;
+static __device__ unsigned long long g_mk_trace[MK_TRACE_PH][MK_TRACE_CTA][MK_TRACE_EV];   // per translation unit
+__device__ __forceinline__ unsigned long long mk_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+#define MK_TRACE(p, ev)                                                                                \
+    do {                                                                                               \
+        if ((p) >= 0 && (p) < MK_TRACE_PH && blockIdx.x < MK_TRACE_CTA) g_mk_trace[p][blockIdx.x][ev] = mk_now(); \
+    } while (0)
+#else
+#define MK_TRACE(p, ev) \
+    do {                \
+    } while (0)
+#endif
+
 constexpr int KIND_KROT = 0, KIND_KRAW = 1, KIND_V = 2;   // ring kinds
 constexpr int SINK_KRAW = 0, SINK_KROT = 1, SINK_V = 2;   // sink kinds
 constexpr int BANK_KRAW = 0, BANK_V = 1;                  // bank kinds

@@ -117,6 +117,60 @@ __device__ __noinline__ void attn_merged8(const StateDev &s, int b, int e0, int 
     for (int j = 0; j < 8; ++j) v[j] = O[j] / L;
 }
 
+// Last-CTA merge of the n_splits unnormalised partials (o, m, l) of (sequence b, KV group g) into s.attn, in split
+// order: out = sum_sp o_sp exp(m_sp - M) / sum_sp l_sp exp(m_sp - M), M = max_sp m_sp.  The (m, l) pairs are staged
+// in shared memory first (spans of up to ATT_KPC splits; longer ones read them from global memory), then each thread
+// produces four output dims of one head with the o loads of 8 splits in flight at a time (the merge of a long span
+// is otherwise one dependent L2 round trip per split).  The per-output arithmetic is the same fma chain in split
+// order whatever the load schedule.  The K buffer of sm is free here and holds the staged l values.
+template <int D>
+__device__ void attn_merge_splits(const StateDev &s, int b, int g, int n_splits, AttnSmem<D> &sm, int nt) {
+    constexpr int PS = att_part_stride(D);
+    const int H = s.H, G = s.G, grp = H / G, tid = threadIdx.x;
+    const float *p0 = s.att_part + (((size_t)b * G + g) * s.max_splits) * grp * PS;
+    const bool staged = n_splits <= ATT_KPC;
+    float *ms = &sm.p[0][0], *ls = reinterpret_cast<float *>(sm.k);
+    static_assert(sizeof(AttnSmem<D>::k) >= ATT_GRP_MAX * ATT_KPC * sizeof(float), "l staging fits the K buffer");
+    if (staged)
+        for (int i = tid; i < grp * n_splits; i += nt) {
+            const int hr = i / n_splits, sp = i - hr * n_splits;
+            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p0 + ((size_t)sp * grp + hr) * PS + D));
+            ms[hr * ATT_KPC + sp] = ml.x;
+            ls[hr * ATT_KPC + sp] = ml.y;
+        }
+    sync_threads(nt);
+    auto m_of = [&](int hr, int sp) { return staged ? ms[hr * ATT_KPC + sp] : __ldcg(p0 + ((size_t)sp * grp + hr) * PS + D); };
+    auto l_of = [&](int hr, int sp) {
+        return staged ? ls[hr * ATT_KPC + sp] : __ldcg(p0 + ((size_t)sp * grp + hr) * PS + D + 1);
+    };
+    for (int idx = tid; idx < grp * (D / 4); idx += nt) {
+        const int hr = idx / (D / 4), dd = 4 * (idx - hr * (D / 4));
+        float M = -INFINITY;
+        for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, m_of(hr, sp));
+        float L = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int sp0 = 0; sp0 < n_splits; sp0 += 8) {
+            float4 o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (sp0 + j < n_splits)
+                    o[j] = __ldcg(reinterpret_cast<const float4 *>(p0 + ((size_t)(sp0 + j) * grp + hr) * PS + dd));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (sp0 + j < n_splits) {
+                    const float w = expf(m_of(hr, sp0 + j) - M);
+                    L = fmaf(l_of(hr, sp0 + j), w, L);
+                    O[0] = fmaf(o[j].x, w, O[0]);
+                    O[1] = fmaf(o[j].y, w, O[1]);
+                    O[2] = fmaf(o[j].z, w, O[2]);
+                    O[3] = fmaf(o[j].w, w, O[3]);
+                }
+            }
+        }
+        *reinterpret_cast<float4 *>(&s.attn[((size_t)b * H + g * grp + hr) * D + dd]) =
+            make_float4(O[0] / L, O[1] / L, O[2] / L, O[3] / L);
+    }
+}
+
 // One work item = ATT_KPC keys of one (sequence b, KV head g) for its `grp` query heads, run by one CTA on the
 // tensor cores.  All K and V rows of the chunk are staged in shared memory with cp.async (one round trip).  Scores:
 // for each block of 8 keys, mma steps over the head dimension with A = the group's queries (rows 0-7 their high
@@ -424,22 +478,9 @@ __device__ bool attn_span(const StateDev &s, const KeySpan &ks, int layer, float
     sync_threads(nt);
     if (tid == 0) sm.last = atomicAdd(&s.att_cnt[b * G + g], 1u) == (uint32_t)(n_splits - 1);
     sync_threads(nt);
-    if (sm.last) {
+    if (sm.last) {   // uniform over the CTA
         __threadfence();
-        const float *p0 = s.att_part + (((size_t)b * G + g) * s.max_splits) * grp * PS;
-        for (int idx = tid; idx < grp * D; idx += nt) {
-            const int hr = idx / D, dd = idx - hr * D;
-            float M = -INFINITY;
-            for (int sp2 = 0; sp2 < n_splits; ++sp2) M = fmaxf(M, __ldcg(&p0[((size_t)sp2 * grp + hr) * PS + D]));
-            float L = 0.f, O = 0.f;
-            for (int sp2 = 0; sp2 < n_splits; ++sp2) {
-                const float *pp = p0 + ((size_t)sp2 * grp + hr) * PS;
-                const float w = expf(__ldcg(&pp[D]) - M);
-                L = fmaf(__ldcg(&pp[D + 1]), w, L);
-                O = fmaf(__ldcg(&pp[dd]), w, O);
-            }
-            s.attn[((size_t)b * H + g * grp + hr) * D + dd] = O / L;
-        }
+        attn_merge_splits<D>(s, b, g, n_splits, sm, nt);
         if (tid == 0) s.att_cnt[b * G + g] = 0u;
     }
     sync_threads(nt);

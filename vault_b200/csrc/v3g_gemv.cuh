@@ -242,7 +242,7 @@ struct XPlain {
 // activation values (XPlain reads a.x).
 template <bool BSUM, int CACHE = 0, class XL = XPlain>
 __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_scale, float *s_red, float *bsum,
-                                     int nt, const float *nw_s = nullptr, const XL &xl = XL()) {
+                                     int nt, const float *nw_s = nullptr, const XL &xl = XL(), int trace_p = -1) {
     const int tid = threadIdx.x, nw = nt / 32;
     const bool norm = a.prologue == PRO_RMSNORM;
     const bool vec = (a.K & 31) == 0 && (a.x_ld & 3) == 0;
@@ -313,7 +313,9 @@ __device__ inline void gemv_prologue(const GemvArgs &a, uint16_t *xs, float *s_s
             }
         }
     }
+    if (tid == 0) MK_TRACE(trace_p, 5);
     sync_threads(nt);
+    if (tid == 0) MK_TRACE(trace_p, 6);
     // every thread derives the multiplier of the rows it converts (same arithmetic everywhere: no second sync);
     // threads b < B also publish the scale the GEMV undoes.  Warp partials are summed in warp order.
     auto row_mul = [&](int b, float &scale) {

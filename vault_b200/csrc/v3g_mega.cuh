@@ -29,27 +29,6 @@
 
 namespace v3g {
 
-// Optional timeline of the persistent kernel (compile with -DV3G_MK_TRACE): per phase and CTA, %globaltimer at the
-// phase start, after the activation prologue, after the phase's work and after the grid barrier; plus the time the
-// producer issued its first copy of the phase.  Read back with v3g_mk_trace_read.
-#ifdef V3G_MK_TRACE
-constexpr int MK_TRACE_PH = 512, MK_TRACE_CTA = 160;
-__device__ unsigned long long g_mk_trace[MK_TRACE_PH][MK_TRACE_CTA][5];
-__device__ __forceinline__ unsigned long long mk_now() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-#define MK_TRACE(p, ev)                                                                    \
-    do {                                                                                   \
-        if ((p) < MK_TRACE_PH && blockIdx.x < MK_TRACE_CTA) g_mk_trace[p][blockIdx.x][ev] = mk_now(); \
-    } while (0)
-#else
-#define MK_TRACE(p, ev) \
-    do {                \
-    } while (0)
-#endif
-
 enum : int { MK_GEMV = 0, MK_ATTN = 1 };
 enum : int { MK_EPI_QKV = 0, MK_EPI_RESID = 1, MK_EPI_GATEUP = 2, MK_EPI_STORE = 3 };
 constexpr int MK_WARPS = GEMV_THREADS / 32;            // consumer warps
@@ -860,7 +839,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode(const ModelDev *mp, co
             // a CTA without row tiles in this phase converts nothing (CTA 0 still captures scorer features)
             if (lite[p].own[1] > lite[p].own[0] || (P.a.feat && c == 0))
                 gemv_prologue<BSUM, 5>(P.a, xs, s_scale, s_red, bsum, MK_CT, P.norm_staged ? nw_s : nullptr,
-                                       MkXLoad<D>{&misc.sd, misc.ks, P.attn_in});
+                                       MkXLoad<D>{&misc.sd, misc.ks, P.attn_in}, p);
             if (threadIdx.x == 0) misc.quiet = 0;   // activations are in place: the ring may refill
             if (P.next_norm) {   // stage the next phase's norm weights while this one streams (landed by the barrier)
                 for (int i = threadIdx.x; i < P.next_k / 4; i += MK_CT) cp_async16(nw_s + 4 * i, P.next_norm + 4 * i);

@@ -978,7 +978,7 @@ cudaError_t launch_step(const v3g_model *m, v3g_state *s, bool boundary, bool wa
 
 #ifdef V3G_MK_TRACE
 #include "../../include/vault_b200.h"
-// timeline of the last persistent-kernel launch ([phase][cta][5] u64 nanoseconds; see v3g_mega.cuh)
+// timeline of the last persistent-kernel launch ([phase][cta][event] u64 nanoseconds; see v3g.cuh)
 extern "C" V3G_API int v3g_mk_trace_read(void *dst, size_t bytes) {
     return (int)cudaMemcpyFromSymbol(dst, v3g::g_mk_trace, bytes < sizeof(v3g::g_mk_trace) ? bytes : sizeof(v3g::g_mk_trace));
 }
