@@ -162,6 +162,25 @@ static cudaError_t make_xmap(CUtensorMap *map, const __half *x, int rows, int K,
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// weight tensor map of one matrix: its row-tile buffer as [n_rtiles rows] x [stored bytes of a row tile / 8] elements
+// of 8 bytes (rows contiguous), boxes of 8 rows x one 64-k stage; reads past the row (the last stage of a K that is
+// not a multiple of 64) or past the last row tile return zeros
+static cudaError_t make_wmap(CUtensorMap *map, const MatW &w) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const int tb = tile_bytes(w.fmt), row = w.n_ktiles * tb, box_bytes = tc_stage_raw_bytes(w.fmt);
+    if ((reinterpret_cast<uintptr_t>(w.tiles) & 15) || row % 16 || box_bytes % 16 || box_bytes / 8 > 256)
+        return cudaErrorInvalidValue;
+    const cuuint64_t dims[2] = {(cuuint64_t)(row / 8), (cuuint64_t)w.n_rtiles};
+    const cuuint64_t strides[1] = {(cuuint64_t)row};
+    const cuuint32_t box[2] = {(cuuint32_t)(box_bytes / 8), 8u};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t *>(w.tiles), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // ------------------------------------------------------------------------------------------------ launch plan
 cudaError_t tc_setup(TcLaunch &L, const MatW *const *mats, int n, const __half *x16, int ldx, const float *xscale,
                      int n_tok, int *status, int n_sm, const TcSplitWs *sk) {
@@ -209,7 +228,8 @@ cudaError_t tc_setup(TcLaunch &L, const MatW *const *mats, int n, const __half *
     a.seg_base = 0;
     a.stage_a = TC_BM * TC_BK * 2;
     a.stage_x = a.bn * TC_BK * 2;
-    a.stage_raw = 8 * TC_RAW_ROW;
+    a.raw_row = std::max(tc_stage_raw_bytes(L.fa), tc_stage_raw_bytes(L.fb));   // multiples of 16 bytes
+    a.stage_raw = 8 * a.raw_row;
     const int per_stage = a.stage_a + a.stage_x + a.stage_raw;
     const int budget = 227 * 1024 - 1024 - 256;
     a.stages = budget / per_stage < TC_MAX_STAGES ? budget / per_stage : TC_MAX_STAGES;
@@ -234,6 +254,11 @@ cudaError_t tc_setup(TcLaunch &L, const MatW *const *mats, int n, const __half *
     }
     const int work = tiles * a.splits;
     L.grid = work < n_sm ? work : n_sm;
+    // weights by one TMA box per stage when no CTA tile straddles two matrices (segments start at multiples of 8
+    // row tiles); otherwise one bulk copy per row tile
+    a.w_tma = 1;
+    for (int i = 0; i < n; ++i)
+        if (a.rbase[i] % 8 != 0 || make_wmap(&L.wm.w[i], *mats[i]) != cudaSuccess) a.w_tma = 0;
     return make_xmap(&L.xmap, x16, n_tok, a.K, ldx, a.bn);
 }
 

@@ -45,8 +45,7 @@ constexpr int TC_BK = 64;             // k per stage (one 128-byte swizzled row)
 constexpr int TC_CONV_WARPS = 8;      // one per row tile of the CTA tile
 constexpr int TC_THREADS = 32 * (2 + TC_CONV_WARPS + 4);   // producer, MMA, converters, 4 epilogue warps
 constexpr int TC_EPI_CHUNK = 8;   // tokens per epilogue chunk() call
-constexpr int TC_RAW_ROW = 2048;      // stored weight bytes of one row tile per stage (16-bit tiles: 4 x 512)
-constexpr int TC_MAX_STAGES = 4;
+constexpr int TC_MAX_STAGES = 8;
 constexpr int TC_TMEM_COLS = 512;
 // split-K workspace of a state: tiles x splits <= SMs, so 256 SMs x 256 tokens x 128 rows of fp32 always suffice
 constexpr size_t TC_SPLITK_WS_BYTES = (size_t)256 * 256 * 128 * 4;
@@ -74,6 +73,14 @@ struct TcArgs {
     int *status;           // sticky error word (bit 4: a bounded wait ran out)
     // shared-memory layout (bytes from the 1024-aligned base)
     int a_off, x_off, raw_off, bar_off, stage_a, stage_x, stage_raw;
+    int raw_row;          // stored weight bytes of one row tile per stage (Q8_0: 2 x 544, Q4_0: 576, 16-bit: 4 x 512)
+    int w_tma;            // 1: every CTA tile lies in one segment and its weights arrive by one TMA box per stage
+};
+
+// weight tensor maps of the segments: a segment's row-tile buffer viewed as a [row tiles] x [stored bytes / 8] array
+// of 8-byte elements; one box = 8 row tiles x one stage's stored bytes (rows land tc_stage_raw_bytes(fmt) apart)
+struct alignas(64) TcMaps {
+    CUtensorMap w[3];
 };
 
 __host__ __device__ inline int tc_stage_raw_bytes(int fmt) {
@@ -203,7 +210,8 @@ __device__ __forceinline__ void tc_work(const TcArgs &a, int w, int &mt, int &nt
 
 template <int FA, int FB, class Epi>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ TcArgs a,
-                                                          const __grid_constant__ CUtensorMap xmap, Epi epi) {
+                                                          const __grid_constant__ CUtensorMap xmap,
+                                                          const __grid_constant__ TcMaps wm, Epi epi) {
     extern __shared__ uint8_t smem_raw[];
     // operand tiles need 1024-byte aligned shared-memory addresses (the swizzle reads address bits 7-9)
     uint8_t *smem = smem_raw + ((1024u - (tc::smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -239,7 +247,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
 
     if (warp == 0) {   // ------------------------------------------------------------------------- producer
         // lane r < 8 streams row tile r of the CTA tile (its stored k tiles are contiguous); lane 8 the activations
-        if (lane == 0) tc::prefetch_tmap(&xmap);
+        if (lane == 0) {
+            tc::prefetch_tmap(&xmap);
+            if (a.w_tma)
+                for (int i = 0; i < a.n_seg; ++i) tc::prefetch_tmap(&wm.w[i]);
+        }
         const uint64_t pol = tc::l2_evict_first_policy();
         int it = 0;
         bool ok = true;
@@ -257,11 +269,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
                 per = TC_BK / tile_k(sg.fmt);
                 base = sg.tiles + (size_t)rt * nkt * tb;
             }
+            int wseg = 0, wrt = 0;   // TMA mode: the CTA tile's segment and its first row tile there
+            if (a.w_tma && mt * 8 < total_rt) wseg = tc_seg_of(a, mt * 8, wrt);
+            const int wtb = tile_bytes(a.seg[wseg].fmt), wper = TC_BK / tile_k(a.seg[wseg].fmt);
             for (int ks = ks0; ks < ks1; ++ks, ++it) {
                 const int s = it % S;
                 if (it >= S && !tc::mbar_wait(EMPTY(s), ((it / S) - 1) & 1)) {
                     ok = false;
                     break;
+                }
+                if (a.w_tma) {   // two copies per stage: the weight box (8 row tiles) and the activation box
+                    if (lane == 0) {
+                        tc::mbar_expect_tx(FULL(s), (uint32_t)(8 * wper * wtb + a.bn * TC_BK * 2));
+                        tc::tma_load_2d_hint(tc::smem_addr(smem + a.raw_off + s * a.stage_raw), &wm.w[wseg],
+                                             ks * wper * wtb / 8, wrt, FULL(s), pol);
+                        tc::tma_load_2d(tc::smem_addr(smem + a.x_off + s * a.stage_x), &xmap, ks * TC_BK, nt * a.bn,
+                                        FULL(s));
+                    }
+                    continue;
                 }
                 const int kt0 = ks * per;
                 const int n = base ? max(0, min(per, nkt - kt0)) : 0;
@@ -271,7 +296,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
                 if (lane == 0) tc::mbar_expect_tx(FULL(s), (uint32_t)(bytes + a.bn * TC_BK * 2));
                 __syncwarp();
                 if (n > 0)
-                    tc::bulk_g2s(tc::smem_addr(smem + a.raw_off + s * a.stage_raw + lane * TC_RAW_ROW),
+                    tc::bulk_g2s(tc::smem_addr(smem + a.raw_off + s * a.stage_raw + lane * a.raw_row),
                                  base + (size_t)kt0 * tb, (uint32_t)(n * tb), FULL(s), pol);
                 if (lane == 8)
                     tc::tma_load_2d(tc::smem_addr(smem + a.x_off + s * a.stage_x), &xmap, ks * TC_BK, nt * a.bn,
@@ -324,6 +349,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             int mt, nt, sp, ks0, ks1;
             tc_work(a, w, mt, nt, sp, ks0, ks1);
             const int R = mt * 8 + rl;
+            int row_bytes = a.raw_row;   // TMA mode: rows of the box sit one stage of the tile's format apart
+            if (a.w_tma && R < total_rt) {
+                int rt_unused;
+                row_bytes = tc_stage_raw_bytes(a.seg[tc_seg_of(a, R, rt_unused)].fmt);
+            }
             for (int ks = ks0; ks < ks1; ++ks, ++it) {
                 const int s = it % S;
                 if (!tc::mbar_wait(FULL(s), (it / S) & 1)) {
@@ -332,7 +362,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
                 }
                 if (R < total_rt)
                     tc_convert_row_tile<FA, FB>(a, smem + a.a_off + s * a.stage_a,
-                                                smem + a.raw_off + s * a.stage_raw + rl * TC_RAW_ROW, R, rl, ks, lane);
+                                                smem + a.raw_off + s * a.stage_raw + rl * row_bytes, R, rl, ks, lane);
                 tc::fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(CONV(s));
@@ -446,6 +476,7 @@ __global__ void __launch_bounds__(256) k_tc_splitk_reduce(const __grid_constant_
 struct TcLaunch {
     TcArgs a;
     CUtensorMap xmap;
+    TcMaps wm;
     int fa, fb;
     int grid;
     size_t smem;
@@ -470,7 +501,7 @@ cudaError_t tc_launch_t(const TcLaunch &L, const Epi &epi, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    k_gemm_tc<FA, FB, Epi><<<L.grid, TC_THREADS, L.smem, st>>>(L.a, L.xmap, epi);
+    k_gemm_tc<FA, FB, Epi><<<L.grid, TC_THREADS, L.smem, st>>>(L.a, L.xmap, L.wm, epi);
     if (L.a.splits > 1) {
         const int64_t n = (int64_t)L.a.m_tiles * L.a.n_tiles * 64 * L.a.bn;
         k_tc_splitk_reduce<Epi><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(L.a, epi);

@@ -56,6 +56,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int 
             "r"(dst), "l"(tmap), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
+// the same with an L2 cache policy (weights streamed once: evict first)
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const void *tmap, int x, int y, uint32_t bar,
+                                                 uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3}], [%4], %5;" ::"r"(dst),
+        "l"(tmap), "r"(x), "r"(y), "r"(bar), "l"(pol)
+        : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
