@@ -137,16 +137,23 @@ __global__ void k_piece_scan(const StateDev *sp, int n, const float *feat, float
     if (k >= fd || !(q.seg_on && q.seg_budget > 0)) return;
     bool ready = q.ema_ready != 0;
     float e = s.ema[(size_t)b * fd + k];
-    for (int j = 0; j < n; ++j) {
-        const size_t t = (size_t)b * n + j;
-        const float f = feat[t * fd + k];
-        if (ready) {
-            hin[t * fd + k] = sc_hab_in(f, e);
-            e = sc_ema_next(e, f);
-        } else {   // the stream's first token: no habituated score, the EMA starts at f
-            hin[t * fd + k] = f;
-            e = f;
-            ready = true;
+    for (int j0 = 0; j0 < n; j0 += 8) {   // the features of 8 tokens loaded together, then the recurrence
+        float fv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) fv[i] = j0 + i < n ? feat[((size_t)b * n + j0 + i) * fd + k] : 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (j0 + i >= n) break;
+            const size_t t = (size_t)b * n + j0 + i;
+            const float f = fv[i];
+            if (ready) {
+                hin[t * fd + k] = sc_hab_in(f, e);
+                e = sc_ema_next(e, f);
+            } else {   // the stream's first token: no habituated score, the EMA starts at f
+                hin[t * fd + k] = f;
+                e = f;
+                ready = true;
+            }
         }
     }
     s.ema[(size_t)b * fd + k] = e;
@@ -189,30 +196,51 @@ __global__ void __launch_bounds__(SCORER_THREADS) k_piece_fc1(const ModelDev *mp
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int u = blockIdx.x * (SCORER_THREADS / 32) + warp;
     const float *w1 = m.sc_w1 + (size_t)min(u, hdn - 1) * fd;
+    const float *ln_w = m.sc_ln_w, *ln_b = m.sc_ln_b;
     float s0[PF_FC1_TOK], s1[PF_FC1_TOK];
 #pragma unroll
     for (int j = 0; j < PF_FC1_TOK; ++j) s0[j] = s1[j] = 0.f;
     for (int kc = 0; kc < fd; kc += PF_FC1_KC) {
+        float wv[PF_FC1_KC / 32];   // this lane's W1 elements of the chunk, loaded while the inputs are staged
+#pragma unroll
+        for (int i = 0; i < PF_FC1_KC / 32; ++i) {
+            const int k = kc + lane + 32 * i;
+            wv[i] = k < fd ? __ldg(w1 + k) : 0.f;
+        }
+        // this thread's inputs of the chunk: every load issued before the first use
+        constexpr int PER = PF_FC1_TOK * PF_FC1_KC / SCORER_THREADS;
+        float f0[PER], f1[PER], lw[PER], lb[PER];
+#pragma unroll
+        for (int r = 0; r < PER; ++r) {
+            const int i = threadIdx.x + r * SCORER_THREADS, tt = i / PF_FC1_KC, kk = i - tt * PF_FC1_KC, k = kc + kk;
+            const bool ok = tt < nt && k < fd;
+            f0[r] = ok ? __ldg(feat + (size_t)(t0 + tt) * fd + k) : 0.f;
+            f1[r] = ok ? __ldg(hin + (size_t)(t0 + tt) * fd + k) : 0.f;
+            lw[r] = ok ? __ldg(ln_w + k) : 0.f;
+            lb[r] = ok ? __ldg(ln_b + k) : 0.f;
+        }
         __syncthreads();   // the previous chunk is consumed (first pass: st is written)
-        for (int i = threadIdx.x; i < PF_FC1_TOK * PF_FC1_KC; i += SCORER_THREADS) {
-            const int tt = i / PF_FC1_KC, kk = i - tt * PF_FC1_KC, k = kc + kk;
+#pragma unroll
+        for (int r = 0; r < PER; ++r) {
+            const int i = threadIdx.x + r * SCORER_THREADS, tt = i / PF_FC1_KC, kk = i - tt * PF_FC1_KC, k = kc + kk;
             float v0 = 0.f, v1 = 0.f;
             if (tt < nt && k < fd) {
-                const float lw = m.sc_ln_w[k], lb = m.sc_ln_b[k];
                 const float4 q = st[tt];
-                v0 = sc_ln(feat[(size_t)(t0 + tt) * fd + k], q.x, q.z, lw, lb);
-                v1 = sc_ln(hin[(size_t)(t0 + tt) * fd + k], q.y, q.w, lw, lb);
+                v0 = sc_ln(f0[r], q.x, q.z, lw[r], lb[r]);
+                v1 = sc_ln(f1[r], q.y, q.w, lw[r], lb[r]);
             }
             ln0[tt][kk] = v0;
             ln1[tt][kk] = v1;
         }
         __syncthreads();
-        for (int kk = lane; kk < PF_FC1_KC && kc + kk < fd; kk += 32) {
-            const float wk = w1[kc + kk];
+#pragma unroll
+        for (int i = 0; i < PF_FC1_KC / 32; ++i) {
+            const int kk = lane + 32 * i;
+            if (kc + kk >= fd) break;
 #pragma unroll
             for (int j = 0; j < PF_FC1_TOK; ++j) {
-                s0[j] = sc_fc1_term(s0[j], wk, ln0[j][kk]);
-                s1[j] = sc_fc1_term(s1[j], wk, ln1[j][kk]);
+                s0[j] = sc_fc1_term(s0[j], wv[i], ln0[j][kk]);
+                s1[j] = sc_fc1_term(s1[j], wv[i], ln1[j][kk]);
             }
         }
     }

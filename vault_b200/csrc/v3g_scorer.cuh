@@ -100,7 +100,8 @@ __device__ void scorer_fc1_block(const ModelDev &m, int fd, const In0 &in0, cons
     if (u >= m.seg_hidden) return;
     const float *w1 = m.sc_w1 + (size_t)u * fd;
     float s0 = 0.f, s1 = 0.f;
-    for (int k = lane; k < fd; k += 32) {
+#pragma unroll 4
+    for (int k = lane; k < fd; k += 32) {   // unrolled: the loads of 4 steps in flight, the sums still in k order
         const float lw = m.sc_ln_w[k], lb = m.sc_ln_b[k], wk = w1[k];
         s0 = sc_fc1_term(s0, wk, sc_ln(in0(k), st[0], st[2], lw, lb));
         s1 = sc_fc1_term(s1, wk, sc_ln(in1(k), st[1], st[3], lw, lb));
