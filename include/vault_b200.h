@@ -123,8 +123,8 @@ V3G_API int v3g_step_host(v3g_state *s, const uint32_t *tokens, float *logits, u
 /* Stream n_tokens ids per sequence (device int32, row b at dev_ids + b * ld) through the state, computing the
  * lm head only for the last one (src/vault_v3_model.py:2163 prefill; the chunk-recurrent forward :1938-2116).
  * The prompt runs in window-aligned pieces (each layer's projections as tensor-core GEMMs over all of a piece's
- * tokens, one block-window attention launch) unless V3G_STATE_TOKEN_PREFILL is set or the model / state needs the
- * per-token path (F32 weight matrices, segment memory). */
+ * tokens, one block-window attention launch, the segment scorer over every token of the piece) unless
+ * V3G_STATE_TOKEN_PREFILL is set or a weight matrix is stored as F32 (those models stream token by token). */
 V3G_API int v3g_prefill(v3g_state *s, const int32_t *dev_ids, uint32_t n_tokens, uint64_t ld, float *dev_logits,
                 int32_t *dev_next, void *stream);
 /* Greedy decode on the device: feeds dev_first [batch], then each step's argmax, for n_steps steps, writing the
