@@ -9,9 +9,11 @@
 // CTA tile), the tokens its B operand (N = bn tokens, 16..256), the fp32 accumulator lives in tensor memory.
 //
 // One persistent CTA per SM walks the (128-row, bn-token) output tiles with warp-specialised roles:
-//   warp 0      producer: for every 64-wide k stage, lanes 0-7 bulk-copy the 8 row tiles' stored weight bytes (their
-//               k tiles are contiguous in HBM) and lane 8 loads the bn x 64 activation box with the tensor map
-//               (TMA, 128-byte swizzle), all completing on the stage's `full` mbarrier;
+//   warp 0      producer: for every 64-wide k stage, one TMA box of the weights (the segment's row-tile buffer viewed
+//               as [row tiles] x [stored bytes / 8] 8-byte elements; box = the CTA tile's 8 row tiles x one stage's
+//               stored bytes) and one TMA box of the bn x 64 fp16 activations (128-byte swizzle), both completing on
+//               the stage's `full` mbarrier.  A CTA tile that straddles two stacked matrices falls back to one bulk
+//               copy per row tile (lanes 0-7) plus the activation box (lane 8);
 //   warps 2-9   converters (one per row tile): dequantize the stage's weight bytes into the A operand (fp16, K-major, 128-byte
 //               swizzle) -- Q8_0 codes and Q4_0 nibbles times their fp16 block scale (times a per-matrix power of two
 //               that keeps small scales out of the fp16 subnormal range), 16-bit tiles copied -- then fence the
