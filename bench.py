@@ -152,18 +152,33 @@ def chat_prompt(seed: int, n_pin: int, total: int):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled during the timed region: every 10 ms through NVML
+    (read-only queries), or every 200 ms through nvidia-smi when NVML cannot be loaded."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits: hw_slowdown, hw_thermal_slowdown, sw_thermal_slowdown, sw_power_cap
+    NVML_BITS = (0x8, 0x40, 0x20, 0x4)
 
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.rows = []
         self.proc = None
+        self.nvml = None
+        self.stop = threading.Event()
 
     def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:  # noqa: BLE001
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
@@ -174,11 +189,27 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll(self):
+        n = self.nvml
+        while not self.stop.is_set():
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                mx = n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM)
+                rs = n.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+                self.rows.append([str(self.gpu), str(sm), str(mx), "", hex(rs)] +
+                                 ["Active" if rs & bit else "Not Active" for bit in self.NVML_BITS])
+            except Exception:  # noqa: BLE001
+                return
+            self.stop.wait(0.01)
+
     def _read(self):
         for ln in self.proc.stdout:
             self.rows.append([c.strip() for c in ln.split(",")])
 
     def __exit__(self, *a):
+        self.stop.set()
+        if self.nvml is not None:
+            self.t.join(timeout=2)
         if self.proc:
             self.proc.terminate()
             try:

@@ -46,6 +46,49 @@ __device__ __forceinline__ const kv_t *kv_row(const StateDev &s, int layer, int 
     return kvp(s, layer, b, ring_off(s, ks.par, value ? 2 : 0, g, j));
 }
 
+// K and V row bases of the visible key segments of (layer, sequence b, KV head g) -- sinks, segment bank, previous
+// chunk, current chunk, each [rows][D] -- and the cumulative key counts: computed once per work item, so the copy
+// loops do plain pointer arithmetic instead of re-reading the state descriptor around every cp.async
+struct KvRows {
+    const kv_t *k[4], *v[4];
+    int end[4];
+};
+__device__ __forceinline__ KvRows kv_rows(const StateDev &s, int layer, int b, int g, const KeySpan &ks) {
+    KvRows r;
+    r.k[0] = kvp(s, layer, b, sink_off(s, 1, g, 0));                    // rotated sink keys
+    r.v[0] = kvp(s, layer, b, sink_off(s, 2, g, 0));
+    r.k[1] = kvp(s, layer, b, bank_rot_off(s, g, 0));                   // rotated bank keys
+    r.v[1] = kvp(s, layer, b, bank_off(s, ks.bank_par, 1, g, 0));
+    r.k[2] = kvp(s, layer, b, ring_off(s, ks.par ^ 1, 0, g, 0));        // previous chunk (rotated keys)
+    r.v[2] = kvp(s, layer, b, ring_off(s, ks.par ^ 1, 2, g, 0));
+    r.k[3] = kvp(s, layer, b, ring_off(s, ks.par, 0, g, 0));            // current chunk
+    r.v[3] = kvp(s, layer, b, ring_off(s, ks.par, 2, g, 0));
+    r.end[0] = ks.n_sk;
+    r.end[1] = r.end[0] + ks.n_seg;
+    r.end[2] = r.end[1] + ks.n_prev;
+    r.end[3] = ks.total;
+    return r;
+}
+// the row of visible key j (the same rows as kv_row)
+template <int D>
+__device__ __forceinline__ const kv_t *kv_at(const KvRows &r, int j, bool value) {
+    const kv_t *base = value ? r.v[0] : r.k[0];
+    int j0 = 0;
+    if (j >= r.end[0]) {
+        base = value ? r.v[1] : r.k[1];
+        j0 = r.end[0];
+    }
+    if (j >= r.end[1]) {
+        base = value ? r.v[2] : r.k[2];
+        j0 = r.end[1];
+    }
+    if (j >= r.end[2]) {
+        base = value ? r.v[3] : r.k[3];
+        j0 = r.end[2];
+    }
+    return base + (size_t)(j - j0) * D;
+}
+
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
@@ -368,15 +411,15 @@ __device__ bool attn_span(const StateDev &s, const KeySpan &ks, int layer, float
         sm.m[tid] = -INFINITY;
         sm.l[tid] = 0.f;
     }
+    const KvRows kr = kv_rows(s, layer, b, g, ks);
     for (int j0 = jb; j0 < jb + nkeys; j0 += ATT_KPC) {
         const int nk = min(ATT_KPC, jb + nkeys - j0);
         const int nfar = ks.n_sk + ks.n_seg + ks.n_prev - j0;   // keys j < nfar are scored with the far query
         for (int c = tid; c < ATT_KPC * CH; c += nt) {
             const int j = c / CH, part = c - j * CH;
             if (j < nk) {
-                bool far;
-                cp_async16(&sm.k[j * KP + part * 8], kv_row(s, layer, b, g, ks, j0 + j, false, far) + part * 8);
-                cp_async16(&sm.v[j * KP + part * 8], kv_row(s, layer, b, g, ks, j0 + j, true, far) + part * 8);
+                cp_async16(&sm.k[j * KP + part * 8], kv_at<D>(kr, j0 + j, false) + part * 8);
+                cp_async16(&sm.v[j * KP + part * 8], kv_at<D>(kr, j0 + j, true) + part * 8);
             } else {
                 *reinterpret_cast<uint4 *>(&sm.v[j * KP + part * 8]) = make_uint4(0u, 0u, 0u, 0u);
             }
