@@ -469,6 +469,7 @@ __global__ void __launch_bounds__(256) k_prefill_attn(const StateDev *sp, int la
     const int H = s.H, grp = H / s.G, h = g * grp + warp;
     const int W = s.W, c0 = (int)(p0 % W);
     const KeySpan ks = key_span(s, b, p0);
+    const KvRows kr = kv_rows(s, layer, b, g, ks);   // row bases: the staging loop reads no state fields
     const int nfar = ks.n_sk + ks.n_seg + ks.n_prev;
     const int jmax = min(n, j0 + 16);
     const int ncur = c0 + jmax;
@@ -503,9 +504,8 @@ __global__ void __launch_bounds__(256) k_prefill_attn(const StateDev *sp, int la
         for (int c = threadIdx.x; c < TK * (D / 8); c += blockDim.x) {
             const int kk = c / (D / 8), part = c - kk * (D / 8);
             if (k0 + kk < nkeys) {
-                bool far;
-                cp_async16(kd + kk * KP + part * 8, kv_row(s, layer, b, g, ks, base + k0 + kk, false, far) + part * 8);
-                cp_async16(vd + kk * KP + part * 8, kv_row(s, layer, b, g, ks, base + k0 + kk, true, far) + part * 8);
+                cp_async16(kd + kk * KP + part * 8, kv_at<D>(kr, base + k0 + kk, false) + part * 8);
+                cp_async16(vd + kk * KP + part * 8, kv_at<D>(kr, base + k0 + kk, true) + part * 8);
             } else {   // past the keys: zero values (probability 0 must meet a finite value)
                 *reinterpret_cast<uint4 *>(vd + kk * KP + part * 8) = make_uint4(0u, 0u, 0u, 0u);
                 *reinterpret_cast<uint4 *>(kd + kk * KP + part * 8) = make_uint4(0u, 0u, 0u, 0u);
