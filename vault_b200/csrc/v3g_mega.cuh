@@ -159,7 +159,7 @@ __device__ __forceinline__ uint64_t l2_evict_first() {
     return pol;
 }
 
-// expect `bytes` on bar and copy them global -> shared (no multicast: a plain CTA-local bulk copy) under L2 policy pol
+// expect `bytes` on bar and copy them global -> shared (a plain CTA-local bulk copy of this GPU's memory) under L2 policy pol
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar, uint64_t pol) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
     asm volatile(

@@ -6,7 +6,7 @@
 // CU_TENSOR_MAP_SWIZZLE_128B produce exactly this layout, and the weight converters write it by hand.  Every atom
 // base is 1024-byte aligned (the swizzle is applied on shared-memory address bits 4-6 from bits 7-9).
 //
-// No copy here uses cluster multicast: every load is a plain CTA-local copy of this GPU's own memory.
+// Every load here is a plain CTA-local copy of this GPU's own memory (one destination CTA per copy).
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
