@@ -67,3 +67,17 @@ def test_chat_prompt_pins_its_system_prefix():
     body = ids[512:]
     gaps = [i for i, t in enumerate(body) if t == 198]
     assert len(gaps) > 4096 // 49
+
+
+def test_clock_summary_reads_nvml_rows():
+    """The clock record of a bench line: NVML samples (sm clock, max clock, event-reason bits as Active flags) give
+    the median SM clock, the max clock and the names of the active throttle reasons."""
+    c = bench.ClockSampler(0)
+    bits = bench.ClockSampler.NVML_BITS
+    for sm, reasons in ((1965, 0x0), (1950, 0x4), (1965, 0x0)):
+        c.rows.append(["0", str(sm), "1965", "", hex(reasons)] +
+                      ["Active" if reasons & b else "Not Active" for b in bits])
+    s = c.summary()
+    assert s["sm_mhz"] == 1965 and s["sm_max_mhz"] == 1965 and s["samples"] == 3
+    assert s["reasons"] == ["sw_power_cap"]
+    assert bench.ClockSampler(0).summary()["reasons"] == ["unavailable"]
