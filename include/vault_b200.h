@@ -133,6 +133,10 @@ V3G_API int v3g_generate(v3g_state *s, const int32_t *dev_first, uint32_t n_step
                  void *stream);
 /* Synchronize `stream` and read the sticky device status bits (V3G_STATUS_*); clears them when clear != 0. */
 V3G_API int v3g_status(v3g_state *s, uint32_t *bits, int clear, void *stream);
+/* Asynchronous form of v3g_status for callers that poll between steps: enqueues on `stream` a copy of the sticky
+ * status bits into dst (device memory or pinned host memory, 4 bytes) and returns without synchronizing; the value
+ * is valid once the stream has passed the copy. */
+V3G_API int v3g_status_copy(v3g_state *s, uint32_t *dst, void *stream);
 
 /* Snapshot of one sequence's streaming bookkeeping (VAULTv3State fields, src/vault_v3_model.py:974-1011);
  * mem_pos / mem_score receive up to `cap` bank entries in chronological order.  Synchronizes `stream`. */

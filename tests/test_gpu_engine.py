@@ -211,3 +211,26 @@ def test_chunked_prefill_matches_token_prefill(name, seg_budget, case_files):
             outs.append(np.stack(got, axis=1))
         assert np.abs(outs[0] - outs[1]).max() <= _tol(name), (sp, np.abs(outs[0] - outs[1]).max())
         assert banks[0] == banks[2] and banks[1] == banks[3], (sp, banks)   # pins and bank after prefill / stream
+
+
+def test_status_copy_matches_status(case_files):
+    """The step checks the device status without synchronizing: v3g_status_copy enqueues a copy of the sticky
+    bits that a later step reads.  After a stream with segment memory (every step queues such a copy) the copied
+    word equals what the synchronizing v3g_status returns, and no step raised."""
+    import ctypes as C
+
+    from vault_b200 import _lib
+    name = "tiny_seg_q8_0"
+    spec = CASES[name]
+    cfg = case_config(spec)
+    m = engine(case_files, name)
+    ids = torch.from_numpy(case_ids(spec, cfg))[:, :48]
+    st = m.new_state(ids.shape[0])
+    assert st.seg_active
+    for t in range(ids.shape[1]):
+        m.step(ids[:, t], st)
+    host = torch.full((1,), -1, dtype=torch.int32).pin_memory()
+    _lib.check(_lib.lib().v3g_status_copy(st._h, C.c_void_p(host.data_ptr()),
+                                          C.c_void_p(torch.cuda.current_stream().cuda_stream)), "v3g_status_copy")
+    torch.cuda.synchronize()
+    assert int(host[0]) == st.status() == 0

@@ -922,6 +922,13 @@ extern "C" int v3g_status(v3g_state *s, uint32_t *bits, int clear, void *stream)
     return V3G_OK;
 }
 
+extern "C" int v3g_status_copy(v3g_state *s, uint32_t *dst, void *stream) {
+    if (!s || !dst) return fail(V3G_E_ARG, "null argument");
+    CUDA_TRY(cudaMemcpyAsync(dst, reinterpret_cast<uint8_t *>(s->host.step) + offsetof(StepCtl, status), 4,
+                             cudaMemcpyDefault, (cudaStream_t)stream));
+    return V3G_OK;
+}
+
 extern "C" int v3g_seq_info(v3g_state *s, uint32_t b, v3g_seq_info_t *info, int64_t *mem_pos, float *mem_score,
                             uint32_t cap, void *stream) {
     if (!s || !info || b >= (uint32_t)s->B) return fail(V3G_E_ARG, "invalid argument");

@@ -112,7 +112,29 @@ class VAULTv3State:
         return int(bits.value)
 
     def check(self) -> None:
-        bits = self.status()
+        """Synchronize the engine stream and raise if the device set a status bit."""
+        self._raise_for(self.status())
+
+    def _poll_status(self) -> None:
+        """Raise for status bits of an earlier step whose asynchronous copy has landed; never waits."""
+        ev = getattr(self, "_status_event", None)
+        if ev is not None and ev.query():
+            self._status_event = None
+            self._raise_for(int(self._status_host[0]))
+
+    def _queue_status_copy(self) -> None:
+        """Enqueue a copy of the sticky status bits into pinned host memory (one copy in flight at a time)."""
+        if getattr(self, "_status_event", None) is not None:
+            return
+        if getattr(self, "_status_host", None) is None:
+            self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        _lib.check(_lib.lib().v3g_status_copy(self._h, C.c_void_p(self._status_host.data_ptr()), _stream()),
+                   "v3g_status_copy")
+        self._status_event = torch.cuda.Event()
+        self._status_event.record()   # the current stream: the one _stream() hands the engine
+
+    @staticmethod
+    def _raise_for(bits: int) -> None:
         if bits & _lib.V3G_STATUS_RESONANCE:
             raise NotImplementedError("shingle-resonance bias would be active for this stream (a non-pinned "
                                       "<|im_end|> inside the last 38 tokens with > 2 bank segments); the engine "
@@ -176,16 +198,20 @@ class VAULTv3ForCausalLM:
 
     @torch.no_grad()
     def step(self, token_ids: torch.Tensor, st: VAULTv3State, vault_on: bool = False) -> torch.Tensor:
-        """token_ids [B] -> logits [B, V] (fp32, on the engine device)."""
+        """token_ids [B] -> logits [B, V] (fp32, on the engine device).  The device status bits are checked
+        without synchronizing: each step with segment memory enqueues a copy of them, and a later step (or
+        st.check(), which synchronizes) raises once that copy shows a bit -- NotImplementedError when the
+        shingle-resonance bias would have been active, RuntimeError otherwise."""
         _ = vault_on
         ids = self._ids(token_ids.reshape(-1))
         if ids.numel() != st.batch:
             raise ValueError(f"expected {st.batch} token ids, got {ids.numel()}")
+        st._poll_status()
         out = torch.empty(st.batch, self.cfg.vocab_size, dtype=torch.float32, device=self.device)
         _lib.check(_lib.lib().v3g_step(st._h, C.c_void_p(ids.data_ptr()), C.c_void_p(out.data_ptr()), None,
                                        _stream()), "v3g_step")
         if st.seg_active:
-            st.check()
+            st._queue_status_copy()
         return out
 
     @torch.no_grad()
