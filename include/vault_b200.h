@@ -177,6 +177,15 @@ V3G_API int v3g_decode_pass(v3g_state *s, int want_lm, void *stream);
  * the library holds until exit; more rows fail with V3G_E_LIMIT.  It runs on the current device; its first call
  * on a device looks up the array's device address, so make that first call before any stream capture.  All calls
  * share the array (cleared at the start of each call): calls that overlap on the GPU race. */
+/* Top-k (k <= 64) + temperature sampling of `rows` logit rows (row b at dev_logits + b * ld, `vocab` entries) with
+ * a caller-held xorshift64 state per row (dev_rng[rows], updated in place): v3_sample_topk (runtime/vault3.h:221,
+ * runtime/vault3.c:3204-3230) on the device, same candidate order (value, then lower index), the reference's own
+ * exponential and the same draw.  temp <= 0 or k <= 1 gives the greedy token and leaves dev_rng untouched (it may
+ * then be NULL).  NaN logits are never candidates; a row without a finite logit gives token 0.  Tokens go to
+ * dev_tokens[rows]. */
+V3G_API int v3g_sample_topk(const float *dev_logits, uint32_t rows, uint32_t vocab, uint64_t ld, uint32_t k, float temp,
+                            uint64_t *dev_rng, int32_t *dev_tokens, void *stream);
+
 #define V3G_NOALLOC_MAX_ROWS 4096
 V3G_API int v3g_argmax_noalloc(const float *dev_logits, uint32_t rows, uint32_t vocab, uint64_t ld, int32_t *dev_tokens,
                                void *stream);

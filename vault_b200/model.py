@@ -27,6 +27,23 @@ def _stream() -> C.c_void_p:
     return C.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
+def sample_topk(logits: torch.Tensor, k: int, temp: float, rng: torch.Tensor) -> torch.Tensor:
+    """Top-k (k <= 64) + temperature sampling of logit rows on the device: v3_sample_topk (runtime/vault3.c:3204-3230)
+    per row.  logits: [B, V] fp32 on the GPU; rng: [B] int64 xorshift64 states on the same device (the reference's
+    uint64 state as bits), updated in place; returns int32 tokens [B].  temp <= 0 or k <= 1: greedy."""
+    if logits.dim() != 2 or logits.dtype != torch.float32 or not logits.is_cuda or logits.stride(1) != 1:
+        raise ValueError("logits must be a [B, V] fp32 CUDA tensor with contiguous rows")
+    if rng.shape != (logits.shape[0],) or rng.dtype != torch.int64 or rng.device != logits.device or \
+            not rng.is_contiguous():
+        raise ValueError("rng must be a contiguous [B] int64 tensor on the logits' device")
+    out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    with torch.cuda.device(logits.device):
+        _lib.check(_lib.lib().v3g_sample_topk(C.c_void_p(logits.data_ptr()), logits.shape[0], logits.shape[1],
+                                              logits.stride(0), int(k), float(temp), C.c_void_p(rng.data_ptr()),
+                                              C.c_void_p(out.data_ptr()), _stream()), "v3g_sample_topk")
+    return out
+
+
 class VAULTv3State:
     """Fixed-size streaming state held in a device arena (the reference's VAULTv3State / v3_state)."""
 
