@@ -131,6 +131,14 @@ V3G_API int v3g_prefill(v3g_state *s, const int32_t *dev_ids, uint32_t n_tokens,
  * produced tokens to dev_out (row b at dev_out + b * ld).  No host round trip between steps. */
 V3G_API int v3g_generate(v3g_state *s, const int32_t *dev_first, uint32_t n_steps, int32_t *dev_out, uint64_t ld,
                  void *stream);
+/* Sampled decode on the device, the generation loop of runtime/vault3_host.c:586-606 with --temp / --topk: feeds
+ * dev_first [batch], then for n_steps steps draws each sequence's next token from that step's logits with the
+ * v3g_sample_topk rule (k capped at 64; temp <= 0 or k <= 1 is greedy), writing the tokens to dev_out (row b at
+ * dev_out + b * ld) and advancing the per-sequence xorshift states dev_rng [batch].  No host round trip between
+ * steps; all n_steps run (the loop's stop at <|im_end|> / BOS is the caller's).  The repetition penalty and the
+ * output governor of that loop are not applied. */
+V3G_API int v3g_generate_sampled(v3g_state *s, const int32_t *dev_first, uint32_t n_steps, int32_t *dev_out,
+                                 uint64_t ld, uint32_t k, float temp, uint64_t *dev_rng, void *stream);
 /* Synchronize `stream` and read the sticky device status bits (V3G_STATUS_*); clears them when clear != 0. */
 V3G_API int v3g_status(v3g_state *s, uint32_t *bits, int clear, void *stream);
 /* Asynchronous form of v3g_status for callers that poll between steps: enqueues on `stream` a copy of the sticky

@@ -45,3 +45,36 @@ def test_sample_topk_skips_nan_rows():
     assert tok[0] == 0
     otok, _ = so.sample_topk(logits[1].cpu().numpy(), 4, 1.0, 9)
     assert tok[1] == otok
+
+
+def test_generate_sampled_matches_step_then_sample(case_files):
+    """v3g_generate_sampled (the on-device loop) against step -> sample_topk on the host side, two sequences with
+    their own xorshift states: same tokens, same final states; every draw of the host loop also matches the sampler
+    oracle on that step's logits."""
+    from tests.golden.cases import CASES, case_config, case_ids
+    from tests.test_gpu_engine import engine
+    from vault_b200.model import sample_topk
+    torch.cuda.set_device(0)
+    m = engine(case_files, "mini_gqa_q8_0")
+    spec = CASES["mini_gqa_q8_0"]
+    ids = torch.from_numpy(case_ids(spec, case_config(spec)))[:1, :40]
+    ids = torch.cat([ids, ids.roll(3, dims=1)])
+    k, temp, n = 20, 1.5, 24
+    lg, st = m.prefill(ids)
+    rng = torch.tensor([0, 0x1234567], dtype=torch.int64, device="cuda")
+    first = sample_topk(lg, k, temp, rng)
+    rng_a, rng_b = rng.clone(), rng.clone()
+    gen = m.generate(st, first, n, top_k=k, temperature=temp, rng=rng_a).cpu()
+    _, st2 = m.prefill(ids)
+    states = [_to_u64(x) for x in rng_b.cpu().tolist()]
+    tok, chain = first, []
+    for _ in range(n):
+        logits = m.step(tok, st2)
+        tok = sample_topk(logits, k, temp, rng_b)
+        for r in range(2):
+            otok, states[r] = so.sample_topk(logits[r].cpu().numpy(), k, temp, states[r])
+            assert int(tok[r]) == otok
+        chain.append(tok.cpu())
+    assert torch.equal(gen, torch.stack(chain, 1))
+    assert torch.equal(rng_a, rng_b) and [_to_u64(x) for x in rng_a.cpu().tolist()] == states
+    assert not torch.equal(rng_a, rng)

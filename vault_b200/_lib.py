@@ -61,6 +61,7 @@ _SIGS = {
     "v3g_attention": (C.c_int, [_P, C.c_uint32, _P]),
     "v3g_status_copy": (C.c_int, [_P, _P, _P]),
     "v3g_sample_topk": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint32, C.c_float, _P, _P, _P]),
+    "v3g_generate_sampled": (C.c_int, [_P, _P, C.c_uint32, _P, C.c_uint64, C.c_uint32, C.c_float, _P, _P]),
     "v3g_gemm_work_size": (C.c_size_t, [_P, C.c_uint32, C.c_uint32]),
     "v3g_gemm": (C.c_int, [_P, C.c_uint32, _P, C.c_uint32, _P, _P, C.c_size_t, _P]),
     "v3g_argmax_noalloc": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.c_uint64, _P, _P]),

@@ -909,6 +909,24 @@ extern "C" int v3g_generate(v3g_state *s, const int32_t *dev_first, uint32_t n_s
     return rc != V3G_OK ? rc : rc2;
 }
 
+extern "C" int v3g_generate_sampled(v3g_state *s, const int32_t *dev_first, uint32_t n_steps, int32_t *dev_out,
+                                    uint64_t ld, uint32_t k, float temp, uint64_t *dev_rng, void *stream) {
+    if (!s || !dev_first || !dev_out || !dev_rng) return fail(V3G_E_ARG, "null argument");
+    if (n_steps > ld && s->B > 1) return fail(V3G_E_ARG, "v3g_generate_sampled: ld below n_steps");
+    cudaStream_t st = (cudaStream_t)stream;
+    const ModelDev &md = s->m->host;
+    CUDA_TRY(cudaMemcpyAsync(s->host.tok_in, dev_first, (size_t)s->B * 4, cudaMemcpyDeviceToDevice, st));
+    int rc = set_step_io(s, nullptr, 0, nullptr, 0, st);
+    if (rc != V3G_OK) return rc;
+    // each step's greedy token in tok_in is replaced by the draw from that step's logits before the next step reads it
+    for (uint32_t i = 0; i < n_steps; ++i) {
+        if ((rc = run_step(s, true, st)) != V3G_OK) return rc;
+        CUDA_TRY(launch_sample_topk(s->host.logits, (uint32_t)s->B, (uint32_t)md.vocab, (uint64_t)md.vocab, k, temp,
+                                    dev_rng, s->host.tok_in, dev_out + i, (int64_t)ld, st));
+    }
+    return V3G_OK;
+}
+
 extern "C" int v3g_status(v3g_state *s, uint32_t *bits, int clear, void *stream) {
     if (!s || !bits) return fail(V3G_E_ARG, "null argument");
     CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));

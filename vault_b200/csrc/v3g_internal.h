@@ -104,6 +104,10 @@ cudaError_t launch_boundary(const v3g_model *m, v3g_state *s, cudaStream_t st);
 // final RMSNorm + tied lm head of B rows (row b at x + b * x_ld) into the state's logits, and their argmax keys
 cudaError_t launch_lm_head(const v3g_model *m, v3g_state *s, const float *x, int x_ld, cudaStream_t st);
 cudaError_t launch_argmax_only(const v3g_model *m, v3g_state *s, cudaStream_t st);
+// top-k + temperature draw per logit row (v3g_sample.cu); out, when not null, also receives row b's token at
+// out[b * out_ld]
+cudaError_t launch_sample_topk(const float *logits, uint32_t rows, uint32_t vocab, uint64_t ld, uint32_t k, float temp,
+                               uint64_t *rng, int32_t *tokens, int32_t *out, int64_t out_ld, cudaStream_t st);
 cudaError_t launch_step_begin(const v3g_model *m, v3g_state *s, bool boundary, cudaStream_t st);
 cudaError_t launch_scorer(const v3g_model *m, v3g_state *s, cudaStream_t st);
 // batched decode step (B > 8) with every projection on the tensor-core GEMM (v3g_prefill.cu)

@@ -54,10 +54,15 @@ __device__ __forceinline__ uint64_t logit_key(float v, uint32_t i) {
     return ((uint64_t)float_key(v) << 32) | (uint64_t)(0xFFFFFFFFu - i);
 }
 
+// tokens[row] gets the draw; out (when not null) also gets it at out[row * out_ld] (the generation token sink)
 __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample_topk(const float *logits, uint32_t vocab, uint64_t ld,
                                                                uint32_t k, float temp, uint64_t *rng,
-                                                               int32_t *tokens) {
+                                                               int32_t *tokens, int32_t *out, int64_t out_ld) {
     const int tid = threadIdx.x, nt = blockDim.x;
+    auto emit = [&](int32_t tok) {
+        tokens[blockIdx.x] = tok;
+        if (out) out[(int64_t)blockIdx.x * out_ld] = tok;
+    };
     const float *lg = logits + (size_t)blockIdx.x * ld;
     __shared__ unsigned int hist[256];
     __shared__ uint64_t sel[SAMPLE_KMAX], sorted[SAMPLE_KMAX];
@@ -78,7 +83,7 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample_topk(const float *log
         }
         atomicMax(&best, b);
         __syncthreads();
-        if (tid == 0) tokens[blockIdx.x] = best ? (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu)) : 0;
+        if (tid == 0) emit(best ? (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu)) : 0);
         return;
     }
     const uint32_t kk = k > (uint32_t)SAMPLE_KMAX ? (uint32_t)SAMPLE_KMAX : k;
@@ -146,7 +151,7 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample_topk(const float *log
     __syncthreads();
     if (tid != 0) return;
     if (n == 0) {   // no finite logit
-        tokens[blockIdx.x] = 0;
+        emit(0);
         return;
     }
     float p[SAMPLE_KMAX];
@@ -172,7 +177,13 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample_topk(const float *log
             break;
         }
     }
-    tokens[blockIdx.x] = tok;
+    emit(tok);
+}
+
+cudaError_t launch_sample_topk(const float *logits, uint32_t rows, uint32_t vocab, uint64_t ld, uint32_t k, float temp,
+                               uint64_t *rng, int32_t *tokens, int32_t *out, int64_t out_ld, cudaStream_t st) {
+    k_sample_topk<<<rows, SAMPLE_THREADS, 0, st>>>(logits, vocab, ld, k, temp, rng, tokens, out, out_ld);
+    return cudaGetLastError();
 }
 
 }  // namespace v3g
@@ -185,8 +196,7 @@ extern "C" int v3g_sample_topk(const float *dev_logits, uint32_t rows, uint32_t 
         return v3g_fail(V3G_E_ARG, "v3g_sample_topk: null pointer");
     if (vocab == 0 || ld < vocab) return v3g_fail(V3G_E_ARG, "v3g_sample_topk: vocab must be > 0 and <= ld");
     if (rows == 0) return V3G_OK;
-    k_sample_topk<<<rows, SAMPLE_THREADS, 0, (cudaStream_t)stream>>>(dev_logits, vocab, ld, k, temp, dev_rng,
-                                                                    dev_tokens);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_sample_topk(dev_logits, rows, vocab, ld, k, temp, dev_rng, dev_tokens, nullptr, 0,
+                                             (cudaStream_t)stream);
     return e == cudaSuccess ? V3G_OK : v3g_fail(V3G_E_CUDA, cudaGetErrorString(e));
 }

@@ -271,12 +271,24 @@ class VAULTv3ForCausalLM:
     __call__ = forward
 
     @torch.no_grad()
-    def generate(self, st: VAULTv3State, first_tokens: torch.Tensor, n_steps: int) -> torch.Tensor:
-        """Greedy decode n_steps tokens on the device starting from first_tokens [B]; returns int32 [B, n_steps]."""
+    def generate(self, st: VAULTv3State, first_tokens: torch.Tensor, n_steps: int, top_k: int = 1,
+                 temperature: float = 0.0, rng: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Decode n_steps tokens on the device starting from first_tokens [B]; returns int32 [B, n_steps].
+        Greedy by default; with temperature > 0 and top_k > 1 every token is drawn by sample_topk's rule (the
+        reference's v3_sample_topk) from the per-sequence xorshift states rng ([B] int64, advanced in place)."""
         first = self._ids(first_tokens.reshape(-1))
         out = torch.empty(st.batch, n_steps, dtype=torch.int32, device=self.device)
-        _lib.check(_lib.lib().v3g_generate(st._h, C.c_void_p(first.data_ptr()), n_steps, C.c_void_p(out.data_ptr()),
-                                           n_steps, _stream()), "v3g_generate")
+        if temperature > 0.0 and top_k > 1:
+            if rng is None or rng.shape != (st.batch,) or rng.dtype != torch.int64 or rng.device != out.device \
+                    or not rng.is_contiguous():
+                raise ValueError("sampled generation needs rng: a contiguous [B] int64 tensor on the model's device")
+            _lib.check(_lib.lib().v3g_generate_sampled(st._h, C.c_void_p(first.data_ptr()), n_steps,
+                                                       C.c_void_p(out.data_ptr()), n_steps, int(top_k),
+                                                       float(temperature), C.c_void_p(rng.data_ptr()), _stream()),
+                       "v3g_generate_sampled")
+        else:
+            _lib.check(_lib.lib().v3g_generate(st._h, C.c_void_p(first.data_ptr()), n_steps,
+                                               C.c_void_p(out.data_ptr()), n_steps, _stream()), "v3g_generate")
         if st.seg_active:
             st.check()
         return out
