@@ -87,6 +87,27 @@ typedef struct {
     uint64_t device_bytes;            /* device memory held by the model */
 } v3g_model_info;
 
+/* CAAI output governor (runtime/vault3.h:191-216).  The rules are built on the host (v3g_gov_add_rule,
+ * v3g_gov_arm_system) and passed by value to the device calls; the stream state (canonical history of the emitted
+ * text, an unfinished UTF-8 sequence, the raw byte tail) is one v3g_gov_stream_t per sequence in device memory,
+ * all zero at the start of a stream. */
+#define V3G_GOV_MAX_RULES 8
+#define V3G_GOV_RULE_CAP 32
+#define V3G_GOV_HIST_CAP 64
+#define V3G_GOV_RAW_CAP 96
+typedef struct {
+    uint32_t n_rules;                                   /* 0: the governor is off */
+    uint32_t rule_len[V3G_GOV_MAX_RULES];
+    uint8_t rules[V3G_GOV_MAX_RULES][V3G_GOV_RULE_CAP];  /* canonical patterns */
+} v3g_gov_rules_t;
+typedef struct {
+    uint32_t hist_len, utf8_len, raw_len, reserved;
+    uint8_t hist[V3G_GOV_HIST_CAP];
+    uint8_t utf8_rem[4];
+    uint8_t raw_tail[V3G_GOV_RAW_CAP];
+    uint8_t pad[12];
+} v3g_gov_stream_t;
+
 /* Parse + validate a VLT3 buffer (same rules as v3_load, runtime/vault3.c:273-455; runtime/vault3.h:89) and
  * upload it to `device`, re-tiled for the decode kernels.  verify_crc = 1 also checks every tensor CRC32.
  * max_sink: cap of the ChatML auto-pinned prefix (the Python reference's VAULTv3Config.max_sink, default 512;
@@ -134,11 +155,14 @@ V3G_API int v3g_generate(v3g_state *s, const int32_t *dev_first, uint32_t n_step
 /* Sampled decode on the device, the generation loop of runtime/vault3_host.c:586-606 with --temp / --topk: feeds
  * dev_first [batch], then for n_steps steps draws each sequence's next token from that step's logits with the
  * v3g_sample_topk rule (k capped at 64; temp <= 0 or k <= 1 is greedy), writing the tokens to dev_out (row b at
- * dev_out + b * ld) and advancing the per-sequence xorshift states dev_rng [batch].  No host round trip between
- * steps; all n_steps run (the loop's stop at <|im_end|> / BOS is the caller's).  The repetition penalty and the
- * output governor of that loop are not applied. */
+ * dev_out + b * ld) and advancing the per-sequence xorshift states dev_rng [batch].  With gov (rules, n_rules > 0)
+ * and dev_gov (stream states [batch]) each step's logits are first masked by v3g_govern_logits with the loop's
+ * guard (16 when temp <= 0 or k < 16, else min(k, 64)) and each drawn token is committed by v3g_gov_commit.  No
+ * host round trip between steps; all n_steps run (the loop's stop at <|im_end|> / BOS is the caller's).  The
+ * loop's repetition penalty is not applied. */
 V3G_API int v3g_generate_sampled(v3g_state *s, const int32_t *dev_first, uint32_t n_steps, int32_t *dev_out,
-                                 uint64_t ld, uint32_t k, float temp, uint64_t *dev_rng, void *stream);
+                                 uint64_t ld, uint32_t k, float temp, uint64_t *dev_rng, const v3g_gov_rules_t *gov,
+                                 v3g_gov_stream_t *dev_gov, void *stream);
 /* Synchronize `stream` and read the sticky device status bits (V3G_STATUS_*); clears them when clear != 0. */
 V3G_API int v3g_status(v3g_state *s, uint32_t *bits, int clear, void *stream);
 /* Asynchronous form of v3g_status for callers that poll between steps: enqueues on `stream` a copy of the sticky
@@ -193,6 +217,24 @@ V3G_API int v3g_decode_pass(v3g_state *s, int want_lm, void *stream);
  * dev_tokens[rows]. */
 V3G_API int v3g_sample_topk(const float *dev_logits, uint32_t rows, uint32_t vocab, uint64_t ld, uint32_t k, float temp,
                             uint64_t *dev_rng, int32_t *dev_tokens, void *stream);
+
+/* Governor rules (host only, no device call).  v3g_gov_init: no rules (v3_gov_init).  v3g_gov_add_rule: canonicalize
+ * pat and add it unless present (v3_gov_add_rule, runtime/vault3.c:2933-2957): V3G_E_SIZE when the canonical form is
+ * shorter than 4 bytes, V3G_E_LIMIT when 8 rules are held.  v3g_gov_arm_system: reset, then derive the rules from a
+ * system prompt that states a prohibition (v3_gov_arm_system, runtime/vault3.c:2970-3013). */
+V3G_API void v3g_gov_init(v3g_gov_rules_t *g);
+V3G_API int v3g_gov_add_rule(v3g_gov_rules_t *g, const uint8_t *pat, size_t len);
+V3G_API void v3g_gov_arm_system(v3g_gov_rules_t *g, const uint8_t *sys_text, size_t len);
+/* Mask, in place, every candidate token whose bytes would complete a rule (forward, reversed, or inside a base64 /
+ * hex tail) after that row's stream: v3_govern_logits (runtime/vault3.c:3133-3181) per row, up to 4 passes over the
+ * top-k (k = top_k_guard, 0 or > 64 -> 64) logits above -3e38, a masked logit becoming -3.4e38.  Rows at
+ * dev_logits + b * ld with the model's vocabulary; dev_streams[rows].  Logits are taken to be NaN-free. */
+V3G_API int v3g_govern_logits(const v3g_model *m, const v3g_gov_rules_t *rules, const v3g_gov_stream_t *dev_streams,
+                              float *dev_logits, uint32_t rows, uint64_t ld, uint32_t top_k_guard, void *stream);
+/* Append each row's chosen token to its stream (v3_gov_commit, runtime/vault3.c:3183-3194): EOS, <|im_start|> and
+ * <|im_end|> reset the stream; nothing happens while rules->n_rules == 0. */
+V3G_API int v3g_gov_commit(const v3g_model *m, const v3g_gov_rules_t *rules, v3g_gov_stream_t *dev_streams,
+                           const int32_t *dev_tokens, uint32_t rows, void *stream);
 
 #define V3G_NOALLOC_MAX_ROWS 4096
 V3G_API int v3g_argmax_noalloc(const float *dev_logits, uint32_t rows, uint32_t vocab, uint64_t ld, int32_t *dev_tokens,

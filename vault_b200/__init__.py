@@ -11,11 +11,11 @@ from .vlt3 import VLT3Error, read_vlt3, vlt3_config, write_vlt3
 
 def __getattr__(name):
     # torch-dependent classes load lazily so the format tools work without CUDA
-    if name in ("VAULTv3ForCausalLM", "VAULTv3State", "sample_topk"):
+    if name in ("Governor", "VAULTv3ForCausalLM", "VAULTv3State", "sample_topk"):
         from . import model
         return getattr(model, name)
     raise AttributeError(name)
 
 
-__all__ = ["VAULTv3Config", "VAULTv3ForCausalLM", "VAULTv3State", "VLT3Error", "read_vlt3", "sample_topk",
+__all__ = ["Governor", "VAULTv3Config", "VAULTv3ForCausalLM", "VAULTv3State", "VLT3Error", "read_vlt3", "sample_topk",
            "vlt3_config", "write_vlt3"]

@@ -36,6 +36,13 @@ class SeqInfo(C.Structure):
                                           "ema_ready", "seg_budget")] + [("pos", C.c_uint64)]
 
 
+class GovRules(C.Structure):
+    """v3g_gov_rules_t: the governor's canonical patterns (the rule part of runtime/vault3.h:198-209 v3_governor)."""
+    _fields_ = [("n_rules", C.c_uint32), ("rule_len", C.c_uint32 * 8), ("rules", (C.c_uint8 * 32) * 8)]
+
+
+GOV_STREAM_BYTES = 192   # sizeof(v3g_gov_stream_t)
+
 _P = C.c_void_p
 _SIGS = {
     "v3g_load": (C.c_int, [C.POINTER(_P), _P, C.c_uint64, C.c_int, C.c_int, C.c_uint32]),
@@ -61,7 +68,13 @@ _SIGS = {
     "v3g_attention": (C.c_int, [_P, C.c_uint32, _P]),
     "v3g_status_copy": (C.c_int, [_P, _P, _P]),
     "v3g_sample_topk": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint32, C.c_float, _P, _P, _P]),
-    "v3g_generate_sampled": (C.c_int, [_P, _P, C.c_uint32, _P, C.c_uint64, C.c_uint32, C.c_float, _P, _P]),
+    "v3g_generate_sampled": (C.c_int, [_P, _P, C.c_uint32, _P, C.c_uint64, C.c_uint32, C.c_float, _P,
+                                       C.POINTER(GovRules), _P, _P]),
+    "v3g_gov_init": (None, [C.POINTER(GovRules)]),
+    "v3g_gov_add_rule": (C.c_int, [C.POINTER(GovRules), C.c_char_p, C.c_size_t]),
+    "v3g_gov_arm_system": (None, [C.POINTER(GovRules), C.c_char_p, C.c_size_t]),
+    "v3g_govern_logits": (C.c_int, [_P, C.POINTER(GovRules), _P, _P, C.c_uint32, C.c_uint64, C.c_uint32, _P]),
+    "v3g_gov_commit": (C.c_int, [_P, C.POINTER(GovRules), _P, _P, C.c_uint32, _P]),
     "v3g_gemm_work_size": (C.c_size_t, [_P, C.c_uint32, C.c_uint32]),
     "v3g_gemm": (C.c_int, [_P, C.c_uint32, _P, C.c_uint32, _P, _P, C.c_size_t, _P]),
     "v3g_argmax_noalloc": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.c_uint64, _P, _P]),

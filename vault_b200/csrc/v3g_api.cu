@@ -910,8 +910,13 @@ extern "C" int v3g_generate(v3g_state *s, const int32_t *dev_first, uint32_t n_s
 }
 
 extern "C" int v3g_generate_sampled(v3g_state *s, const int32_t *dev_first, uint32_t n_steps, int32_t *dev_out,
-                                    uint64_t ld, uint32_t k, float temp, uint64_t *dev_rng, void *stream) {
+                                    uint64_t ld, uint32_t k, float temp, uint64_t *dev_rng, const v3g_gov_rules_t *gov,
+                                    v3g_gov_stream_t *dev_gov, void *stream) {
     if (!s || !dev_first || !dev_out || !dev_rng) return fail(V3G_E_ARG, "null argument");
+    const bool governed = gov && gov->n_rules > 0;
+    if (governed && !dev_gov) return fail(V3G_E_ARG, "v3g_generate_sampled: governor rules without stream states");
+    // the loop's guard (runtime/vault3_host.c:588): 16 candidates for greedy or small k, else k up to 64
+    const uint32_t guard = (temp <= 0.0f || k < 16u) ? 16u : (k > 64u ? 64u : k);
     if (n_steps > ld && s->B > 1) return fail(V3G_E_ARG, "v3g_generate_sampled: ld below n_steps");
     cudaStream_t st = (cudaStream_t)stream;
     const ModelDev &md = s->m->host;
@@ -921,8 +926,11 @@ extern "C" int v3g_generate_sampled(v3g_state *s, const int32_t *dev_first, uint
     // each step's greedy token in tok_in is replaced by the draw from that step's logits before the next step reads it
     for (uint32_t i = 0; i < n_steps; ++i) {
         if ((rc = run_step(s, true, st)) != V3G_OK) return rc;
+        if (governed)
+            CUDA_TRY(launch_govern(s->m, *gov, dev_gov, s->host.logits, (uint32_t)s->B, (uint64_t)md.vocab, guard, st));
         CUDA_TRY(launch_sample_topk(s->host.logits, (uint32_t)s->B, (uint32_t)md.vocab, (uint64_t)md.vocab, k, temp,
                                     dev_rng, s->host.tok_in, dev_out + i, (int64_t)ld, st));
+        if (governed) CUDA_TRY(launch_gov_commit(s->m, *gov, dev_gov, s->host.tok_in, (uint32_t)s->B, st));
     }
     return V3G_OK;
 }

@@ -7,6 +7,7 @@
 #include <string>
 #include <vector>
 
+#include "../../include/vault_b200.h"
 #include "v3g.cuh"
 #include "v3g_gemm.cuh"
 #include "v3g_gemv.cuh"
@@ -108,6 +109,11 @@ cudaError_t launch_argmax_only(const v3g_model *m, v3g_state *s, cudaStream_t st
 // out[b * out_ld]
 cudaError_t launch_sample_topk(const float *logits, uint32_t rows, uint32_t vocab, uint64_t ld, uint32_t k, float temp,
                                uint64_t *rng, int32_t *tokens, int32_t *out, int64_t out_ld, cudaStream_t st);
+// governor masking / commit over rows of logits and stream states (v3g_sample.cu); no launch while n_rules == 0
+cudaError_t launch_govern(const v3g_model *m, const v3g_gov_rules_t &rules, const v3g_gov_stream_t *streams,
+                          float *logits, uint32_t rows, uint64_t ld, uint32_t top_k_guard, cudaStream_t st);
+cudaError_t launch_gov_commit(const v3g_model *m, const v3g_gov_rules_t &rules, v3g_gov_stream_t *streams,
+                              const int32_t *tokens, uint32_t rows, cudaStream_t st);
 cudaError_t launch_step_begin(const v3g_model *m, v3g_state *s, bool boundary, cudaStream_t st);
 cudaError_t launch_scorer(const v3g_model *m, v3g_state *s, cudaStream_t st);
 // batched decode step (B > 8) with every projection on the tensor-core GEMM (v3g_prefill.cu)

@@ -44,6 +44,51 @@ def sample_topk(logits: torch.Tensor, k: int, temp: float, rng: torch.Tensor) ->
     return out
 
 
+class Governor:
+    """CAAI output governor (runtime/vault3.h:191-216): forbidden patterns built on the host, one stream state per
+    sequence on the device.  govern() masks, in place, the candidate tokens that would complete a pattern
+    (v3_govern_logits); commit() appends the chosen tokens to the streams (v3_gov_commit); pass the governor to
+    VAULTv3ForCausalLM.generate to run both inside the on-device loop."""
+
+    def __init__(self, batch: int = 1, device: Optional[Union[int, torch.device]] = None):
+        self.rules = _lib.GovRules()
+        _lib.lib().v3g_gov_init(C.byref(self.rules))
+        dev = torch.device("cuda", device) if isinstance(device, int) else (device or torch.device("cuda"))
+        self.streams = torch.zeros(batch, _lib.GOV_STREAM_BYTES, dtype=torch.uint8, device=dev)
+
+    @property
+    def active(self) -> bool:
+        return self.rules.n_rules > 0
+
+    def add_rule(self, pattern: bytes) -> None:
+        _lib.check(_lib.lib().v3g_gov_add_rule(C.byref(self.rules), pattern, len(pattern)), "v3g_gov_add_rule")
+
+    def arm_system(self, text: bytes) -> None:
+        """Reset, then derive the rules from a system prompt (v3_gov_arm_system)."""
+        _lib.lib().v3g_gov_arm_system(C.byref(self.rules), text, len(text))
+
+    def reset_stream(self) -> None:
+        self.streams.zero_()
+
+    def govern(self, model: "VAULTv3ForCausalLM", logits: torch.Tensor, top_k_guard: int = 64) -> torch.Tensor:
+        if logits.dim() != 2 or logits.dtype != torch.float32 or logits.stride(1) != 1 or \
+                logits.shape[0] != self.streams.shape[0] or logits.shape[1] < model.cfg.vocab_size:
+            raise ValueError("logits must be [batch, >= vocab] fp32 with contiguous rows")
+        with torch.cuda.device(logits.device):
+            _lib.check(_lib.lib().v3g_govern_logits(model._h, C.byref(self.rules), C.c_void_p(self.streams.data_ptr()),
+                                                    C.c_void_p(logits.data_ptr()), logits.shape[0], logits.stride(0),
+                                                    int(top_k_guard), _stream()), "v3g_govern_logits")
+        return logits
+
+    def commit(self, model: "VAULTv3ForCausalLM", tokens: torch.Tensor) -> None:
+        tok = tokens.to(device=self.streams.device, dtype=torch.int32).reshape(-1).contiguous()
+        if tok.numel() != self.streams.shape[0]:
+            raise ValueError("one token per sequence")
+        with torch.cuda.device(tok.device):
+            _lib.check(_lib.lib().v3g_gov_commit(model._h, C.byref(self.rules), C.c_void_p(self.streams.data_ptr()),
+                                                 C.c_void_p(tok.data_ptr()), tok.numel(), _stream()), "v3g_gov_commit")
+
+
 class VAULTv3State:
     """Fixed-size streaming state held in a device arena (the reference's VAULTv3State / v3_state)."""
 
@@ -272,20 +317,28 @@ class VAULTv3ForCausalLM:
 
     @torch.no_grad()
     def generate(self, st: VAULTv3State, first_tokens: torch.Tensor, n_steps: int, top_k: int = 1,
-                 temperature: float = 0.0, rng: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 temperature: float = 0.0, rng: Optional[torch.Tensor] = None,
+                 governor: Optional[Governor] = None) -> torch.Tensor:
         """Decode n_steps tokens on the device starting from first_tokens [B]; returns int32 [B, n_steps].
         Greedy by default; with temperature > 0 and top_k > 1 every token is drawn by sample_topk's rule (the
-        reference's v3_sample_topk) from the per-sequence xorshift states rng ([B] int64, advanced in place)."""
+        reference's v3_sample_topk) from the per-sequence xorshift states rng ([B] int64, advanced in place).
+        With an armed governor each step's logits are masked and each token committed, as in
+        runtime/vault3_host.c:586-606."""
         first = self._ids(first_tokens.reshape(-1))
         out = torch.empty(st.batch, n_steps, dtype=torch.int32, device=self.device)
-        if temperature > 0.0 and top_k > 1:
-            if rng is None or rng.shape != (st.batch,) or rng.dtype != torch.int64 or rng.device != out.device \
-                    or not rng.is_contiguous():
+        governed = governor is not None and governor.active
+        if governed and governor.streams.shape[0] != st.batch:
+            raise ValueError("the governor holds a stream per sequence: batch sizes differ")
+        if (temperature > 0.0 and top_k > 1) or governed:
+            if rng is None:
+                rng = torch.zeros(st.batch, dtype=torch.int64, device=out.device)
+            if rng.shape != (st.batch,) or rng.dtype != torch.int64 or rng.device != out.device or \
+                    not rng.is_contiguous():
                 raise ValueError("sampled generation needs rng: a contiguous [B] int64 tensor on the model's device")
-            _lib.check(_lib.lib().v3g_generate_sampled(st._h, C.c_void_p(first.data_ptr()), n_steps,
-                                                       C.c_void_p(out.data_ptr()), n_steps, int(top_k),
-                                                       float(temperature), C.c_void_p(rng.data_ptr()), _stream()),
-                       "v3g_generate_sampled")
+            _lib.check(_lib.lib().v3g_generate_sampled(
+                st._h, C.c_void_p(first.data_ptr()), n_steps, C.c_void_p(out.data_ptr()), n_steps, int(top_k),
+                float(temperature), C.c_void_p(rng.data_ptr()), C.byref(governor.rules) if governed else None,
+                C.c_void_p(governor.streams.data_ptr()) if governed else None, _stream()), "v3g_generate_sampled")
         else:
             _lib.check(_lib.lib().v3g_generate(st._h, C.c_void_p(first.data_ptr()), n_steps,
                                                C.c_void_p(out.data_ptr()), n_steps, _stream()), "v3g_generate")
