@@ -236,6 +236,19 @@ V3G_API int v3g_govern_logits(const v3g_model *m, const v3g_gov_rules_t *rules, 
 V3G_API int v3g_gov_commit(const v3g_model *m, const v3g_gov_rules_t *rules, v3g_gov_stream_t *dev_streams,
                            const int32_t *dev_tokens, uint32_t rows, void *stream);
 
+/* Host tokenizer of a VLT3 file's VTOK blob (runtime/vault3.h:162-188 v3_tok_init / v3_encode_ex / v3_encode;
+ * v3_token_bytes :189): byte-level BPE behind the Qwen2 pre-tokenizer, UAX #15 NFC on spans holding bytes >= 0xCC,
+ * special tokens (<|im_start|> ...) matched as whole strings when allow_special != 0.  Same ids as the reference for
+ * the same text; V3G_E_SIZE with the first max_out ids in out when more would follow.  v3g_tokenizer_create
+ * validates buf as v3g_validate does (without the CRC pass) and keeps its own copy of the blob.  Host only. */
+typedef struct v3g_tokenizer v3g_tokenizer;
+V3G_API int v3g_tokenizer_create(v3g_tokenizer **out, const uint8_t *buf, uint64_t size);
+V3G_API void v3g_tokenizer_free(v3g_tokenizer *t);
+V3G_API int v3g_encode_ex(v3g_tokenizer *t, const uint8_t *text, size_t len, uint32_t *out, size_t max_out,
+                          size_t *n_out, int allow_special);
+V3G_API int v3g_encode(v3g_tokenizer *t, const uint8_t *text, size_t len, uint32_t *out, size_t max_out, size_t *n_out);
+V3G_API int v3g_token_bytes(const v3g_tokenizer *t, uint32_t id, const uint8_t **bytes, uint32_t *len);
+
 #define V3G_NOALLOC_MAX_ROWS 4096
 V3G_API int v3g_argmax_noalloc(const float *dev_logits, uint32_t rows, uint32_t vocab, uint64_t ld, int32_t *dev_tokens,
                                void *stream);

@@ -1,0 +1,167 @@
+"""The host tokenizer (v3g_encode_ex) against the reference's own v3_encode_ex (runtime/vault3.c:2708-2809) from
+oracle/_ref/libvault3.so, on one VLT3 file whose VTOK blob carries a trained merge table: same ids, same return
+code and count, for fuzzed text (ASCII, contractions, ChatML control tokens, precomposed and combining Latin,
+Hangul syllables and jamo, CJK, emoji, Devanagari, invalid UTF-8), NFC spans above 1 KB, pieces above 32 KB,
+decompositions past the 2048-code-point cap, and truncated outputs.  No GPU."""
+import ctypes as C
+import dataclasses
+import json
+import os
+import random
+
+import numpy as np
+import pytest
+
+from tests.ref_governor import RefModel, ref_lib
+
+FRAGMENTS = [
+    "Hello world", " I'm here", " they'll GO", " DON'T", "'s", " 12345", " 3.14159", "!!", " ...", "\n\n", "\r\n",
+    "\t\tindent", "   spaces   ", "<|im_start|>system\nBe brief.<|im_end|>\n", "<|im_start|>user\n", "<|im_end|>",
+    "<|im_sta", "<|endoftext|>", "café", "café", "Å", "Å", "ạ́", "ạ́",
+    "ḍ̇", "q̣̇", "한국어", "각", "하", "中文字",
+    "\U0001F600 ok", "क़", "क़", "Åñ", "αβγ", "Жук",
+    "الع", "  nbsp", " ", "x​y", "ﬁ", "Ω", "̈́", "ཱི",
+    "'ll", "'VE", "a'b", "  \n  x", "line\n", "ab;x}y&q", '",', ". ", ", ",
+]
+BAD_BYTES = [b"\xff", b"\x80", b"\xc0\x80", b"\xed\xa0\x80", b"\xf4\x90\x80\x80", b"\xe2\x82", b"\xcc", b"\xcc\x81"]
+
+
+def _corpus_texts(rng: random.Random, n: int) -> list:
+    out = []
+    for _ in range(n):
+        parts = []
+        for _ in range(rng.randint(1, 12)):
+            if rng.random() < 0.1:
+                parts.append(rng.choice(BAD_BYTES))
+            else:
+                parts.append(rng.choice(FRAGMENTS).encode("utf-8"))
+        out.append(b"".join(parts))
+    return out
+
+
+def _train_merges(tok_dir: str, vocab_size: int, n_merges: int) -> None:
+    """Greedy BPE over the fragments (GPT-2 byte-unicode form), new tokens on free ids; one repeated merge line."""
+    from vault_b200.synth import byte_to_unicode
+    path = os.path.join(tok_dir, "tokenizer.json")
+    tj = json.load(open(path, encoding="utf-8"))
+    vocab = tj["model"]["vocab"]
+    b2u = byte_to_unicode()
+    taken = set(vocab.values()) | {t["id"] for t in tj["added_tokens"]}
+    free = (i for i in range(vocab_size) if i not in taken)
+    words = [[b2u[b] for b in f.encode("utf-8")] for f in FRAGMENTS * 3 + ["the", " the", " there", "ing"] * 5]
+    merges = []
+    for _ in range(n_merges):
+        counts = {}
+        for w in words:
+            for a, b in zip(w, w[1:]):
+                counts[(a, b)] = counts.get((a, b), 0) + 1
+        if not counts:
+            break
+        (a, b), _ = max(counts.items(), key=lambda kv: (kv[1], kv[0]))
+        if a + b not in vocab:
+            vocab[a + b] = next(free)
+        merges.append(f"{a} {b}")
+        for w in words:
+            i = 0
+            while i + 1 < len(w):
+                if w[i] == a and w[i + 1] == b:
+                    w[i:i + 2] = [a + b]
+                i += 1
+    merges.insert(len(merges) // 2, merges[len(merges) // 3])   # a repeated pair: its first rank wins
+    tj["model"]["merges"] = merges
+    json.dump(tj, open(path, "w", encoding="utf-8"), ensure_ascii=False)
+
+
+@pytest.fixture(scope="module")
+def tokenizers(tmp_path_factory):
+    from tests.golden.cases import CASES, case_config
+    from vault_b200 import _lib, synth
+    L = ref_lib()
+    L.ref_sizeof_tokenizer.restype = C.c_size_t
+    L.v3_tok_arena_size.argtypes = [C.c_void_p]
+    L.v3_tok_arena_size.restype = C.c_size_t
+    L.v3_tok_init.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]
+    L.v3_tok_init.restype = C.c_int
+    L.v3_encode_ex.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t, C.c_void_p, C.c_size_t,
+                               C.POINTER(C.c_size_t), C.c_int]
+    L.v3_encode_ex.restype = C.c_int
+    td = str(tmp_path_factory.mktemp("tok"))
+    spec = CASES["mini_gqa_q8_0"]
+    cfg = dataclasses.replace(case_config(spec), vocab_size=1024)
+    tok_dir = os.path.join(td, "tok")
+    synth.make_tokenizer_dir(tok_dir, cfg.vocab_size, synth.SMALL_EXTRA_TOKENS)
+    _train_merges(tok_dir, cfg.vocab_size, 400)
+    path = os.path.join(td, "m.vlt3")
+    synth.write_synthetic_vlt3(path, cfg, spec["fmt"], spec["seed"], tokenizer_dir=tok_dir, model_name="tok",
+                               std=spec["std"])
+    ref_model = RefModel(L, path)
+    arena_n = L.v3_tok_arena_size(ref_model.handle)
+    arena_raw = np.zeros(arena_n + 64, np.uint8)
+    arena = arena_raw[(-arena_raw.ctypes.data) % 64:]
+    ref_tok = C.create_string_buffer(L.ref_sizeof_tokenizer())
+    assert L.v3_tok_init(ref_tok, ref_model.handle, arena.ctypes.data, arena_n) == 0
+    E = _lib.lib()
+    raw = open(path, "rb").read()
+    ours = C.c_void_p()
+    assert E.v3g_tokenizer_create(C.byref(ours), raw, len(raw)) == 0
+    yield L, ref_tok, E, ours, (ref_model, arena_raw)
+    E.v3g_tokenizer_free(ours)
+
+
+def _both(tokenizers, text: bytes, max_out: int, special: int):
+    L, ref_tok, E, ours, _ = tokenizers
+    a = np.zeros(max(1, max_out), np.uint32)
+    b = np.zeros(max(1, max_out), np.uint32)
+    na, nb = C.c_size_t(), C.c_size_t()
+    ra = L.v3_encode_ex(ref_tok, text, len(text), a.ctypes.data, max_out, C.byref(na), special)
+    rb = E.v3g_encode_ex(ours, text, len(text), b.ctypes.data, max_out, C.byref(nb), special)
+    return (ra, na.value, a[:na.value].tolist()), (rb, nb.value, b[:nb.value].tolist())
+
+
+def test_encode_fuzz_matches_reference(tokenizers):
+    rng = random.Random(5)
+    merged = 0
+    for text in _corpus_texts(rng, 1500):
+        for special in (1, 0):
+            ref, ours = _both(tokenizers, text, 4 * len(text) + 8, special)
+            assert ref == ours, (text, special)
+            assert ref[0] == 0
+            merged += len(text) - ref[1]
+    assert merged > 0   # the merge table took part
+
+
+def test_encode_long_spans_match_reference(tokenizers):
+    rng = random.Random(9)
+    cases = [
+        b"a" * 40000,                                         # one letter piece above 32 KB: windowed BPE
+        (b"the " * 9000),                                     # many pieces
+        b" " * 33000 + b"x",                                  # one whitespace piece above 32 KB
+        ("é" * 700).encode(),                           # an NFC span above 1 KB
+        ("a" + "̣́" * 1500).encode(),               # combining run: decomposition cap, span split
+        ("ḉ" * 900 + " tail").encode(),                  # every code point decomposes into 3
+        ("café " * 400 + "\nnext line " * 50).encode(),  # clean boundaries inside the span
+        ("한" * 600 + "abc" + "क़" * 200).encode(),
+        b"".join(rng.choice(FRAGMENTS).encode() for _ in range(3000)),
+    ]
+    for text in cases:
+        ref, ours = _both(tokenizers, text, 2 * len(text) + 8, 1)
+        assert ref == ours, (len(text), ref[0], ref[1], ours[1])
+
+
+def test_encode_truncation_matches_reference(tokenizers):
+    rng = random.Random(13)
+    for text in _corpus_texts(rng, 200) + [b"a" * 40000, ("é" * 50).encode(), b"<|im_end|>" * 5]:
+        full = _both(tokenizers, text, 4 * len(text) + 8, 1)[0][1]
+        for max_out in sorted({0, 1, full // 2, max(0, full - 1)}):
+            ref, ours = _both(tokenizers, text, max_out, 1)
+            assert ref == ours, (text[:40], max_out)
+
+
+def test_token_bytes_match_reference(tokenizers):
+    L, ref_tok, E, ours, (ref_model, _) = tokenizers
+    ref_bytes = ref_model.token_bytes(1024)
+    for i in range(1030):
+        p, n = C.POINTER(C.c_uint8)(), C.c_uint32()
+        rc = E.v3g_token_bytes(ours, i, C.byref(p), C.byref(n))
+        got = bytes(p[:n.value]) if rc == 0 and n.value else b""
+        assert got == (ref_bytes[i] if i < 1024 else b""), i

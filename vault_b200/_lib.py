@@ -71,6 +71,11 @@ _SIGS = {
     "v3g_generate_sampled": (C.c_int, [_P, _P, C.c_uint32, _P, C.c_uint64, C.c_uint32, C.c_float, _P,
                                        C.POINTER(GovRules), _P, _P]),
     "v3g_gov_init": (None, [C.POINTER(GovRules)]),
+    "v3g_tokenizer_create": (C.c_int, [C.POINTER(_P), _P, C.c_uint64]),
+    "v3g_tokenizer_free": (None, [_P]),
+    "v3g_encode_ex": (C.c_int, [_P, C.c_char_p, C.c_size_t, _P, C.c_size_t, C.POINTER(C.c_size_t), C.c_int]),
+    "v3g_encode": (C.c_int, [_P, C.c_char_p, C.c_size_t, _P, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "v3g_token_bytes": (C.c_int, [_P, C.c_uint32, C.POINTER(C.POINTER(C.c_uint8)), C.POINTER(C.c_uint32)]),
     "v3g_gov_add_rule": (C.c_int, [C.POINTER(GovRules), C.c_char_p, C.c_size_t]),
     "v3g_gov_arm_system": (None, [C.POINTER(GovRules), C.c_char_p, C.c_size_t]),
     "v3g_govern_logits": (C.c_int, [_P, C.POINTER(GovRules), _P, _P, C.c_uint32, C.c_uint64, C.c_uint32, _P]),

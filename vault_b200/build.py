@@ -14,7 +14,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libvault_b200.so")
-SOURCES = ["v3g_weights.cu", "v3g_step.cu", "v3g_attn.cu", "v3g_api.cu", "v3g_noalloc.cu", "v3g_gemm.cu", "v3g_prefill.cu", "v3g_sample.cu"]
+SOURCES = ["v3g_weights.cu", "v3g_step.cu", "v3g_attn.cu", "v3g_api.cu", "v3g_noalloc.cu", "v3g_gemm.cu", "v3g_prefill.cu", "v3g_sample.cu",
+           "v3g_tokenizer.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",

@@ -269,6 +269,16 @@ extern "C" int v3g_validate(const uint8_t *buf, uint64_t size, int verify_crc) {
     return rc;
 }
 
+// the VTOK tokenizer blob of a validated VLT3 buffer (a pointer into buf)
+int vlt3_token_blob(const uint8_t *buf, uint64_t size, const uint8_t **tok, uint64_t *tok_size) {
+    Parsed *P = new Parsed();
+    const int rc = parse_vlt3(buf, size, 0, *P);
+    *tok = P->tok;
+    *tok_size = P->tok_size;
+    delete P;
+    return rc;
+}
+
 extern "C" int v3g_load(v3g_model **out, const uint8_t *buf, uint64_t size, int verify_crc, int device,
                         uint32_t max_sink) {
     if (!out) return fail(V3G_E_ARG, "null output pointer");

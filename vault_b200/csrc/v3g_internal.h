@@ -80,6 +80,8 @@ struct v3g_state {
 
 // records msg as this thread's v3g_last_error() and returns code
 int v3g_fail(int code, const std::string &msg);
+// validate a VLT3 buffer (no CRC pass) and return its VTOK tokenizer blob (v3g_api.cu)
+int vlt3_token_blob(const uint8_t *buf, uint64_t size, const uint8_t **tok, uint64_t *tok_size);
 
 namespace v3g {
 int repack_matrix(MatW &w, const uint8_t *dev_src0, const uint8_t *dev_src1, int fmt, int src_rows, int cols,
