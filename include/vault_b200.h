@@ -240,7 +240,8 @@ V3G_API int v3g_gov_commit(const v3g_model *m, const v3g_gov_rules_t *rules, v3g
  * v3_token_bytes :189): byte-level BPE behind the Qwen2 pre-tokenizer, UAX #15 NFC on spans holding bytes >= 0xCC,
  * special tokens (<|im_start|> ...) matched as whole strings when allow_special != 0.  Same ids as the reference for
  * the same text; V3G_E_SIZE with the first max_out ids in out when more would follow.  v3g_tokenizer_create
- * validates buf as v3g_validate does (without the CRC pass) and keeps its own copy of the blob.  Host only. */
+ * validates buf as v3g_validate does (without the CRC pass; buf 64-byte aligned as for v3g_load) and keeps its own
+ * copy of the blob.  Host only. */
 typedef struct v3g_tokenizer v3g_tokenizer;
 V3G_API int v3g_tokenizer_create(v3g_tokenizer **out, const uint8_t *buf, uint64_t size);
 V3G_API void v3g_tokenizer_free(v3g_tokenizer *t);

@@ -101,10 +101,9 @@ def tokenizers(tmp_path_factory):
     ref_tok = C.create_string_buffer(L.ref_sizeof_tokenizer())
     assert L.v3_tok_init(ref_tok, ref_model.handle, arena.ctypes.data, arena_n) == 0
     E = _lib.lib()
-    raw = open(path, "rb").read()
-    ours = C.c_void_p()
-    assert E.v3g_tokenizer_create(C.byref(ours), raw, len(raw)) == 0
-    yield L, ref_tok, E, ours, (ref_model, arena_raw)
+    ours = C.c_void_p()   # from the same page-aligned copy: VLT3 buffers are read at their alignment
+    assert E.v3g_tokenizer_create(C.byref(ours), C.c_void_p(ref_model._buf.ctypes.data), len(ref_model._buf)) == 0
+    yield L, ref_tok, E, ours, (ref_model, arena_raw, path)
     E.v3g_tokenizer_free(ours)
 
 
@@ -158,10 +157,23 @@ def test_encode_truncation_matches_reference(tokenizers):
 
 
 def test_token_bytes_match_reference(tokenizers):
-    L, ref_tok, E, ours, (ref_model, _) = tokenizers
+    L, ref_tok, E, ours, (ref_model, _, _) = tokenizers
     ref_bytes = ref_model.token_bytes(1024)
     for i in range(1030):
         p, n = C.POINTER(C.c_uint8)(), C.c_uint32()
         rc = E.v3g_token_bytes(ours, i, C.byref(p), C.byref(n))
         got = bytes(p[:n.value]) if rc == 0 and n.value else b""
         assert got == (ref_bytes[i] if i < 1024 else b""), i
+
+
+def test_python_tokenizer_matches_reference(tokenizers):
+    from vault_b200 import Tokenizer
+    path = tokenizers[4][2]
+    tok = Tokenizer(path)
+    for text in _corpus_texts(random.Random(21), 50) + [b"<|im_start|>user\nhi<|im_end|>"]:
+        for special in (True, False):
+            ref = _both(tokenizers, text, 4 * len(text) + 8, int(special))[0]
+            assert tok.encode(text, allow_special=special) == ref[2]
+            assert tok.decode(ref[2]) == b"".join(tok.token_bytes(i) for i in ref[2])
+    ids = tok.encode("café <|im_end|>")
+    assert tok.encode("café <|im_end|>", allow_special=False) != ids

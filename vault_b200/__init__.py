@@ -6,6 +6,7 @@ CUDA library `libvault_b200.so` behind the C ABI in include/vault_b200.h.
 """
 
 from .config import VAULTv3Config
+from .tokenizer import Tokenizer
 from .vlt3 import VLT3Error, read_vlt3, vlt3_config, write_vlt3
 
 
@@ -18,4 +19,4 @@ def __getattr__(name):
 
 
 __all__ = ["Governor", "VAULTv3Config", "VAULTv3ForCausalLM", "VAULTv3State", "VLT3Error", "read_vlt3", "sample_topk",
-           "vlt3_config", "write_vlt3"]
+           "Tokenizer", "vlt3_config", "write_vlt3"]
