@@ -132,3 +132,17 @@ def test_round_trip_dequant(good_q8):
     vf = vlt3.read_vlt3(good_q8)
     w = vf.tensor("layers.0.self_attn.q_proj.weight")
     assert w.dtype == np.float32 and w.shape == (64, 64)
+
+
+def test_config_from_qwen_config_and_dict_round_trip():
+    """VAULTv3Config.from_qwen_config maps a Qwen2 config.json the way src/vault_v3_model.py:87-103 does (the
+    Qwen2.5-1.5B numbers give the default v3 backbone), overrides apply, and to_dict / from_dict round-trip."""
+    from vault_b200 import VAULTv3Config
+    qc = {"vocab_size": 151936, "hidden_size": 1536, "num_hidden_layers": 28, "num_attention_heads": 12,
+          "num_key_value_heads": 2, "intermediate_size": 8960, "rms_norm_eps": 1e-6, "rope_theta": 1000000.0,
+          "tie_word_embeddings": True}
+    cfg = VAULTv3Config.from_qwen_config(qc, seg_budget=1024, seg_layers=(8, 16, 24))
+    assert cfg == VAULTv3Config(seg_budget=1024, seg_layers=(8, 16, 24))
+    assert cfg.head_dim == 128 and cfg.group_size == 6 and cfg.n_cells == 0 and cfg.has_seg_scorer
+    assert VAULTv3Config.from_dict(cfg.to_dict()) == cfg
+    assert VAULTv3Config.from_qwen_config(dict(qc, tie_word_embeddings=False)).tie_embeddings is False

@@ -32,6 +32,11 @@ class VAULTv3Config:
     seg_layers: Tuple[int, ...] = ()
 
     @property
+    def n_cells(self) -> int:
+        """Kenyon memory cells: none in v3 (src/vault_v3_model.py:63-65)."""
+        return 0
+
+    @property
     def group_size(self) -> int:
         return self.n_heads // self.n_kv_heads
 
@@ -55,3 +60,16 @@ class VAULTv3Config:
         if "seg_layers" in d:
             d["seg_layers"] = tuple(int(x) for x in d["seg_layers"])
         return cls(**d)
+
+    @classmethod
+    def from_qwen_config(cls, qc: dict, **overrides) -> "VAULTv3Config":
+        """Backbone sizes from a Hugging Face Qwen2 config.json dict, then keyword overrides
+        (src/vault_v3_model.py:87-103)."""
+        cfg = cls(vocab_size=qc["vocab_size"], d_model=qc["hidden_size"], n_layers=qc["num_hidden_layers"],
+                  n_heads=qc["num_attention_heads"], n_kv_heads=qc["num_key_value_heads"],
+                  head_dim=qc["hidden_size"] // qc["num_attention_heads"], d_ff=qc["intermediate_size"],
+                  rms_eps=qc["rms_norm_eps"], rope_theta=qc["rope_theta"],
+                  tie_embeddings=qc.get("tie_word_embeddings", True))
+        for k, v in overrides.items():
+            setattr(cfg, k, v)
+        return cfg
