@@ -11,7 +11,6 @@
 
 #include <algorithm>
 #include <functional>
-#include <queue>
 #include <unordered_map>
 #include <vector>
 
@@ -147,6 +146,7 @@ struct v3g_tokenizer {
     const uint8_t *table = nullptr, *pool = nullptr, *special = nullptr, *ranges = nullptr, *bytemap = nullptr;
     std::unordered_map<uint64_t, std::pair<uint32_t, uint32_t>> merges;   // (left << 32 | right) -> (rank, result)
     std::vector<uint32_t> sym, win;
+    std::vector<uint64_t> heap;   // merge candidates, a min-heap kept across pieces
     std::vector<int32_t> prv, nxt;
     std::vector<uint32_t> cps;
     std::vector<uint8_t> nfc;
@@ -240,13 +240,19 @@ struct v3g_tokenizer {
         }
         nxt[n - 1] = -1;
         // candidates keyed (rank << 32 | left position): the smallest key merges first
-        std::priority_queue<uint64_t, std::vector<uint64_t>, std::greater<uint64_t>> q;
+        const std::greater<uint64_t> later;
+        auto push = [&](uint64_t key) {
+            heap.push_back(key);
+            std::push_heap(heap.begin(), heap.end(), later);
+        };
+        heap.clear();
         uint32_t r, res;
         for (size_t i = 0; i + 1 < n; ++i)
-            if (merge_of(sym[i], sym[i + 1], r, res)) q.push(((uint64_t)r << 32) | (uint32_t)i);
-        while (!q.empty()) {
-            const uint64_t top = q.top();
-            q.pop();
+            if (merge_of(sym[i], sym[i + 1], r, res)) push(((uint64_t)r << 32) | (uint32_t)i);
+        while (!heap.empty()) {
+            std::pop_heap(heap.begin(), heap.end(), later);
+            const uint64_t top = heap.back();
+            heap.pop_back();
             const int32_t i = (int32_t)(uint32_t)top;
             if (sym[i] == DEAD) continue;
             const int32_t j = nxt[i];
@@ -257,8 +263,8 @@ struct v3g_tokenizer {
             const int32_t after = nxt[j];
             nxt[i] = after;
             if (after >= 0) prv[after] = i;
-            if (prv[i] >= 0 && merge_of(sym[prv[i]], sym[i], r, res)) q.push(((uint64_t)r << 32) | (uint32_t)prv[i]);
-            if (after >= 0 && merge_of(sym[i], sym[after], r, res)) q.push(((uint64_t)r << 32) | (uint32_t)i);
+            if (prv[i] >= 0 && merge_of(sym[prv[i]], sym[i], r, res)) push(((uint64_t)r << 32) | (uint32_t)prv[i]);
+            if (after >= 0 && merge_of(sym[i], sym[after], r, res)) push(((uint64_t)r << 32) | (uint32_t)i);
         }
         size_t k = 0;
         for (int32_t c = 0; c >= 0; c = nxt[c]) {
@@ -465,6 +471,7 @@ extern "C" int v3g_tokenizer_create(v3g_tokenizer **out, const uint8_t *buf, uin
     t->win.resize(MAX_PIECE);
     t->prv.resize(MAX_PIECE);
     t->nxt.resize(MAX_PIECE);
+    t->heap.reserve(3 * MAX_PIECE);
     t->cps.reserve(NFC_MAX_CPS);
     t->nfc.reserve(4 * NFC_MAX_CPS);
     *out = t;
