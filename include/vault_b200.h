@@ -117,6 +117,11 @@ V3G_API int v3g_load(v3g_model **out, const uint8_t *buf, uint64_t size, int ver
  * uploads anything.  The Python reader (vault_b200.vlt3.read_vlt3, the counterpart of tools/vlt3.py:453-545
  * read_vlt3) validates through it, so both loaders accept and reject the same files. */
 V3G_API int v3g_validate(const uint8_t *buf, uint64_t size, int verify_crc);
+/* The same two calls on a file path: the file is mapped read-only (mmap, page-aligned) for the length of the call
+ * and read in place, with no host copy (runtime/vault3_host.c maps its model file the same way).  A missing or
+ * unmappable file gives V3G_E_ARG, an empty one V3G_E_SIZE; otherwise the codes of v3g_load / v3g_validate. */
+V3G_API int v3g_load_file(v3g_model **out, const char *path, int verify_crc, int device, uint32_t max_sink);
+V3G_API int v3g_validate_file(const char *path, int verify_crc);
 V3G_API int v3g_model_get_info(const v3g_model *m, v3g_model_info *out);
 V3G_API void v3g_free(v3g_model *m);
 

@@ -105,6 +105,23 @@ def test_engine_loader_rejects_misaligned_buffer(good_q8):
     assert _lib.lib().v3g_load(C.byref(h), C.c_void_p(a.ctypes.data), len(good_q8), 1, 0, 0) == -11
 
 
+def test_file_validation_matches_buffer_validation(good_q8, tmp_path):
+    """v3g_validate_file (the file mapped read-only, read in place) gives the codes of v3g_validate on an aligned
+    copy, for the good file and every corrupt case; a missing file is an argument error, an empty one a size error."""
+    L = _lib.lib()
+    cases = [("good", bytearray(good_q8), True, None)] + list(corrupt_cases(good_q8))
+    for name, data, verify, _ in cases:
+        p = tmp_path / f"{name}.vlt3"
+        p.write_bytes(bytes(data))
+        buf = vlt3.aligned_buffer(bytes(data))
+        want = L.v3g_validate(C.c_void_p(buf.ctypes.data), buf.size, int(verify))
+        assert L.v3g_validate_file(str(p).encode(), int(verify)) == want, name
+    assert L.v3g_validate_file(str(tmp_path / "good.vlt3").encode(), 1) == 0
+    assert L.v3g_validate_file(str(tmp_path / "missing.vlt3").encode(), 0) == -21
+    (tmp_path / "empty.vlt3").write_bytes(b"")
+    assert L.v3g_validate_file(str(tmp_path / "empty.vlt3").encode(), 0) == -1
+
+
 @pytest.mark.skipif(not os.path.exists(REF_HOST), reason="reference C runtime not built (oracle/Makefile)")
 def test_reference_runtime_agrees_on_rejections(good_q8, tmp_path):
     for name, data, verify, _ in corrupt_cases(good_q8):

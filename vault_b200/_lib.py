@@ -47,6 +47,8 @@ _P = C.c_void_p
 _SIGS = {
     "v3g_load": (C.c_int, [C.POINTER(_P), _P, C.c_uint64, C.c_int, C.c_int, C.c_uint32]),
     "v3g_validate": (C.c_int, [_P, C.c_uint64, C.c_int]),
+    "v3g_load_file": (C.c_int, [C.POINTER(_P), C.c_char_p, C.c_int, C.c_int, C.c_uint32]),
+    "v3g_validate_file": (C.c_int, [C.c_char_p, C.c_int]),
     "v3g_model_get_info": (C.c_int, [_P, C.POINTER(ModelInfo)]),
     "v3g_free": (None, [_P]),
     "v3g_state_arena_size": (C.c_size_t, [_P, C.c_uint32, C.c_uint32]),

@@ -2,7 +2,11 @@
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <fcntl.h>
 #include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <string>
@@ -267,6 +271,45 @@ extern "C" int v3g_validate(const uint8_t *buf, uint64_t size, int verify_crc) {
     const int rc = parse_vlt3(buf, size, verify_crc, *P);
     delete P;
     return rc;
+}
+
+// A VLT3 file mapped read-only for the length of one call (page-aligned, so the format's alignment rule holds
+// without a host copy); the loader reads the mapping directly.
+struct MappedFile {
+    const uint8_t *data = nullptr;
+    uint64_t size = 0;
+    int open_file(const char *path) {
+        if (!path) return fail(V3G_E_ARG, "null path");
+        const int fd = open(path, O_RDONLY | O_CLOEXEC);
+        if (fd < 0) return fail(V3G_E_ARG, std::string("cannot open ") + path);
+        struct stat sb;
+        if (fstat(fd, &sb) != 0 || sb.st_size <= 0) {
+            close(fd);
+            return fail(V3G_E_SIZE, std::string("empty or unreadable file ") + path);
+        }
+        void *p = mmap(nullptr, (size_t)sb.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+        close(fd);
+        if (p == MAP_FAILED) return fail(V3G_E_ARG, std::string("cannot map ") + path);
+        madvise(p, (size_t)sb.st_size, MADV_SEQUENTIAL);
+        data = static_cast<const uint8_t *>(p);
+        size = (uint64_t)sb.st_size;
+        return V3G_OK;
+    }
+    ~MappedFile() {
+        if (data) munmap(const_cast<uint8_t *>(data), (size_t)size);
+    }
+};
+
+extern "C" int v3g_validate_file(const char *path, int verify_crc) {
+    MappedFile f;
+    const int rc = f.open_file(path);
+    return rc != V3G_OK ? rc : v3g_validate(f.data, f.size, verify_crc);
+}
+
+extern "C" int v3g_load_file(v3g_model **out, const char *path, int verify_crc, int device, uint32_t max_sink) {
+    MappedFile f;
+    const int rc = f.open_file(path);
+    return rc != V3G_OK ? rc : v3g_load(out, f.data, f.size, verify_crc, device, max_sink);
 }
 
 // the VTOK tokenizer blob of a validated VLT3 buffer (a pointer into buf)
