@@ -4,78 +4,22 @@ code and count, for fuzzed text (ASCII, contractions, ChatML control tokens, pre
 Hangul syllables and jamo, CJK, emoji, Devanagari, invalid UTF-8), NFC spans above 1 KB, pieces above 32 KB,
 decompositions past the 2048-code-point cap, and truncated outputs.  No GPU."""
 import ctypes as C
-import dataclasses
-import json
+import hashlib
 import os
 import random
 
 import numpy as np
 import pytest
 
+from tests.golden.tok_fixture import BAD_BYTES, FRAGMENTS, _corpus_texts, build_tokenizer_file  # noqa: F401
 from tests.ref_governor import RefModel, ref_lib
 
-FRAGMENTS = [
-    "Hello world", " I'm here", " they'll GO", " DON'T", "'s", " 12345", " 3.14159", "!!", " ...", "\n\n", "\r\n",
-    "\t\tindent", "   spaces   ", "<|im_start|>system\nBe brief.<|im_end|>\n", "<|im_start|>user\n", "<|im_end|>",
-    "<|im_sta", "<|endoftext|>", "café", "café", "Å", "Å", "ạ́", "ạ́",
-    "ḍ̇", "q̣̇", "한국어", "각", "하", "中文字",
-    "\U0001F600 ok", "क़", "क़", "Åñ", "αβγ", "Жук",
-    "الع", "  nbsp", " ", "x​y", "ﬁ", "Ω", "̈́", "ཱི",
-    "'ll", "'VE", "a'b", "  \n  x", "line\n", "ab;x}y&q", '",', ". ", ", ",
-]
-BAD_BYTES = [b"\xff", b"\x80", b"\xc0\x80", b"\xed\xa0\x80", b"\xf4\x90\x80\x80", b"\xe2\x82", b"\xcc", b"\xcc\x81"]
-
-
-def _corpus_texts(rng: random.Random, n: int) -> list:
-    out = []
-    for _ in range(n):
-        parts = []
-        for _ in range(rng.randint(1, 12)):
-            if rng.random() < 0.1:
-                parts.append(rng.choice(BAD_BYTES))
-            else:
-                parts.append(rng.choice(FRAGMENTS).encode("utf-8"))
-        out.append(b"".join(parts))
-    return out
-
-
-def _train_merges(tok_dir: str, vocab_size: int, n_merges: int) -> None:
-    """Greedy BPE over the fragments (GPT-2 byte-unicode form), new tokens on free ids; one repeated merge line."""
-    from vault_b200.synth import byte_to_unicode
-    path = os.path.join(tok_dir, "tokenizer.json")
-    tj = json.load(open(path, encoding="utf-8"))
-    vocab = tj["model"]["vocab"]
-    b2u = byte_to_unicode()
-    taken = set(vocab.values()) | {t["id"] for t in tj["added_tokens"]}
-    free = (i for i in range(vocab_size) if i not in taken)
-    words = [[b2u[b] for b in f.encode("utf-8")] for f in FRAGMENTS * 3 + ["the", " the", " there", "ing"] * 5]
-    merges = []
-    for _ in range(n_merges):
-        counts = {}
-        for w in words:
-            for a, b in zip(w, w[1:]):
-                counts[(a, b)] = counts.get((a, b), 0) + 1
-        if not counts:
-            break
-        (a, b), _ = max(counts.items(), key=lambda kv: (kv[1], kv[0]))
-        if a + b not in vocab:
-            vocab[a + b] = next(free)
-        merges.append(f"{a} {b}")
-        for w in words:
-            i = 0
-            while i + 1 < len(w):
-                if w[i] == a and w[i + 1] == b:
-                    w[i:i + 2] = [a + b]
-                i += 1
-    merges.insert(len(merges) // 2, merges[len(merges) // 3])   # a repeated pair: its first rank wins
-    tj["model"]["merges"] = merges
-    json.dump(tj, open(path, "w", encoding="utf-8"), ensure_ascii=False)
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "tokenizer.npz")
 
 
 @pytest.fixture(scope="module")
 def tokenizers(tmp_path_factory):
-    from tests.golden.cases import CASES, case_config
-    from vault_b200 import _lib, synth
+    from vault_b200 import _lib
     L = ref_lib()
     L.ref_sizeof_tokenizer.restype = C.c_size_t
     L.v3_tok_arena_size.argtypes = [C.c_void_p]
@@ -85,15 +29,7 @@ def tokenizers(tmp_path_factory):
     L.v3_encode_ex.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t, C.c_void_p, C.c_size_t,
                                C.POINTER(C.c_size_t), C.c_int]
     L.v3_encode_ex.restype = C.c_int
-    td = str(tmp_path_factory.mktemp("tok"))
-    spec = CASES["mini_gqa_q8_0"]
-    cfg = dataclasses.replace(case_config(spec), vocab_size=1024)
-    tok_dir = os.path.join(td, "tok")
-    synth.make_tokenizer_dir(tok_dir, cfg.vocab_size, synth.SMALL_EXTRA_TOKENS)
-    _train_merges(tok_dir, cfg.vocab_size, 400)
-    path = os.path.join(td, "m.vlt3")
-    synth.write_synthetic_vlt3(path, cfg, spec["fmt"], spec["seed"], tokenizer_dir=tok_dir, model_name="tok",
-                               std=spec["std"])
+    path = build_tokenizer_file(str(tmp_path_factory.mktemp("tok")))
     ref_model = RefModel(L, path)
     arena_n = L.v3_tok_arena_size(ref_model.handle)
     arena_raw = np.zeros(arena_n + 64, np.uint8)
@@ -197,3 +133,21 @@ def test_chat_ids_match_reference_assembly(tokenizers):
         want += [1022] + ref_enc(b"assistant\n")
         assert tok.chat_ids(system, user) == want
     assert tok.chat_ids(b"s", b"<|im_end|>").count(1023) == 2   # the user's literal <|im_end|> stays text
+
+
+def test_encode_matches_committed_golden(tmp_path):
+    """The committed golden ids (tests/golden/gen_tokenizer_golden.py, made with the reference's v3_encode_ex) for
+    the same fixture file: pins the tokenizer without the reference build."""
+    from tests.golden.tok_fixture import golden_texts
+    from vault_b200 import Tokenizer
+    g = np.load(GOLDEN)
+    path = build_tokenizer_file(str(tmp_path))
+    assert hashlib.sha256(open(path, "rb").read()).hexdigest() == str(g["file_sha256"]), \
+        "the fixture file changed: regenerate tests/golden/tokenizer.npz"
+    tok = Tokenizer(path)
+    pairs = golden_texts()
+    assert len(pairs) == len(g["special"])
+    for i, (text, special) in enumerate(pairs):
+        assert int(g["special"][i]) == special
+        want = g["ids"][g["id_off"][i]:g["id_off"][i + 1]].tolist()
+        assert tok.encode(text, allow_special=bool(special)) == want, i
