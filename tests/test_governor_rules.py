@@ -40,15 +40,20 @@ def _code_points():
     return [cp for cp in cps if not 0xD800 <= cp <= 0xDFFF]
 
 
+def fold_patterns() -> list:
+    """Patterns around every code point of the folded ranges, malformed UTF-8, short and long patterns."""
+    pats = [b"qwert" + chr(cp).encode("utf-8") + b"z" for cp in _code_points()]
+    return pats + [b"qwert\xc0\x80z", b"qwert\xc1\xbfz", b"qwert\xed\xa0\x80z", b"qwert\xf4\x90\x80\x80z",
+                   b"qwert\xf5\x80\x80\x80z", b"qwert\xe2\x82z", b"qwert\x80z", b"qw\xe2\x82\xacert\xffz",
+                   b"\xe0\xa4", b"ab", b"a_b-c d", b"ABCDEFGHIJKLMNOPQRSTUVWXYZ0123456789abcdefghij",
+                   "сисколл_ехес".encode()]
+
+
 def test_add_rule_canonical_form_matches_reference():
     """Every code point of the folded ranges (ASCII, Latin, Greek, Cyrillic, format characters, fullwidth forms)
     and malformed UTF-8 inside a pattern: same return code and the same canonical bytes."""
     L, E = _pair()
-    pats = [b"qwert" + chr(cp).encode("utf-8") + b"z" for cp in _code_points()]
-    pats += [b"qwert\xc0\x80z", b"qwert\xc1\xbfz", b"qwert\xed\xa0\x80z", b"qwert\xf4\x90\x80\x80z",
-             b"qwert\xf5\x80\x80\x80z", b"qwert\xe2\x82z", b"qwert\x80z", b"qw\xe2\x82\xacert\xffz", b"\xe0\xa4",
-             b"ab", b"a_b-c d", b"ABCDEFGHIJKLMNOPQRSTUVWXYZ0123456789abcdefghij", "сисколл_ехес".encode()]
-    for p in pats:
+    for p in fold_patterns():
         ref, ours = RefGov(), _lib.GovRules()
         rc_ref = L.v3_gov_add_rule(C.byref(ref), p, len(p))
         rc_ours = E.v3g_gov_add_rule(C.byref(ours), p, len(p))
@@ -63,3 +68,25 @@ def test_add_rule_limit_and_duplicates_match_reference():
         p = b"rule_%02d" % (i % 10)
         assert L.v3_gov_add_rule(C.byref(ref), p, len(p)) == E.v3g_gov_add_rule(C.byref(ours), p, len(p))
     assert ours.n_rules == 8 and rules_of(ref) == rules_of(ours)
+
+
+def test_rules_match_committed_golden():
+    """The committed reference outputs (tests/golden/gen_governor_golden.py): pins the rule builder without the
+    reference build."""
+    import gzip
+    import json
+    import os
+    E = _lib.lib()
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "governor_rules.json.gz")
+    g = json.load(gzip.open(path, "rt"))
+    assert [bytes.fromhex(e["text"]) for e in g["arm_system"]] == SYSTEM_TEXTS
+    for e in g["arm_system"]:
+        text, ours = bytes.fromhex(e["text"]), _lib.GovRules()
+        E.v3g_gov_arm_system(C.byref(ours), text, len(text))
+        assert [r.hex() for r in rules_of(ours)] == e["rules"], text
+    pats = fold_patterns()
+    assert len(pats) == len(g["add_rule"])
+    for p, e in zip(pats, g["add_rule"]):
+        ours = _lib.GovRules()
+        assert E.v3g_gov_add_rule(C.byref(ours), p, len(p)) == e["rc"], p
+        assert [r.hex() for r in rules_of(ours)] == e["rules"], p
